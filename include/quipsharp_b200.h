@@ -1,0 +1,165 @@
+/*
+ * quipsharp_b200 -- C ABI of the B200 (sm_100a) kernels behind QuIP#'s
+ * quantized-linear forward path.
+ *
+ * Every entry point takes plain device pointers owned by the caller, sizes,
+ * and a CUDA stream (cudaStream_t passed as qs_stream_t; NULL = legacy default
+ * stream).  Work is enqueued on that stream; nothing synchronises unless the
+ * comment says so.  No entry point allocates device memory: buffers that a
+ * path needs beyond its inputs and outputs ("workspace") are passed in by the
+ * caller, who asks for their size with the matching *_bytes() function.
+ *
+ * Return value: QS_OK (0) or one of the qs_status codes; qs_last_error()
+ * gives a message for the last failing call on the calling thread.  The
+ * status codes map onto the exceptions the reference raises for the same
+ * conditions (see each entry point).
+ *
+ * Reference citations are `path:line` inside the reference project
+ * (numbersletter/quipsharp).
+ */
+#ifndef QUIPSHARP_B200_H
+#define QUIPSHARP_B200_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+typedef struct CUstream_st *qs_stream_t; /* == cudaStream_t */
+
+typedef enum qs_status {
+  QS_OK = 0,
+  QS_ERR_INVALID_ARG = 1, /* bad pointer / size / enum value                     */
+  QS_ERR_NOT_POW2 = 2,    /* fwht on a non-power-of-two size (ValueError, hadamard.py:28-29) */
+  QS_ERR_ODD_DIM = 3,     /* RFFT on an odd size (AssertionError, rfft.py:42, rfft.py:55)   */
+  QS_ERR_INDEX = 4,       /* 1-bit codebook index outside [-256, 256) (IndexError, e8_1bit.py:87) */
+  QS_ERR_UNSUPPORTED = 5, /* size beyond what the kernels handle                  */
+  QS_ERR_ALIGNMENT = 6,   /* pointer not aligned as the kernel requires           */
+  QS_ERR_CUDA = 7,        /* a CUDA runtime call or launch failed                 */
+  QS_ERR_WORKSPACE = 8    /* workspace missing or smaller than *_bytes() asked for */
+} qs_status;
+
+/* Codebook kinds (one per RVQ stage). */
+typedef enum qs_codebook_kind {
+  QS_CB_E8P = 0,    /* 16-bit E8P code per 8 weights, quipsharp/codebooks/e8p.py */
+  QS_CB_E8_1BIT = 1 /* 8-bit index per 8 weights, quipsharp/codebooks/e8_1bit.py */
+} qs_codebook_kind;
+
+/* Element types. */
+typedef enum qs_dtype {
+  QS_F32 = 0, QS_F16 = 1, QS_BF16 = 2, QS_I16 = 3, QS_I32 = 4, QS_I64 = 5
+} qs_dtype;
+
+/* Incoherence transform of a layer (quipsharp/incoherence.py:115-131). */
+typedef enum qs_transform { QS_RHT = 0, QS_RFFT = 1 } qs_transform;
+
+const char *qs_version(void);
+const char *qs_last_error(void);
+
+/* Host-only.  Writes the 256x8 float32 table of `kind` (row-major) to host
+ * memory: E8P = build_abs_table() (quipsharp/codebooks/e8p.py:84-89),
+ * E8_1BIT = build_table() (quipsharp/codebooks/e8_1bit.py:67-71). */
+int qs_codebook_table(int kind, float *out_host);
+
+/* E8PCodebook.dequantize (quipsharp/codebooks/e8p.py:197-199) and
+ * E8OneBitCodebook.dequantize (quipsharp/codebooks/e8_1bit.py:86-87):
+ * out[i*8 + j] = decode(codes[i])[j], bit-exact float32.  codes has element
+ * type code_dtype (QS_I16, QS_I32 or QS_I64); E8P uses the low 16 bits of
+ * each code (e8p.py:174-180).  For E8_1BIT an index outside [-256, 256)
+ * returns QS_ERR_INDEX (this check synchronises the stream). */
+int qs_decode(int kind, const void *codes, int code_dtype, int64_t count, float *out,
+              qs_stream_t stream);
+
+/* rvq_dequantize (quipsharp/rvq.py:83-88) through RVQCodebookAdapter.dequantize
+ * (quipsharp/quantize.py:43-45): out = sum_s fl32(decode_s(codes[s][i]) *
+ * stage_scales[s]), accumulated in stage order.  stage_scales is host memory
+ * (float32 per stage). */
+int qs_rvq_decode(int stages, const int *kinds, const void *const *codes, int code_dtype,
+                  const float *stage_scales, int64_t count, float *out, qs_stream_t stream);
+
+/* dequantize_linear (quipsharp/quantize.py:107-113) on the QuantizedLinear
+ * int16 buffer (quipsharp/checkpoint.py:99-103, :132-139):
+ * codes is int16 (stages, m, n/8), out is float32 (m, n).  stage_scales is
+ * host memory or NULL for a plain (non-RVQ) codebook; layer_scale points to
+ * the float32 `scale` buffer on the device. */
+int qs_dequantize_linear(const int16_t *codes, int stages, const int *kinds,
+                         const float *stage_scales, const float *layer_scale, int64_t m,
+                         int64_t n, float *out, qs_stream_t stream);
+
+/* fwht (quipsharp/hadamard.py:17-40) over rows of length n (a power of two,
+ * n <= 32768), fused with the sign vectors of transform_input / transform_output
+ * (quipsharp/incoherence.py:86-93): y = post * H_n(pre * x) / sqrt(n).
+ * pre/post are float32 device vectors of length n or NULL.  x and y have
+ * element type dtype (QS_F32, QS_F16, QS_BF16), row strides ld_x / ld_y
+ * elements; computation is float32. */
+int qs_fwht(const void *x, int64_t ld_x, void *y, int64_t ld_y, int dtype, int64_t rows,
+            int64_t n, const float *pre, const float *post, qs_stream_t stream);
+
+/* to_transformed_space (inverse = 0, quipsharp/rfft.py:37-47) and
+ * from_transformed_space (inverse = 1, quipsharp/rfft.py:50-60) over rows of
+ * length n (even, n/2 <= 16384, prime factors of n/2 at most 43):
+ * forward: y = view_as_real(FFT_ortho(view_as_complex(x) * phase));
+ * inverse: y = view_as_real(IFFT_ortho(view_as_complex(x)) * conj(phase)).
+ * phase is complex64 (interleaved float2) of length n/2 on the device. */
+int qs_rfft(int inverse, const void *x, int64_t ld_x, void *y, int64_t ld_y, int dtype,
+            int64_t rows, int64_t n, const void *phase, qs_stream_t stream);
+
+/* Size in bytes of the kernel-ready weight stream for a layer of `stages`
+ * codebooks (kinds) with m outputs and n inputs, as written by qs_pack_codes. */
+int64_t qs_packed_bytes(int stages, const int *kinds, int64_t m, int64_t n);
+
+/* Re-lays the QuantizedLinear int16 codes (stages, m, n/8) into the tiled
+ * bit-sliced stream the fused kernels read.  The mapping is a bijection of
+ * the code bits (no information is dropped); 1-bit stages are narrowed to
+ * uint8 (an index >= 256 returns QS_ERR_INDEX, as table indexing does in
+ * e8_1bit.py:87; this check synchronises the stream). */
+int qs_pack_codes(const int16_t *codes, int stages, const int *kinds, int64_t m, int64_t n,
+                  void *packed, int64_t packed_bytes, qs_stream_t stream);
+
+/* Workspace bytes qs_linear_fwd needs for `batch` rows of a layer (m, n). */
+int64_t qs_linear_workspace_bytes(int64_t batch, int64_t m, int64_t n);
+
+/* QuantizedLinear.forward (quipsharp/checkpoint.py:141-146) ->
+ * linear_forward (quipsharp/quantize.py:116-124):
+ *   y = cast(transform_out(transform_in(float(x)) @ What^T) + bias)
+ * x: (batch, n) of x_dtype (QS_F32/F16/BF16), y: (batch, m) of the same type.
+ * packed: from qs_pack_codes.  stage_scales: host float32 per stage or NULL
+ * for a plain codebook.  layer_scale: device pointer to the float32 `scale`.
+ * transform QS_RHT uses su (m) / sv (n) float32; QS_RFFT uses phase_u (m/2) /
+ * phase_v (n/2) complex64.  bias: float32 (m) or NULL.  workspace: device
+ * buffer of qs_linear_workspace_bytes(batch, m, n) bytes (256-byte aligned). */
+int qs_linear_fwd(const void *x, int x_dtype, int64_t batch, int64_t n, int64_t m,
+                  const void *packed, int stages, const int *kinds, const float *stage_scales,
+                  const float *layer_scale, int transform, const float *su, const float *sv,
+                  const void *phase_u, const void *phase_v, const float *bias, void *y,
+                  void *workspace, int64_t workspace_bytes, qs_stream_t stream);
+
+/* The three steps of qs_linear_fwd, for callers that put a collective between
+ * the matmul and the output transform (column-sharded tensor parallelism:
+ * each rank runs qs_linear_input + qs_linear_matmul on its rows of the
+ * weight, the y1 shards are all-gathered, then every rank runs
+ * qs_linear_output on the full y1).
+ *  - qs_linear_input: x -> x2 (fp16 tiles + per-row scale in workspace) and
+ *    zeroes y1 (batch, m_local) float32.
+ *  - qs_linear_matmul: y1 += x2 @ What_local^T * scales (rows m_local).
+ *  - qs_linear_output: y = cast(transform_out(y1) + bias), y1 float32 (batch, m)
+ *    with row stride ld_y1. */
+int64_t qs_linear_input_bytes(int64_t batch, int64_t n);
+int qs_linear_input(const void *x, int x_dtype, int64_t batch, int64_t n, int transform,
+                    const float *sv, const void *phase_v, void *x2_workspace,
+                    int64_t x2_workspace_bytes, float *y1, int64_t m_local, qs_stream_t stream);
+int qs_linear_matmul(const void *x2_workspace, int64_t batch, int64_t n, int64_t m_local,
+                     const void *packed, int stages, const int *kinds,
+                     const float *stage_scales, const float *layer_scale, float *y1,
+                     qs_stream_t stream);
+int qs_linear_output(const float *y1, int64_t ld_y1, int64_t batch, int64_t m, int transform,
+                     const float *su, const void *phase_u, const float *bias, void *y,
+                     int y_dtype, qs_stream_t stream);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* QUIPSHARP_B200_H */

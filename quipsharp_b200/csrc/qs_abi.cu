@@ -1,0 +1,249 @@
+// extern "C" entry points of libquipsharp_b200: argument validation, error
+// reporting and dispatch to the launchers of the other translation units.
+#include <cstdarg>
+#include <cstdio>
+#include <cstring>
+
+#include "qs_common.cuh"
+#include "qs_launch.h"
+
+#define QS_API extern "C" __attribute__((visibility("default")))
+
+namespace qs {
+
+static thread_local char g_last_error[512] = "";
+
+void set_error(const char *fmt, ...) {
+  va_list ap;
+  va_start(ap, fmt);
+  vsnprintf(g_last_error, sizeof(g_last_error), fmt, ap);
+  va_end(ap);
+}
+
+int fail(int status, const char *fmt, ...) {
+  va_list ap;
+  va_start(ap, fmt);
+  vsnprintf(g_last_error, sizeof(g_last_error), fmt, ap);
+  va_end(ap);
+  return status;
+}
+
+int check_launch(const char *what) {
+  cudaError_t e = cudaGetLastError();
+  if (e != cudaSuccess) return fail(QS_ERR_CUDA, "%s launch failed: %s", what, cudaGetErrorString(e));
+  return QS_OK;
+}
+
+static bool valid_kind(int k) { return k == QS_CB_E8P || k == QS_CB_E8_1BIT; }
+static bool valid_io_dtype(int d) { return d == QS_F32 || d == QS_F16 || d == QS_BF16; }
+static bool valid_code_dtype(int d) { return d == QS_I16 || d == QS_I32 || d == QS_I64; }
+
+static int check_kinds(int stages, const int *kinds) {
+  if (stages < 1 || stages > 2 || kinds == nullptr)
+    return fail(QS_ERR_INVALID_ARG, "stages must be 1 or 2 (got %d) with a kinds array", stages);
+  for (int i = 0; i < stages; ++i)
+    if (!valid_kind(kinds[i])) return fail(QS_ERR_INVALID_ARG, "bad codebook kind %d", kinds[i]);
+  return QS_OK;
+}
+
+static bool aligned(const void *p, size_t a) { return (reinterpret_cast<uintptr_t>(p) % a) == 0; }
+
+}  // namespace qs
+
+using namespace qs;
+
+QS_API const char *qs_version(void) { return "quipsharp_b200 0.1 (sm_100a)"; }
+
+QS_API const char *qs_last_error(void) { return g_last_error; }
+
+QS_API int qs_codebook_table(int kind, float *out_host) {
+  if (!out_host) return fail(QS_ERR_INVALID_ARG, "null output");
+  if (kind == QS_CB_E8P) memcpy(out_host, kE8pAbsF32Host, sizeof(kE8pAbsF32Host));
+  else if (kind == QS_CB_E8_1BIT) memcpy(out_host, kE81BitF32Host, sizeof(kE81BitF32Host));
+  else return fail(QS_ERR_INVALID_ARG, "bad codebook kind %d", kind);
+  return QS_OK;
+}
+
+QS_API int qs_decode(int kind, const void *codes, int code_dtype, int64_t count, float *out,
+                     qs_stream_t stream) {
+  if (!valid_kind(kind)) return fail(QS_ERR_INVALID_ARG, "bad codebook kind %d", kind);
+  if (!valid_code_dtype(code_dtype)) return fail(QS_ERR_INVALID_ARG, "bad code dtype %d", code_dtype);
+  if (count < 0) return fail(QS_ERR_INVALID_ARG, "negative count");
+  if (count == 0) return QS_OK;
+  if (!codes || !out) return fail(QS_ERR_INVALID_ARG, "null pointer");
+  return launch_decode(kind, codes, code_dtype, count, out, (cudaStream_t)stream);
+}
+
+QS_API int qs_rvq_decode(int stages, const int *kinds, const void *const *codes, int code_dtype,
+                         const float *stage_scales, int64_t count, float *out,
+                         qs_stream_t stream) {
+  int st = check_kinds(stages, kinds);
+  if (st) return st;
+  if (!valid_code_dtype(code_dtype)) return fail(QS_ERR_INVALID_ARG, "bad code dtype %d", code_dtype);
+  if (count < 0) return fail(QS_ERR_INVALID_ARG, "negative count");
+  if (count == 0) return QS_OK;
+  if (!codes || !out || !stage_scales) return fail(QS_ERR_INVALID_ARG, "null pointer");
+  for (int i = 0; i < stages; ++i)
+    if (!codes[i]) return fail(QS_ERR_INVALID_ARG, "null codes for stage %d", i);
+  return launch_rvq_decode(stages, kinds, codes, code_dtype, stage_scales, count, out,
+                           (cudaStream_t)stream);
+}
+
+QS_API int qs_dequantize_linear(const int16_t *codes, int stages, const int *kinds,
+                                const float *stage_scales, const float *layer_scale, int64_t m,
+                                int64_t n, float *out, qs_stream_t stream) {
+  int st = check_kinds(stages, kinds);
+  if (st) return st;
+  if (m < 0 || n < 0 || n % 8) return fail(QS_ERR_INVALID_ARG, "bad shape (%lld, %lld)", (long long)m, (long long)n);
+  if (m == 0 || n == 0) return QS_OK;
+  if (!codes || !out || !layer_scale) return fail(QS_ERR_INVALID_ARG, "null pointer");
+  return launch_dequantize_linear(codes, stages, kinds, stage_scales, layer_scale, m, n, out,
+                                  (cudaStream_t)stream);
+}
+
+QS_API int qs_fwht(const void *x, int64_t ld_x, void *y, int64_t ld_y, int dtype, int64_t rows,
+                   int64_t n, const float *pre, const float *post, qs_stream_t stream) {
+  if (!valid_io_dtype(dtype)) return fail(QS_ERR_INVALID_ARG, "bad dtype %d", dtype);
+  if (n <= 0 || (n & (n - 1)))
+    return fail(QS_ERR_NOT_POW2, "fwht requires a power-of-two size along dim, got %lld", (long long)n);
+  if (n > 32768) return fail(QS_ERR_UNSUPPORTED, "fwht size %lld exceeds 32768", (long long)n);
+  if (rows < 0 || ld_x < n || ld_y < n) return fail(QS_ERR_INVALID_ARG, "bad rows/strides");
+  if (rows == 0) return QS_OK;
+  if (!x || !y) return fail(QS_ERR_INVALID_ARG, "null pointer");
+  return launch_fwht(x, ld_x, y, ld_y, dtype, rows, n, pre, post, (cudaStream_t)stream);
+}
+
+QS_API int qs_rfft(int inverse, const void *x, int64_t ld_x, void *y, int64_t ld_y, int dtype,
+                   int64_t rows, int64_t n, const void *phase, qs_stream_t stream) {
+  if (!valid_io_dtype(dtype)) return fail(QS_ERR_INVALID_ARG, "bad dtype %d", dtype);
+  if (n <= 0 || (n % 2)) return fail(QS_ERR_ODD_DIM, "RFFT requires an even size, got %lld", (long long)n);
+  int st = check_fft_size(n / 2);
+  if (st) return st;
+  if (rows < 0 || ld_x < n || ld_y < n) return fail(QS_ERR_INVALID_ARG, "bad rows/strides");
+  if (rows == 0) return QS_OK;
+  if (!x || !y || !phase) return fail(QS_ERR_INVALID_ARG, "null pointer");
+  if (!aligned(phase, 8)) return fail(QS_ERR_ALIGNMENT, "phase must be 8-byte aligned");
+  return launch_rfft(inverse, x, ld_x, y, ld_y, dtype, rows, n, phase, (cudaStream_t)stream);
+}
+
+QS_API int64_t qs_packed_bytes(int stages, const int *kinds, int64_t m, int64_t n) {
+  if (check_kinds(stages, kinds) || m <= 0 || n <= 0 || n % 8) return -1;
+  int64_t total = 0;
+  for (int s = 0; s < stages; ++s) total += round_up(stage_bytes(kinds[s], m, n), 256);
+  return total;
+}
+
+QS_API int qs_pack_codes(const int16_t *codes, int stages, const int *kinds, int64_t m, int64_t n,
+                         void *packed, int64_t packed_bytes, qs_stream_t stream) {
+  int st = check_kinds(stages, kinds);
+  if (st) return st;
+  if (m <= 0 || n <= 0 || n % 8) return fail(QS_ERR_INVALID_ARG, "bad shape (%lld, %lld)", (long long)m, (long long)n);
+  if (!codes || !packed) return fail(QS_ERR_INVALID_ARG, "null pointer");
+  if (packed_bytes < qs_packed_bytes(stages, kinds, m, n))
+    return fail(QS_ERR_WORKSPACE, "packed buffer too small");
+  if (!aligned(packed, 256)) return fail(QS_ERR_ALIGNMENT, "packed buffer must be 256-byte aligned");
+  return launch_pack(codes, stages, kinds, m, n, packed, (cudaStream_t)stream);
+}
+
+static int64_t ws_align(int64_t b) { return round_up(b, 256); }
+
+QS_API int64_t qs_linear_input_bytes(int64_t batch, int64_t n) {
+  if (batch < 0 || n <= 0) return -1;
+  return linear_input_bytes(batch, n);
+}
+
+QS_API int64_t qs_linear_workspace_bytes(int64_t batch, int64_t m, int64_t n) {
+  if (batch < 0 || m <= 0 || n <= 0) return -1;
+  return ws_align(linear_input_bytes(batch, n)) + ws_align(batch * m * (int64_t)sizeof(float));
+}
+
+static int check_transform_args(int transform, int64_t m, int64_t n, const float *su,
+                                const float *sv, const void *phase_u, const void *phase_v) {
+  if (transform == QS_RHT) {
+    if (n <= 0 || (n & (n - 1)) || m <= 0 || (m & (m - 1)))
+      return fail(QS_ERR_NOT_POW2, "RHT needs power-of-two dims, got (%lld, %lld)", (long long)m, (long long)n);
+    if (n > 32768 || m > 32768) return fail(QS_ERR_UNSUPPORTED, "RHT dims above 32768");
+    if (!su || !sv) return fail(QS_ERR_INVALID_ARG, "RHT needs su and sv");
+  } else if (transform == QS_RFFT) {
+    if (n % 2 || m % 2) return fail(QS_ERR_ODD_DIM, "RFFT needs even dims, got (%lld, %lld)", (long long)m, (long long)n);
+    int st = check_fft_size(n / 2);
+    if (st) return st;
+    st = check_fft_size(m / 2);
+    if (st) return st;
+    if (!phase_u || !phase_v) return fail(QS_ERR_INVALID_ARG, "RFFT needs phase_u and phase_v");
+  } else {
+    return fail(QS_ERR_INVALID_ARG, "bad transform %d", transform);
+  }
+  return QS_OK;
+}
+
+QS_API int qs_linear_input(const void *x, int x_dtype, int64_t batch, int64_t n, int transform,
+                           const float *sv, const void *phase_v, void *x2_workspace,
+                           int64_t x2_workspace_bytes, float *y1, int64_t m_local,
+                           qs_stream_t stream) {
+  if (!valid_io_dtype(x_dtype)) return fail(QS_ERR_INVALID_ARG, "bad dtype %d", x_dtype);
+  int st = check_transform_args(transform, transform == QS_RHT ? 1 : 2, n, sv, sv, phase_v, phase_v);
+  if (st) return st;
+  if (batch < 0 || m_local < 0) return fail(QS_ERR_INVALID_ARG, "bad batch / m_local");
+  if (batch == 0) return QS_OK;
+  if (!x || !x2_workspace) return fail(QS_ERR_INVALID_ARG, "null pointer");
+  if (x2_workspace_bytes < linear_input_bytes(batch, n)) return fail(QS_ERR_WORKSPACE, "x2 workspace too small");
+  if (!aligned(x2_workspace, 256)) return fail(QS_ERR_ALIGNMENT, "workspace must be 256-byte aligned");
+  return launch_linear_input(x, x_dtype, batch, n, transform, sv, phase_v, x2_workspace, y1,
+                             m_local, (cudaStream_t)stream);
+}
+
+QS_API int qs_linear_matmul(const void *x2_workspace, int64_t batch, int64_t n, int64_t m_local,
+                            const void *packed, int stages, const int *kinds,
+                            const float *stage_scales, const float *layer_scale, float *y1,
+                            qs_stream_t stream) {
+  int st = check_kinds(stages, kinds);
+  if (st) return st;
+  if (batch < 0 || n <= 0 || n % 8 || m_local <= 0) return fail(QS_ERR_INVALID_ARG, "bad shape");
+  if (batch == 0) return QS_OK;
+  if (!x2_workspace || !packed || !layer_scale || !y1) return fail(QS_ERR_INVALID_ARG, "null pointer");
+  if (stages == 2 && !stage_scales) return fail(QS_ERR_INVALID_ARG, "RVQ needs stage scales");
+  if (!aligned(packed, 256)) return fail(QS_ERR_ALIGNMENT, "packed buffer must be 256-byte aligned");
+  return launch_matmul(x2_workspace, batch, n, m_local, packed, stages, kinds, stage_scales,
+                       layer_scale, y1, (cudaStream_t)stream);
+}
+
+QS_API int qs_linear_output(const float *y1, int64_t ld_y1, int64_t batch, int64_t m, int transform,
+                            const float *su, const void *phase_u, const float *bias, void *y,
+                            int y_dtype, qs_stream_t stream) {
+  if (!valid_io_dtype(y_dtype)) return fail(QS_ERR_INVALID_ARG, "bad dtype %d", y_dtype);
+  int st = check_transform_args(transform, m, transform == QS_RHT ? 1 : 2, su, su, phase_u, phase_u);
+  if (st) return st;
+  if (batch < 0 || ld_y1 < m) return fail(QS_ERR_INVALID_ARG, "bad batch / ld_y1");
+  if (batch == 0) return QS_OK;
+  if (!y1 || !y) return fail(QS_ERR_INVALID_ARG, "null pointer");
+  return launch_linear_output(y1, ld_y1, batch, m, transform, su, phase_u, bias, y, y_dtype,
+                              (cudaStream_t)stream);
+}
+
+QS_API int qs_linear_fwd(const void *x, int x_dtype, int64_t batch, int64_t n, int64_t m,
+                         const void *packed, int stages, const int *kinds,
+                         const float *stage_scales, const float *layer_scale, int transform,
+                         const float *su, const float *sv, const void *phase_u,
+                         const void *phase_v, const float *bias, void *y, void *workspace,
+                         int64_t workspace_bytes, qs_stream_t stream) {
+  int st = check_kinds(stages, kinds);
+  if (st) return st;
+  if (!valid_io_dtype(x_dtype)) return fail(QS_ERR_INVALID_ARG, "bad dtype %d", x_dtype);
+  if (batch < 0 || n <= 0 || m <= 0 || n % 8) return fail(QS_ERR_INVALID_ARG, "bad shape");
+  st = check_transform_args(transform, m, n, su, sv, phase_u, phase_v);
+  if (st) return st;
+  if (batch == 0) return QS_OK;
+  if (!x || !y || !packed || !layer_scale || !workspace) return fail(QS_ERR_INVALID_ARG, "null pointer");
+  if (stages == 2 && !stage_scales) return fail(QS_ERR_INVALID_ARG, "RVQ needs stage scales");
+  if (workspace_bytes < qs_linear_workspace_bytes(batch, m, n)) return fail(QS_ERR_WORKSPACE, "workspace too small");
+  if (!aligned(workspace, 256) || !aligned(packed, 256)) return fail(QS_ERR_ALIGNMENT, "workspace/packed must be 256-byte aligned");
+  const int64_t x2b = ws_align(linear_input_bytes(batch, n));
+  float *y1 = reinterpret_cast<float *>(static_cast<char *>(workspace) + x2b);
+  cudaStream_t s = (cudaStream_t)stream;
+  st = launch_linear_input(x, x_dtype, batch, n, transform, sv, phase_v, workspace, y1, m, s);
+  if (st) return st;
+  st = launch_matmul(workspace, batch, n, m, packed, stages, kinds, stage_scales, layer_scale, y1, s);
+  if (st) return st;
+  return launch_linear_output(y1, m, batch, m, transform, su, phase_u, bias, y, x_dtype, s);
+}

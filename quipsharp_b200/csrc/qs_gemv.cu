@@ -1,0 +1,256 @@
+// Fused codebook decode + matmul for the decode regime (few tokens):
+//   y1[tok, row] += layer_scale * rowscale[tok] * sum_s s_s * sum_k x2h[tok, k] * What_s[row, k]
+//
+// Weights stream from HBM once in the packed layout of qs_pack.cu and are
+// decoded in registers into fp16 mma.sync A fragments; the tokens form the
+// N=8 side of m16n8k16 (swap-AB GEMV).  Decode of one E8P code (8 weights):
+//   * one 8-byte shared-memory load of the fp16 high bytes of the table row
+//     (the table is replicated 16x so the 16 lanes of a half-warp hit distinct
+//     banks),
+//   * the eight sign flips are XORed into the byte sign bits: the packed code
+//     stores prefix parities g_i, so flips = g ^ (g << 8) for all codes of a
+//     16-byte quad at once, and the inferred 8th flip comes out of the same XOR,
+//   * four byte permutes build the f16x2 words, and the +-1/4 shift is one
+//     f16x2 add.  All decoded values are exact in fp16.
+// RVQ stages accumulate separately (exact weights) and are combined with their
+// float32 stage scales in the epilogue.  Each warp walks a contiguous range of
+// (code-chunk, row-tile) items; partial sums of a row tile are added to the
+// float32 y1 with atomics (y1 is zeroed by the input-transform kernel).
+#include "qs_common.cuh"
+#include "qs_launch.h"
+
+namespace qs {
+
+constexpr int kGemvThreads = 256;
+constexpr int kTblBytes = 256 * 256;  // 256 rows x (16 E8P replicas + 16 1-bit replicas) x 8 B
+
+struct GemvArgs {
+  const __half *x2h;       // (batch, n_pad)
+  const float *rowscale;   // (batch)
+  const uint8_t *stage[2];
+  float sscale[2];
+  const float *layer_scale;
+  float *y1;               // (batch, m)
+  int64_t m, RT, KC, n_pad, items;
+  int tok0, ntok;
+};
+
+__device__ __forceinline__ void load_table(uint8_t *tbl) {
+  for (int k = threadIdx.x; k < 256 * 32; k += blockDim.x) {
+    const int row = k >> 5, slot = k & 31;
+    const uint2 v = slot < 16 ? kE8pHiBytes[row] : kE81BitHiBytes[row];
+    *reinterpret_cast<uint2 *>(tbl + row * 256 + slot * 8) = v;
+  }
+}
+
+// Decoded f16x2 words of one code: W[0] = coords (0,1), ..., W[3] = (6,7).
+__device__ __forceinline__ void e8p_words(uint32_t tbl_lane, uint32_t idxsrc, int csel,
+                                          uint32_t flo, uint32_t fhi, uint32_t sw,
+                                          uint32_t (&W)[4]) {
+  const uint32_t a = prmt(idxsrc, tbl_lane & 0xFFu, 0x5504u | (static_cast<uint32_t>(csel) << 4));
+  const uint2 T = lds64((tbl_lane & ~0xFFu) + a);
+  const uint32_t tl = T.x ^ (flo & 0x80808080u);
+  const uint32_t th = T.y ^ (fhi & 0x80808080u);
+  W[0] = hadd2_u32(prmt(tl, 0u, 0x1404u), sw);
+  W[1] = hadd2_u32(prmt(tl, 0u, 0x3424u), sw);
+  W[2] = hadd2_u32(prmt(th, 0u, 0x1404u), sw);
+  W[3] = hadd2_u32(prmt(th, 0u, 0x3424u), sw);
+}
+
+__device__ __forceinline__ void onebit_words(uint32_t tbl_lane, uint32_t idxsrc, int csel,
+                                             uint32_t (&W)[4]) {
+  const uint32_t a = prmt(idxsrc, tbl_lane & 0xFFu, 0x5504u | (static_cast<uint32_t>(csel) << 4));
+  const uint2 T = lds64((tbl_lane & ~0xFFu) + a);
+  W[0] = prmt(T.x, 0u, 0x1404u);
+  W[1] = prmt(T.x, 0u, 0x3424u);
+  W[2] = prmt(T.y, 0u, 0x1404u);
+  W[3] = prmt(T.y, 0u, 0x3424u);
+}
+
+// One stage of one item: 8 codes for each of the lane's two rows, 16 mma.
+template <int KIND>
+__device__ __forceinline__ void stage_item(uint32_t tbl_e8p, uint32_t tbl_1b, const uint4 &qa,
+                                           const uint4 &qb, const uint32_t (&bf)[32],
+                                           float (&acc)[4]) {
+  if constexpr (KIND == QS_CB_E8P) {
+    const uint32_t floa = qa.z ^ (qa.z << 8), flob = qb.z ^ (qb.z << 8);
+    const uint32_t fhia = (qa.w & 0x00FFFFFFu) ^ shf_l_wrap(qa.z, qa.w, 8);
+    const uint32_t fhib = (qb.w & 0x00FFFFFFu) ^ shf_l_wrap(qb.z, qb.w, 8);
+#pragma unroll
+    for (int c = 0; c < 8; ++c) {
+      const uint32_t swa = 0x34003400u ^ (prmt(qa.w << c, 0u, 0xB4B4u) & 0x80008000u);
+      const uint32_t swb = 0x34003400u ^ (prmt(qb.w << c, 0u, 0xB4B4u) & 0x80008000u);
+      uint32_t Wa[4], Wb[4];
+      e8p_words(tbl_e8p, c < 4 ? qa.x : qa.y, c & 3, floa << c, fhia << c, swa, Wa);
+      e8p_words(tbl_e8p, c < 4 ? qb.x : qb.y, c & 3, flob << c, fhib << c, swb, Wb);
+      mma_16816(acc, Wa[0], Wb[0], Wa[1], Wb[1], bf[4 * c + 0], bf[4 * c + 1]);
+      mma_16816(acc, Wa[2], Wb[2], Wa[3], Wb[3], bf[4 * c + 2], bf[4 * c + 3]);
+    }
+  } else {
+    // 1-bit quad: qa = 16 bytes: row g codes 0..7 in (x, y), row g+8 in (z, w)
+#pragma unroll
+    for (int c = 0; c < 8; ++c) {
+      uint32_t Wa[4], Wb[4];
+      onebit_words(tbl_1b, c < 4 ? qa.x : qa.y, c & 3, Wa);
+      onebit_words(tbl_1b, c < 4 ? qa.z : qa.w, c & 3, Wb);
+      mma_16816(acc, Wa[0], Wb[0], Wa[1], Wb[1], bf[4 * c + 0], bf[4 * c + 1]);
+      mma_16816(acc, Wa[2], Wb[2], Wa[3], Wb[3], bf[4 * c + 2], bf[4 * c + 3]);
+    }
+  }
+}
+
+// Quad registers of one item: stage 0 in q[0..n0), stage 1 in q[n0..n0+n1),
+// with n = 2 for E8P (rows g and g+8) and 1 for 1-bit (both rows in 16 B).
+template <int K>
+constexpr int nquads() { return K == QS_CB_E8P ? 2 : 1; }
+
+template <int K0, int K1, int NST>
+__device__ __forceinline__ void load_item(const GemvArgs &a, int64_t it, int lane, uint4 (&q)[4]) {
+  const uint8_t *p0 = a.stage[0] + it * item_bytes(K0) + lane * 16;
+  q[0] = ldg_nc_v4(p0);
+  if constexpr (K0 == QS_CB_E8P) q[1] = ldg_nc_v4(p0 + 512);
+  if constexpr (NST == 2) {
+    constexpr int o = nquads<K0>();
+    const uint8_t *p1 = a.stage[1] + it * item_bytes(K1) + lane * 16;
+    q[o] = ldg_nc_v4(p1);
+    if constexpr (K1 == QS_CB_E8P) q[o + 1] = ldg_nc_v4(p1 + 512);
+  }
+}
+
+template <int K0, int K1, int NST>
+__global__ void __launch_bounds__(kGemvThreads, 2) gemv_kernel(GemvArgs a) {
+  extern __shared__ __align__(256) uint8_t gsm[];
+  // the table must start on a 256-byte boundary of the shared window: the
+  // decode puts the row index in address bits 8..15 with a byte permute
+  uint8_t *tbl = gsm + ((256u - (smem_u32(gsm) & 255u)) & 255u);
+  load_table(tbl);
+  __syncthreads();
+
+  const int lane = threadIdx.x & 31;
+  const int64_t warp = blockIdx.x * (kGemvThreads / 32) + (threadIdx.x >> 5);
+  const int64_t nwarps = static_cast<int64_t>(gridDim.x) * (kGemvThreads / 32);
+  const int64_t start = warp * a.items / nwarps, end = (warp + 1) * a.items / nwarps;
+  if (start >= end) return;
+
+  const uint32_t tbase = smem_u32(tbl);
+  const uint32_t tbl_e8p = tbase + (lane & 15) * 8;        // byte 0 < 128: lane replica
+  const uint32_t tbl_1b = tbase + 128 + (lane & 15) * 8;   // byte 0 in [128, 256)
+  const int g = lane >> 2, t = lane & 3;
+  const float ls = *a.layer_scale;
+
+  uint32_t bf[32];
+  int64_t kc_cur = -1;
+  uint4 q[4], nq[4];
+  load_item<K0, K1, NST>(a, start, lane, q);
+  for (int64_t it = start; it < end; ++it) {
+    const int64_t kc = it / a.RT, rt = it % a.RT;
+    if (kc != kc_cur) {
+      kc_cur = kc;
+      if (g < a.ntok) {
+        const uint4 *src = reinterpret_cast<const uint4 *>(a.x2h + (a.tok0 + g) * a.n_pad + kc * 256 + t * 64);
+#pragma unroll
+        for (int c = 0; c < 8; ++c) {
+          const uint4 v = __ldg(src + c);
+          bf[4 * c + 0] = v.x;
+          bf[4 * c + 1] = v.y;
+          bf[4 * c + 2] = v.z;
+          bf[4 * c + 3] = v.w;
+        }
+      } else {
+#pragma unroll
+        for (int i = 0; i < 32; ++i) bf[i] = 0u;
+      }
+    }
+    if (it + 1 < end) load_item<K0, K1, NST>(a, it + 1, lane, nq);
+
+    float acc0[4] = {0.f, 0.f, 0.f, 0.f};
+    float acc1[4] = {0.f, 0.f, 0.f, 0.f};
+    stage_item<K0>(tbl_e8p, tbl_1b, q[0], q[nquads<K0>() - 1], bf, acc0);
+    if constexpr (NST == 2) {
+      constexpr int o = nquads<K0>();
+      stage_item<K1>(tbl_e8p, tbl_1b, q[o], q[o + nquads<K1>() - 1], bf, acc1);
+    }
+
+    // epilogue: c0 (row g, tok 2t), c1 (row g, tok 2t+1), c2/c3 rows g+8
+    const int64_t row0 = rt * kRowsPerTile + g, row1 = row0 + 8;
+#pragma unroll
+    for (int j = 0; j < 2; ++j) {
+      const int tok = 2 * t + j;
+      if (tok < a.ntok) {
+        const int gt = a.tok0 + tok;
+        const float f = ls * a.rowscale[gt];
+        float v0 = a.sscale[0] * acc0[j], v1 = a.sscale[0] * acc0[2 + j];
+        if constexpr (NST == 2) {
+          v0 = fmaf(a.sscale[1], acc1[j], v0);
+          v1 = fmaf(a.sscale[1], acc1[2 + j], v1);
+        }
+        if (row0 < a.m) atomicAdd(a.y1 + gt * a.m + row0, v0 * f);
+        if (row1 < a.m) atomicAdd(a.y1 + gt * a.m + row1, v1 * f);
+      }
+    }
+#pragma unroll
+    for (int i = 0; i < 4; ++i) q[i] = nq[i];
+  }
+}
+
+static int num_sms() {
+  static int cached[64] = {0};
+  int dev = 0;
+  cudaGetDevice(&dev);
+  if (dev < 64 && cached[dev]) return cached[dev];
+  int n = 148;
+  cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, dev);
+  if (dev < 64) cached[dev] = n;
+  return n;
+}
+
+template <int K0, int K1, int NST>
+static int run_gemv(GemvArgs &a, int64_t batch, cudaStream_t s) {
+  auto kern = gemv_kernel<K0, K1, NST>;
+  QS_CUDA_TRY(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, kTblBytes + 256));
+  const int64_t warps_needed = a.items;
+  int grid = 2 * num_sms();
+  if (warps_needed < static_cast<int64_t>(grid) * (kGemvThreads / 32))
+    grid = static_cast<int>(ceil_div(warps_needed, kGemvThreads / 32));
+  for (int64_t tok0 = 0; tok0 < batch; tok0 += 8) {
+    a.tok0 = static_cast<int>(tok0);
+    a.ntok = static_cast<int>(batch - tok0 < 8 ? batch - tok0 : 8);
+    kern<<<grid, kGemvThreads, kTblBytes + 256, s>>>(a);
+    int st = check_launch("gemv");
+    if (st) return st;
+  }
+  return QS_OK;
+}
+
+int launch_matmul(const void *x2ws, int64_t batch, int64_t n, int64_t m, const void *packed,
+                  int stages, const int *kinds, const float *stage_scales,
+                  const float *layer_scale, float *y1, cudaStream_t s) {
+  GemvArgs a{};
+  a.n_pad = padded_T(n) * 8;
+  a.x2h = static_cast<const __half *>(x2ws);
+  a.rowscale = reinterpret_cast<const float *>(static_cast<const char *>(x2ws) +
+                                               round_up(batch * a.n_pad * 2, 256));
+  a.m = m;
+  a.RT = padded_m(m) / kRowsPerTile;
+  a.KC = padded_T(n) / kCodesPerChunk;
+  a.items = a.RT * a.KC;
+  a.layer_scale = layer_scale;
+  a.y1 = y1;
+  const uint8_t *p = static_cast<const uint8_t *>(packed);
+  for (int st = 0; st < stages; ++st) {
+    a.stage[st] = p;
+    a.sscale[st] = stage_scales ? stage_scales[st] : 1.f;
+    p += round_up(stage_bytes(kinds[st], m, n), 256);
+  }
+  const int k0 = kinds[0], k1 = stages == 2 ? kinds[1] : 0;
+  if (stages == 1) {
+    return k0 == QS_CB_E8P ? run_gemv<QS_CB_E8P, 0, 1>(a, batch, s)
+                           : run_gemv<QS_CB_E8_1BIT, 0, 1>(a, batch, s);
+  }
+  if (k0 == QS_CB_E8P && k1 == QS_CB_E8_1BIT) return run_gemv<QS_CB_E8P, QS_CB_E8_1BIT, 2>(a, batch, s);
+  if (k0 == QS_CB_E8P && k1 == QS_CB_E8P) return run_gemv<QS_CB_E8P, QS_CB_E8P, 2>(a, batch, s);
+  if (k0 == QS_CB_E8_1BIT && k1 == QS_CB_E8P) return run_gemv<QS_CB_E8_1BIT, QS_CB_E8P, 2>(a, batch, s);
+  return run_gemv<QS_CB_E8_1BIT, QS_CB_E8_1BIT, 2>(a, batch, s);
+}
+
+}  // namespace qs

@@ -1,0 +1,41 @@
+// Internal launchers shared between the translation units of the library.
+#pragma once
+
+#include <cuda_runtime.h>
+#include <stdint.h>
+
+namespace qs {
+
+// qs_decode.cu
+int launch_decode(int kind, const void *codes, int code_dtype, int64_t count, float *out,
+                  cudaStream_t s);
+int launch_rvq_decode(int stages, const int *kinds, const void *const *codes, int code_dtype,
+                      const float *stage_scales, int64_t count, float *out, cudaStream_t s);
+int launch_dequantize_linear(const int16_t *codes, int stages, const int *kinds,
+                             const float *stage_scales, const float *layer_scale, int64_t m,
+                             int64_t n, float *out, cudaStream_t s);
+
+// qs_transform.cu
+int launch_fwht(const void *x, int64_t ld_x, void *y, int64_t ld_y, int dtype, int64_t rows,
+                int64_t n, const float *pre, const float *post, cudaStream_t s);
+int launch_rfft(int inverse, const void *x, int64_t ld_x, void *y, int64_t ld_y, int dtype,
+                int64_t rows, int64_t n, const void *phase, cudaStream_t s);
+int64_t linear_input_bytes(int64_t batch, int64_t n);
+int launch_linear_input(const void *x, int x_dtype, int64_t batch, int64_t n, int transform,
+                        const float *sv, const void *phase_v, void *x2ws, float *y1,
+                        int64_t m_local, cudaStream_t s);
+int launch_linear_output(const float *y1, int64_t ld_y1, int64_t batch, int64_t m, int transform,
+                         const float *su, const void *phase_u, const float *bias, void *y,
+                         int y_dtype, cudaStream_t s);
+int check_fft_size(int64_t n_complex);
+
+// qs_pack.cu
+int launch_pack(const int16_t *codes, int stages, const int *kinds, int64_t m, int64_t n,
+                void *packed, cudaStream_t s);
+
+// qs_gemv.cu
+int launch_matmul(const void *x2ws, int64_t batch, int64_t n, int64_t m, const void *packed,
+                  int stages, const int *kinds, const float *stage_scales,
+                  const float *layer_scale, float *y1, cudaStream_t s);
+
+}  // namespace qs
