@@ -273,7 +273,7 @@ def run_ours(args):
             N.check(N.lib().qs_linear_matmul(N.ptr(ws_in), B, n, m, N.ptr(k.packed), len(k.kinds), kinds_c, ss_c,
                                              N.ptr(k.scale), N.ptr(y1), s))
             if not matmul_only:
-                N.check(N.lib().qs_linear_output(N.ptr(y1), m, B, m, k.transform, N.ptr(k.su), N.ptr(k.phase_u),
+                N.check(N.lib().qs_linear_output(N.ptr(y1), m, 1, B, m, k.transform, N.ptr(k.su), N.ptr(k.phase_u),
                                                  N.ptr(k.bias), N.ptr(y_dev[0]), io, s))
 
     def capture(fn):

@@ -144,8 +144,11 @@ int qs_linear_fwd(const void *x, int x_dtype, int64_t batch, int64_t n, int64_t 
  *  - qs_linear_input: x -> x2 (fp16 tiles + per-row scale in workspace) and
  *    zeroes y1 (batch, m_local) float32.
  *  - qs_linear_matmul: y1 += x2 @ What_local^T * scales (rows m_local).
- *  - qs_linear_output: y = cast(transform_out(y1) + bias), y1 float32 (batch, m)
- *    with row stride ld_y1. */
+ *  - qs_linear_output: y = cast(transform_out(y1) + bias).  With shards == 1,
+ *    y1 is float32 (batch, m) with row stride ld_y1.  With shards = P > 1, y1
+ *    is the rank-major result of an all-gather of P shards of (batch, m/P):
+ *    element (b, c) sits at ((c / (m/P)) * batch + b) * (m/P) + c % (m/P)
+ *    (ld_y1 is ignored), so no re-layout copy is needed after the gather. */
 int64_t qs_linear_input_bytes(int64_t batch, int64_t n);
 int qs_linear_input(const void *x, int x_dtype, int64_t batch, int64_t n, int transform,
                     const float *sv, const void *phase_v, void *x2_workspace,
@@ -154,9 +157,9 @@ int qs_linear_matmul(const void *x2_workspace, int64_t batch, int64_t n, int64_t
                      const void *packed, int stages, const int *kinds,
                      const float *stage_scales, const float *layer_scale, float *y1,
                      qs_stream_t stream);
-int qs_linear_output(const float *y1, int64_t ld_y1, int64_t batch, int64_t m, int transform,
-                     const float *su, const void *phase_u, const float *bias, void *y,
-                     int y_dtype, qs_stream_t stream);
+int qs_linear_output(const float *y1, int64_t ld_y1, int64_t shards, int64_t batch, int64_t m,
+                     int transform, const float *su, const void *phase_u, const float *bias,
+                     void *y, int y_dtype, qs_stream_t stream);
 
 #ifdef __cplusplus
 }

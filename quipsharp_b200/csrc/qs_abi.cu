@@ -208,17 +208,20 @@ QS_API int qs_linear_matmul(const void *x2_workspace, int64_t batch, int64_t n, 
                        layer_scale, y1, (cudaStream_t)stream);
 }
 
-QS_API int qs_linear_output(const float *y1, int64_t ld_y1, int64_t batch, int64_t m, int transform,
-                            const float *su, const void *phase_u, const float *bias, void *y,
-                            int y_dtype, qs_stream_t stream) {
+QS_API int qs_linear_output(const float *y1, int64_t ld_y1, int64_t shards, int64_t batch,
+                            int64_t m, int transform, const float *su, const void *phase_u,
+                            const float *bias, void *y, int y_dtype, qs_stream_t stream) {
   if (!valid_io_dtype(y_dtype)) return fail(QS_ERR_INVALID_ARG, "bad dtype %d", y_dtype);
   int st = check_transform_args(transform, m, transform == QS_RHT ? 1 : 2, su, su, phase_u, phase_u);
   if (st) return st;
-  if (batch < 0 || ld_y1 < m) return fail(QS_ERR_INVALID_ARG, "bad batch / ld_y1");
+  if (shards < 1 || m % shards) return fail(QS_ERR_INVALID_ARG, "m=%lld not divisible by %lld shards", (long long)m, (long long)shards);
+  if (shards > 1 && transform == QS_RFFT && (m / shards) % 2)
+    return fail(QS_ERR_INVALID_ARG, "RFFT shards must hold an even number of columns");
+  if (batch < 0 || (shards == 1 && ld_y1 < m)) return fail(QS_ERR_INVALID_ARG, "bad batch / ld_y1");
   if (batch == 0) return QS_OK;
   if (!y1 || !y) return fail(QS_ERR_INVALID_ARG, "null pointer");
-  return launch_linear_output(y1, ld_y1, batch, m, transform, su, phase_u, bias, y, y_dtype,
-                              (cudaStream_t)stream);
+  return launch_linear_output(y1, shards == 1 ? ld_y1 : m, shards, batch, m, transform, su, phase_u,
+                              bias, y, y_dtype, (cudaStream_t)stream);
 }
 
 QS_API int qs_linear_fwd(const void *x, int x_dtype, int64_t batch, int64_t n, int64_t m,
@@ -245,5 +248,5 @@ QS_API int qs_linear_fwd(const void *x, int x_dtype, int64_t batch, int64_t n, i
   if (st) return st;
   st = launch_matmul(workspace, batch, n, m, packed, stages, kinds, stage_scales, layer_scale, y1, s);
   if (st) return st;
-  return launch_linear_output(y1, m, batch, m, transform, su, phase_u, bias, y, x_dtype, s);
+  return launch_linear_output(y1, m, 1, batch, m, transform, su, phase_u, bias, y, x_dtype, s);
 }

@@ -24,9 +24,9 @@ int64_t linear_input_bytes(int64_t batch, int64_t n);
 int launch_linear_input(const void *x, int x_dtype, int64_t batch, int64_t n, int transform,
                         const float *sv, const void *phase_v, void *x2ws, float *y1,
                         int64_t m_local, cudaStream_t s);
-int launch_linear_output(const float *y1, int64_t ld_y1, int64_t batch, int64_t m, int transform,
-                         const float *su, const void *phase_u, const float *bias, void *y,
-                         int y_dtype, cudaStream_t s);
+int launch_linear_output(const float *y1, int64_t ld_y1, int64_t shards, int64_t batch, int64_t m,
+                         int transform, const float *su, const void *phase_u, const float *bias,
+                         void *y, int y_dtype, cudaStream_t s);
 int check_fft_size(int64_t n_complex);
 
 // qs_pack.cu

@@ -639,14 +639,25 @@ int launch_linear_input(const void *x, int x_dtype, int64_t batch, int64_t n, in
   return check_launch("linear_input_rfft");
 }
 
+// Offset of y1 element (row, col): plain row-major with stride ld_y1 when
+// shards == 1, else the rank-major layout of an all-gather of `shards` column
+// blocks of (batch, mp): ((col / mp) * batch + row) * mp + col % mp.
+__device__ __forceinline__ int64_t y1_offset(int64_t row, int64_t col, int64_t ld_y1, int64_t shards,
+                                             int64_t mp, int64_t batch) {
+  if (shards == 1) return row * ld_y1 + col;
+  return ((col / mp) * batch + row) * mp + col % mp;
+}
+
 __global__ void __launch_bounds__(1024) linear_output_rht_kernel(const float *y1, int64_t ld_y1,
+                                                                 int64_t shards, int64_t batch,
                                                                  int L, int E, const float *su,
                                                                  const float *bias, float scale,
                                                                  void *y, int dtype) {
   extern __shared__ float fsm[];
   const int m = 1 << L;
+  const int64_t mp = m / shards;
   const int64_t row = blockIdx.x;
-  for (int i = threadIdx.x; i < m; i += blockDim.x) fsm[fpad(i)] = y1[row * ld_y1 + i];
+  for (int i = threadIdx.x; i < m; i += blockDim.x) fsm[fpad(i)] = y1[y1_offset(row, i, ld_y1, shards, mp, batch)];
   __syncthreads();
   fwht_smem(fsm, L, E);
   for (int i = threadIdx.x; i < m; i += blockDim.x) {
@@ -658,14 +669,15 @@ __global__ void __launch_bounds__(1024) linear_output_rht_kernel(const float *y1
 
 template <bool PP>
 __global__ void __launch_bounds__(PP ? 512 : 1024) linear_output_rfft_kernel(
-    const float *y1, int64_t ld_y1, FftPlan plan, const float2 *phase, const float *bias,
-    float scale, void *y, int dtype) {
+    const float *y1, int64_t ld_y1, int64_t shards, int64_t batch, FftPlan plan, const float2 *phase,
+    const float *bias, float scale, void *y, int dtype) {
   extern __shared__ float2 csm[];
   float2 *buf1 = csm + fft_buf_elems(plan.N);
   const int N = plan.N;
+  const int64_t mp = 2 * N / shards;
   const int64_t row = blockIdx.x;
-  const float2 *src = reinterpret_cast<const float2 *>(y1 + row * ld_y1);
-  for (int i = threadIdx.x; i < N; i += blockDim.x) csm[cpad(i)] = src[i];
+  for (int i = threadIdx.x; i < N; i += blockDim.x)
+    csm[cpad(i)] = *reinterpret_cast<const float2 *>(y1 + y1_offset(row, 2 * i, ld_y1, shards, mp, batch));
   __syncthreads();
   const float2 *res = fft_smem<PP>(csm, buf1, plan, true);
   for (int i = threadIdx.x; i < N; i += blockDim.x) {
@@ -683,16 +695,16 @@ __global__ void __launch_bounds__(PP ? 512 : 1024) linear_output_rfft_kernel(
   }
 }
 
-int launch_linear_output(const float *y1, int64_t ld_y1, int64_t batch, int64_t m, int transform,
-                         const float *su, const void *phase_u, const float *bias, void *y,
-                         int y_dtype, cudaStream_t s) {
+int launch_linear_output(const float *y1, int64_t ld_y1, int64_t shards, int64_t batch, int64_t m,
+                         int transform, const float *su, const void *phase_u, const float *bias,
+                         void *y, int y_dtype, cudaStream_t s) {
   if (transform == QS_RHT) {
     FwhtGeom g = fwht_geom(m);
     QS_CUDA_TRY(cudaFuncSetAttribute(linear_output_rht_kernel,
                                      cudaFuncAttributeMaxDynamicSharedMemorySize,
                                      static_cast<int>(g.smem)));
-    linear_output_rht_kernel<<<batch, g.threads, g.smem, s>>>(y1, ld_y1, g.L, g.E, su, bias,
-                                                             inv_sqrt_f32(m), y, y_dtype);
+    linear_output_rht_kernel<<<batch, g.threads, g.smem, s>>>(y1, ld_y1, shards, batch, g.L, g.E, su,
+                                                             bias, inv_sqrt_f32(m), y, y_dtype);
     return check_launch("linear_output_rht");
   }
   if (ld_y1 % 2) return fail(QS_ERR_ALIGNMENT, "RFFT y1 row stride must be even");
@@ -703,12 +715,12 @@ int launch_linear_output(const float *y1, int64_t ld_y1, int64_t batch, int64_t 
   const float2 *ph = static_cast<const float2 *>(phase_u);
   if (p.pingpong) {
     if ((st = set_smem(linear_output_rfft_kernel<true>, smem))) return st;
-    linear_output_rfft_kernel<true><<<batch, p.threads, smem, s>>>(y1, ld_y1, p, ph, bias,
-                                                                   inv_sqrt_f32(m / 2), y, y_dtype);
+    linear_output_rfft_kernel<true><<<batch, p.threads, smem, s>>>(y1, ld_y1, shards, batch, p, ph,
+                                                                   bias, inv_sqrt_f32(m / 2), y, y_dtype);
   } else {
     if ((st = set_smem(linear_output_rfft_kernel<false>, smem))) return st;
-    linear_output_rfft_kernel<false><<<batch, p.threads, smem, s>>>(y1, ld_y1, p, ph, bias,
-                                                                    inv_sqrt_f32(m / 2), y, y_dtype);
+    linear_output_rfft_kernel<false><<<batch, p.threads, smem, s>>>(y1, ld_y1, shards, batch, p, ph,
+                                                                    bias, inv_sqrt_f32(m / 2), y, y_dtype);
   }
   return check_launch("linear_output_rfft");
 }

@@ -113,6 +113,23 @@ class LinearKernel:
     def workspace_bytes(self, batch: int) -> int:
         return N.lib().qs_linear_workspace_bytes(batch, self.m, self.n)
 
+    # ---- the three steps, for callers that insert a collective (tensor parallel)
+    def input(self, x2: Tensor, y1: Tensor | None) -> Tensor:
+        """x2 (B, n) -> fp16 matmul operand workspace; zeroes y1 (B, m) if given."""
+        B = x2.shape[0]
+        nb = N.lib().qs_linear_input_bytes(B, self.n)
+        ws = torch.empty(max(nb, 1), dtype=torch.uint8, device=x2.device)
+        N.check(N.lib().qs_linear_input(N.ptr(x2), N.IO_DTYPES[x2.dtype], B, self.n, self.transform,
+                                        N.ptr(self.sv), N.ptr(self.phase_v), N.ptr(ws), ws.numel(),
+                                        N.ptr(y1), 0 if y1 is None else self.m, N.stream_of(x2)))
+        return ws
+
+    def matmul(self, ws: Tensor, B: int, y1: Tensor) -> None:
+        """y1 (B, m) float32 += x2 @ What^T (this kernel's rows)."""
+        N.check(N.lib().qs_linear_matmul(N.ptr(ws), B, self.n, self.m, N.ptr(self.packed), len(self.kinds),
+                                         self._kinds_c, self._ss_c, N.ptr(self.scale), N.ptr(y1),
+                                         N.stream_of(y1)))
+
     def __call__(self, x: Tensor, out: Tensor | None = None, workspace: Tensor | None = None) -> Tensor:
         """x (..., n) of float32/float16/bfloat16 -> y (..., m) of the same dtype."""
         N.require_cuda(x)
