@@ -56,6 +56,19 @@ __device__ __forceinline__ uint32_t shf_l_wrap(uint32_t lo, uint32_t hi, uint32_
   return d;
 }
 
+// x * 2^k as an integer multiply-add (runs on the FMA pipe, not the ALU pipe).
+__device__ __forceinline__ uint32_t imul(uint32_t x, uint32_t k) {
+  uint32_t d;
+  asm("mul.lo.u32 %0, %1, %2;" : "=r"(d) : "r"(x), "r"(k));
+  return d;
+}
+
+__device__ __forceinline__ uint32_t imad(uint32_t a, uint32_t b, uint32_t c) {
+  uint32_t d;
+  asm("mad.lo.u32 %0, %1, %2, %3;" : "=r"(d) : "r"(a), "r"(b), "r"(c));
+  return d;
+}
+
 __device__ __forceinline__ uint32_t hadd2_u32(uint32_t a, uint32_t b) {
   uint32_t d;
   asm("add.rn.f16x2 %0, %1, %2;" : "=r"(d) : "r"(a), "r"(b));
@@ -72,18 +85,22 @@ __device__ __forceinline__ uint2 lds64(uint32_t addr) {
   return v;
 }
 
+// Read-only streaming load (weights read once per launch).  Not volatile:
+// ordering follows data dependencies so loads can overlap with compute.
 __device__ __forceinline__ uint4 ldg_nc_v4(const void *p) {
   uint4 v;
-  asm volatile("ld.global.nc.L1::no_allocate.v4.u32 {%0, %1, %2, %3}, [%4];"
-               : "=r"(v.x), "=r"(v.y), "=r"(v.z), "=r"(v.w)
-               : "l"(p));
+  asm("ld.global.nc.L1::no_allocate.v4.u32 {%0, %1, %2, %3}, [%4];"
+      : "=r"(v.x), "=r"(v.y), "=r"(v.z), "=r"(v.w)
+      : "l"(p));
   return v;
 }
 
-// D (16x8 f32) += A (16x16 f16, row) * B (16x8 f16, col)
+// D (16x8 f32) += A (16x16 f16, row) * B (16x8 f16, col).  Not volatile: the
+// accumulator operands order dependent mma; independent ones may interleave
+// with the decode of the next code.
 __device__ __forceinline__ void mma_16816(float (&d)[4], uint32_t a0, uint32_t a1, uint32_t a2,
                                           uint32_t a3, uint32_t b0, uint32_t b1) {
-  asm volatile(
+  asm(
       "mma.sync.aligned.m16n8k16.row.col.f32.f16.f16.f32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, "
       "{%8,%9}, {%0,%1,%2,%3};"
       : "+f"(d[0]), "+f"(d[1]), "+f"(d[2]), "+f"(d[3])

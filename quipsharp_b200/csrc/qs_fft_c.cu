@@ -1,0 +1,7 @@
+// Explicit instantiations of the FFT kernels (split for parallel compilation).
+#include "qs_fft.cuh"
+
+namespace qs {
+QS_DEFINE_FFT_RUNNERS(true, 23)
+QS_DEFINE_FFT_RUNNERS(true, 29)
+}  // namespace qs

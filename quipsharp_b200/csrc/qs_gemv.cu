@@ -44,57 +44,79 @@ __device__ __forceinline__ void load_table(uint8_t *tbl) {
 }
 
 // Decoded f16x2 words of one code: W[0] = coords (0,1), ..., W[3] = (6,7).
-__device__ __forceinline__ void e8p_words(uint32_t tbl_lane, uint32_t idxsrc, int csel,
-                                          uint32_t flo, uint32_t fhi, uint32_t sw,
-                                          uint32_t (&W)[4]) {
-  const uint32_t a = prmt(idxsrc, tbl_lane & 0xFFu, 0x5504u | (static_cast<uint32_t>(csel) << 4));
-  const uint2 T = lds64((tbl_lane & ~0xFFu) + a);
-  const uint32_t tl = T.x ^ (flo & 0x80808080u);
-  const uint32_t th = T.y ^ (fhi & 0x80808080u);
-  W[0] = hadd2_u32(prmt(tl, 0u, 0x1404u), sw);
-  W[1] = hadd2_u32(prmt(tl, 0u, 0x3424u), sw);
-  W[2] = hadd2_u32(prmt(th, 0u, 0x1404u), sw);
-  W[3] = hadd2_u32(prmt(th, 0u, 0x3424u), sw);
+// tbl_lane: table base + this lane's replica offset; idxsrc byte csel holds
+// the row index.  E8P: the eight sign flips (flo/fhi, already shifted to the
+// byte sign bits) are XORed into the fp16 high bytes; the +-1/4 shift is added
+// by the tensor core (see shift_words), so W holds sign*|t| exactly.
+// tbl: the shared table; lane_off: this lane's replica offset within a row.
+// A plain shared-memory load (not asm) so the compiler can hoist it ahead of
+// the previous code's permutes while keeping it after the table fill barrier.
+__device__ __forceinline__ uint2 table_row(const uint8_t *tbl, uint32_t lane_off, uint32_t idxsrc, int csel) {
+  const uint32_t idx = prmt(idxsrc, 0u, 0x4440u | static_cast<uint32_t>(csel));
+  return *reinterpret_cast<const uint2 *>(tbl + imad(idx, 256u, lane_off));
 }
 
-__device__ __forceinline__ void onebit_words(uint32_t tbl_lane, uint32_t idxsrc, int csel,
+__device__ __forceinline__ void e8p_words(const uint8_t *tbl, uint32_t lane_off, uint32_t idxsrc, int csel,
+                                          uint32_t flo, uint32_t fhi, uint32_t (&W)[4]) {
+  const uint2 T = table_row(tbl, lane_off, idxsrc, csel);
+  const uint32_t tl = T.x ^ (flo & 0x80808080u);
+  const uint32_t th = T.y ^ (fhi & 0x80808080u);
+  W[0] = prmt(tl, 0u, 0x1404u);
+  W[1] = prmt(tl, 0u, 0x3424u);
+  W[2] = prmt(th, 0u, 0x1404u);
+  W[3] = prmt(th, 0u, 0x3424u);
+}
+
+__device__ __forceinline__ void onebit_words(const uint8_t *tbl, uint32_t lane_off, uint32_t idxsrc, int csel,
                                              uint32_t (&W)[4]) {
-  const uint32_t a = prmt(idxsrc, tbl_lane & 0xFFu, 0x5504u | (static_cast<uint32_t>(csel) << 4));
-  const uint2 T = lds64((tbl_lane & ~0xFFu) + a);
+  const uint2 T = table_row(tbl, lane_off, idxsrc, csel);
   W[0] = prmt(T.x, 0u, 0x1404u);
   W[1] = prmt(T.x, 0u, 0x3424u);
   W[2] = prmt(T.y, 0u, 0x1404u);
   W[3] = prmt(T.y, 0u, 0x3424u);
 }
 
-// One stage of one item: 8 codes for each of the lane's two rows, 16 mma.
+// The +-1/4 shifts of the 8 codes of a quad as four f16x2 words of +-0.25:
+// sw[p] holds (code 2p+1, code 2p) in (low, high) halves.  w3 carries the
+// negated shift bit of code c at bit 31-c (qs_pack.cu).
+__device__ __forceinline__ void shift_words(uint32_t w3, uint32_t (&sw)[4]) {
+  const uint32_t y = prmt(w3, imul(w3, 2u), 0x3070u);  // byte3 <- w3.b3, byte1 <- (w3<<1).b3
+#pragma unroll
+  for (int p = 0; p < 4; ++p) sw[p] = 0x34003400u ^ (imul(y, 1u << (2 * p)) & 0x80008000u);
+}
+
+// One stage of one item: 8 codes for each of the lane's two rows (16 mma),
+// plus 2 mma for the E8P shifts against the per-code activation sums sf.
 template <int KIND>
-__device__ __forceinline__ void stage_item(uint32_t tbl_e8p, uint32_t tbl_1b, const uint4 &qa,
+__device__ __forceinline__ void stage_item(const uint8_t *tbl, uint32_t off_e8p, uint32_t off_1b, const uint4 &qa,
                                            const uint4 &qb, const uint32_t (&bf)[32],
-                                           float (&acc)[4]) {
+                                           const uint32_t (&sf)[4], float (&acc)[4], float (&acc2)[4]) {
   if constexpr (KIND == QS_CB_E8P) {
-    const uint32_t floa = qa.z ^ (qa.z << 8), flob = qb.z ^ (qb.z << 8);
+    const uint32_t floa = qa.z ^ imul(qa.z, 256u), flob = qb.z ^ imul(qb.z, 256u);
     const uint32_t fhia = (qa.w & 0x00FFFFFFu) ^ shf_l_wrap(qa.z, qa.w, 8);
     const uint32_t fhib = (qb.w & 0x00FFFFFFu) ^ shf_l_wrap(qb.z, qb.w, 8);
 #pragma unroll
     for (int c = 0; c < 8; ++c) {
-      const uint32_t swa = 0x34003400u ^ (prmt(qa.w << c, 0u, 0xB4B4u) & 0x80008000u);
-      const uint32_t swb = 0x34003400u ^ (prmt(qb.w << c, 0u, 0xB4B4u) & 0x80008000u);
       uint32_t Wa[4], Wb[4];
-      e8p_words(tbl_e8p, c < 4 ? qa.x : qa.y, c & 3, floa << c, fhia << c, swa, Wa);
-      e8p_words(tbl_e8p, c < 4 ? qb.x : qb.y, c & 3, flob << c, fhib << c, swb, Wb);
+      e8p_words(tbl, off_e8p, c < 4 ? qa.x : qa.y, c & 3, imul(floa, 1u << c), imul(fhia, 1u << c), Wa);
+      e8p_words(tbl, off_e8p, c < 4 ? qb.x : qb.y, c & 3, imul(flob, 1u << c), imul(fhib, 1u << c), Wb);
       mma_16816(acc, Wa[0], Wb[0], Wa[1], Wb[1], bf[4 * c + 0], bf[4 * c + 1]);
-      mma_16816(acc, Wa[2], Wb[2], Wa[3], Wb[3], bf[4 * c + 2], bf[4 * c + 3]);
+      mma_16816(acc2, Wa[2], Wb[2], Wa[3], Wb[3], bf[4 * c + 2], bf[4 * c + 3]);
     }
+    uint32_t swa[4], swb[4];
+    shift_words(qa.w, swa);
+    shift_words(qb.w, swb);
+    mma_16816(acc, swa[0], swb[0], swa[1], swb[1], sf[0], sf[1]);
+    mma_16816(acc2, swa[2], swb[2], swa[3], swb[3], sf[2], sf[3]);
   } else {
     // 1-bit quad: qa = 16 bytes: row g codes 0..7 in (x, y), row g+8 in (z, w)
 #pragma unroll
     for (int c = 0; c < 8; ++c) {
       uint32_t Wa[4], Wb[4];
-      onebit_words(tbl_1b, c < 4 ? qa.x : qa.y, c & 3, Wa);
-      onebit_words(tbl_1b, c < 4 ? qa.z : qa.w, c & 3, Wb);
+      onebit_words(tbl, off_1b, c < 4 ? qa.x : qa.y, c & 3, Wa);
+      onebit_words(tbl, off_1b, c < 4 ? qa.z : qa.w, c & 3, Wb);
       mma_16816(acc, Wa[0], Wb[0], Wa[1], Wb[1], bf[4 * c + 0], bf[4 * c + 1]);
-      mma_16816(acc, Wa[2], Wb[2], Wa[3], Wb[3], bf[4 * c + 2], bf[4 * c + 3]);
+      mma_16816(acc2, Wa[2], Wb[2], Wa[3], Wb[3], bf[4 * c + 2], bf[4 * c + 3]);
     }
   }
 }
@@ -117,11 +139,45 @@ __device__ __forceinline__ void load_item(const GemvArgs &a, int64_t it, int lan
   }
 }
 
+// Activation fragments of one code chunk for token g (or zeros): bf holds
+// the 64 fp16 inputs of codes 8t..8t+7 (B operands of the 16 mma), sf the
+// per-code sums as (code 2p+1, code 2p) f16x2 pairs (B operands of the shift mma).
+__device__ __forceinline__ void load_activations(const GemvArgs &a, int64_t kc, int g, int t,
+                                                 uint32_t (&bf)[32], uint32_t (&sf)[4]) {
+  if (g < a.ntok) {
+    const uint4 *src = reinterpret_cast<const uint4 *>(a.x2h + (a.tok0 + g) * a.n_pad + kc * 256 + t * 64);
+    float sum[8];
+#pragma unroll
+    for (int c = 0; c < 8; ++c) {
+      const uint4 v = __ldg(src + c);
+      bf[4 * c + 0] = v.x;
+      bf[4 * c + 1] = v.y;
+      bf[4 * c + 2] = v.z;
+      bf[4 * c + 3] = v.w;
+      const float2 f0 = __half22float2(*reinterpret_cast<const __half2 *>(&v.x));
+      const float2 f1 = __half22float2(*reinterpret_cast<const __half2 *>(&v.y));
+      const float2 f2 = __half22float2(*reinterpret_cast<const __half2 *>(&v.z));
+      const float2 f3 = __half22float2(*reinterpret_cast<const __half2 *>(&v.w));
+      sum[c] = ((f0.x + f0.y) + (f1.x + f1.y)) + ((f2.x + f2.y) + (f3.x + f3.y));
+    }
+#pragma unroll
+    for (int p = 0; p < 4; ++p) {
+      const __half2 h = __floats2half2_rn(sum[2 * p + 1], sum[2 * p]);
+      sf[p] = *reinterpret_cast<const uint32_t *>(&h);
+    }
+  } else {
+#pragma unroll
+    for (int i = 0; i < 32; ++i) bf[i] = 0u;
+#pragma unroll
+    for (int p = 0; p < 4; ++p) sf[p] = 0u;
+  }
+}
+
 template <int K0, int K1, int NST>
 __global__ void __launch_bounds__(kGemvThreads, 2) gemv_kernel(GemvArgs a) {
   extern __shared__ __align__(256) uint8_t gsm[];
-  // the table must start on a 256-byte boundary of the shared window: the
-  // decode puts the row index in address bits 8..15 with a byte permute
+  // 256-byte aligned table rows: the row index is multiplied by 256 and the
+  // lane replica offset (< 256) added in one integer multiply-add
   uint8_t *tbl = gsm + ((256u - (smem_u32(gsm) & 255u)) & 255u);
   load_table(tbl);
   __syncthreads();
@@ -132,43 +188,33 @@ __global__ void __launch_bounds__(kGemvThreads, 2) gemv_kernel(GemvArgs a) {
   const int64_t start = warp * a.items / nwarps, end = (warp + 1) * a.items / nwarps;
   if (start >= end) return;
 
-  const uint32_t tbase = smem_u32(tbl);
-  const uint32_t tbl_e8p = tbase + (lane & 15) * 8;        // byte 0 < 128: lane replica
-  const uint32_t tbl_1b = tbase + 128 + (lane & 15) * 8;   // byte 0 in [128, 256)
+  const uint32_t off_e8p = (lane & 15) * 8;        // E8P replicas: bytes [0, 128) of a row
+  const uint32_t off_1b = 128 + (lane & 15) * 8;   // 1-bit replicas: bytes [128, 256)
   const int g = lane >> 2, t = lane & 3;
   const float ls = *a.layer_scale;
+  float tokscale[2];  // layer scale x per-token x2 scale of this lane's two output tokens
+#pragma unroll
+  for (int j = 0; j < 2; ++j) tokscale[j] = 2 * t + j < a.ntok ? ls * a.rowscale[a.tok0 + 2 * t + j] : 0.f;
 
-  uint32_t bf[32];
-  int64_t kc_cur = -1;
+  uint32_t bf[32], sf[4];
+  int64_t kc = start / a.RT, rt = start % a.RT;
+  load_activations(a, kc, g, t, bf, sf);
   uint4 q[4], nq[4];
   load_item<K0, K1, NST>(a, start, lane, q);
   for (int64_t it = start; it < end; ++it) {
-    const int64_t kc = it / a.RT, rt = it % a.RT;
-    if (kc != kc_cur) {
-      kc_cur = kc;
-      if (g < a.ntok) {
-        const uint4 *src = reinterpret_cast<const uint4 *>(a.x2h + (a.tok0 + g) * a.n_pad + kc * 256 + t * 64);
-#pragma unroll
-        for (int c = 0; c < 8; ++c) {
-          const uint4 v = __ldg(src + c);
-          bf[4 * c + 0] = v.x;
-          bf[4 * c + 1] = v.y;
-          bf[4 * c + 2] = v.z;
-          bf[4 * c + 3] = v.w;
-        }
-      } else {
-#pragma unroll
-        for (int i = 0; i < 32; ++i) bf[i] = 0u;
-      }
-    }
     if (it + 1 < end) load_item<K0, K1, NST>(a, it + 1, lane, nq);
 
-    float acc0[4] = {0.f, 0.f, 0.f, 0.f};
-    float acc1[4] = {0.f, 0.f, 0.f, 0.f};
-    stage_item<K0>(tbl_e8p, tbl_1b, q[0], q[nquads<K0>() - 1], bf, acc0);
+    float acc0[4] = {0.f, 0.f, 0.f, 0.f}, acc0b[4] = {0.f, 0.f, 0.f, 0.f};
+    float acc1[4] = {0.f, 0.f, 0.f, 0.f}, acc1b[4] = {0.f, 0.f, 0.f, 0.f};
+    stage_item<K0>(tbl, off_e8p, off_1b, q[0], q[nquads<K0>() - 1], bf, sf, acc0, acc0b);
     if constexpr (NST == 2) {
       constexpr int o = nquads<K0>();
-      stage_item<K1>(tbl_e8p, tbl_1b, q[o], q[o + nquads<K1>() - 1], bf, acc1);
+      stage_item<K1>(tbl, off_e8p, off_1b, q[o], q[o + nquads<K1>() - 1], bf, sf, acc1, acc1b);
+    }
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+      acc0[i] += acc0b[i];
+      acc1[i] += acc1b[i];
     }
 
     // epilogue: c0 (row g, tok 2t), c1 (row g, tok 2t+1), c2/c3 rows g+8
@@ -178,7 +224,7 @@ __global__ void __launch_bounds__(kGemvThreads, 2) gemv_kernel(GemvArgs a) {
       const int tok = 2 * t + j;
       if (tok < a.ntok) {
         const int gt = a.tok0 + tok;
-        const float f = ls * a.rowscale[gt];
+        const float f = tokscale[j];
         float v0 = a.sscale[0] * acc0[j], v1 = a.sscale[0] * acc0[2 + j];
         if constexpr (NST == 2) {
           v0 = fmaf(a.sscale[1], acc1[j], v0);
@@ -190,6 +236,11 @@ __global__ void __launch_bounds__(kGemvThreads, 2) gemv_kernel(GemvArgs a) {
     }
 #pragma unroll
     for (int i = 0; i < 4; ++i) q[i] = nq[i];
+    if (++rt == a.RT) {
+      rt = 0;
+      ++kc;
+      if (it + 1 < end) load_activations(a, kc, g, t, bf, sf);
+    }
   }
 }
 

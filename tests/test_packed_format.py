@@ -63,29 +63,31 @@ def f16x2(word):
     return np.array([word & 0xFFFF, word >> 16], dtype=np.uint16).view(np.float16)
 
 
-def hadd2(a, b):
-    r = (f16x2(a) + f16x2(b)).astype(np.float16).view(np.uint16)
-    return int(r[0]) | int(r[1]) << 16
-
-
 def decode_quad_like_kernel(q):
-    """Mirror of stage_item<E8P> + e8p_words for one row quad -> (8, 8) floats."""
+    """Mirror of stage_item<E8P> (e8p_words + shift_words) for one row quad ->
+    (8, 8) floats: sign*|t| words from the table plus the +-1/4 shift words the
+    tensor core adds against per-code activation sums."""
     w0, w1, w2, w3 = q
     flo = (w2 ^ (w2 << 8)) & M32
     fhi = ((w3 & 0x00FFFFFF) ^ (((w3 << 8) | (w2 >> 24)) & M32)) & M32
+    # shift words: sw[p] = (code 2p+1 in the low half, code 2p in the high half)
+    y = prmt(w3, (w3 << 1) & M32, 0x3070)
+    sw = [0x34003400 ^ (((y << (2 * p)) & M32) & 0x80008000) for p in range(4)]
+    shift = np.zeros(8, np.float32)
+    for p in range(4):
+        lo, hi = f16x2(sw[p])
+        shift[2 * p + 1], shift[2 * p] = lo, hi
     out = []
     for c in range(8):
-        sw = 0x34003400 ^ (prmt((w3 << c) & M32, 0, 0xB4B4) & 0x80008000)
         idxsrc = w0 if c < 4 else w1
-        lane_off = 40  # any lane replica offset < 128
-        a = prmt(idxsrc, lane_off, 0x5504 | ((c & 3) << 4))
-        assert a == ((idxsrc >> (8 * (c & 3))) & 0xFF) * 256 + lane_off
-        T = E8P_HB[a >> 8]
+        idx = prmt(idxsrc, 0, 0x4440 | (c & 3))
+        assert idx == (idxsrc >> (8 * (c & 3))) & 0xFF
+        T = E8P_HB[idx]
         tl = T[0] ^ (((flo << c) & M32) & 0x80808080)
         th = T[1] ^ (((fhi << c) & M32) & 0x80808080)
-        words = [hadd2(prmt(tl, 0, 0x1404), sw), hadd2(prmt(tl, 0, 0x3424), sw),
-                 hadd2(prmt(th, 0, 0x1404), sw), hadd2(prmt(th, 0, 0x3424), sw)]
-        out.append(np.concatenate([f16x2(w) for w in words]).astype(np.float32))
+        words = [prmt(tl, 0, 0x1404), prmt(tl, 0, 0x3424), prmt(th, 0, 0x1404), prmt(th, 0, 0x3424)]
+        vals = np.concatenate([f16x2(w) for w in words]).astype(np.float32)
+        out.append(vals + shift[c])
     return np.stack(out)
 
 
