@@ -136,6 +136,22 @@ int qs_linear_fwd(const void *x, int x_dtype, int64_t batch, int64_t n, int64_t 
                   const void *phase_u, const void *phase_v, const float *bias, void *y,
                   void *workspace, int64_t workspace_bytes, qs_stream_t stream);
 
+/* qs_linear_fwd for callers that cannot allocate device memory (no
+ * counterpart in the reference).  Same arguments and result as qs_linear_fwd
+ * without the workspace: it uses a built-in 8 MiB device array instead, which
+ * every GPU that loads the library holds until exit, so a caller whose memory
+ * is owned by a fixed-budget allocator (a server that reserved HBM up front, a
+ * plugin host) or that must avoid cudaMalloc's implicit synchronisation needs
+ * no allocation.  Returns QS_ERR_WORKSPACE when qs_linear_workspace_bytes(batch,
+ * m, n) exceeds 8 MiB.  The first call on a device looks up the array's device
+ * address (make it before any CUDA graph capture).  Calls share the array:
+ * calls that overlap on the GPU (other streams or threads) race. */
+int qs_linear_fwd_noalloc(const void *x, int x_dtype, int64_t batch, int64_t n, int64_t m,
+                          const void *packed, int stages, const int *kinds,
+                          const float *stage_scales, const float *layer_scale, int transform,
+                          const float *su, const float *sv, const void *phase_u,
+                          const void *phase_v, const float *bias, void *y, qs_stream_t stream);
+
 /* The three steps of qs_linear_fwd, for callers that put a collective between
  * the matmul and the output transform (column-sharded tensor parallelism:
  * each rank runs qs_linear_input + qs_linear_matmul on its rows of the

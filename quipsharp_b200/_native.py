@@ -51,6 +51,8 @@ _SIGS = {
     "qs_linear_workspace_bytes": (_L, [_L, _L, _L]),
     "qs_linear_fwd": (_I, [_P, _I, _L, _L, _L, _P, _I, _P, _P, _P, _I, _P, _P, _P, _P, _P, _P,
                            _P, _L, _P]),
+    "qs_linear_fwd_noalloc": (_I, [_P, _I, _L, _L, _L, _P, _I, _P, _P, _P, _I, _P, _P, _P, _P, _P, _P,
+                                   _P]),
     "qs_linear_input_bytes": (_L, [_L, _L]),
     "qs_linear_input": (_I, [_P, _I, _L, _L, _I, _P, _P, _P, _L, _P, _L, _P]),
     "qs_linear_matmul": (_I, [_P, _L, _L, _L, _P, _I, _P, _P, _P, _P, _P]),
