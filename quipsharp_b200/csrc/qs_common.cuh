@@ -22,6 +22,34 @@ int check_launch(const char *what);
       return ::qs::fail(QS_ERR_CUDA, "%s: %s", #expr, cudaGetErrorString(_e));    \
   } while (0)
 
+// ---- programmatic dependent launch ----------------------------------------
+// The forward's kernels are launched with programmatic stream serialization:
+// a kernel may start while its predecessor on the stream is still running,
+// runs its prologue (tables, weight prefetch), and calls pdl_wait() before it
+// touches anything the predecessor writes or reads (pdl_wait returns once the
+// predecessor has completed and its writes are visible).  pdl_launch_dependents()
+// lets the successor start its own prologue early.
+__device__ __forceinline__ void pdl_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
+__device__ __forceinline__ void pdl_launch_dependents() { asm volatile("griddepcontrol.launch_dependents;" ::: "memory"); }
+
+template <typename... KArgs, typename... Args>
+inline int launch_pdl(const char *what, void (*kern)(KArgs...), dim3 grid, dim3 block, size_t smem,
+                      cudaStream_t s, Args... args) {
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = grid;
+  cfg.blockDim = block;
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = s;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  const cudaError_t e = cudaLaunchKernelEx(&cfg, kern, static_cast<KArgs>(args)...);
+  if (e != cudaSuccess) return fail(QS_ERR_CUDA, "%s launch failed: %s", what, cudaGetErrorString(e));
+  return QS_OK;
+}
+
 // ---- element load / store --------------------------------------------------
 __device__ __forceinline__ float load_as_float(const void *p, int64_t i, int dtype) {
   switch (dtype) {

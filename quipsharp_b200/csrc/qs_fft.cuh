@@ -358,11 +358,11 @@ __device__ __forceinline__ void small_stage(int R, float2 *src, float2 *dst, con
 
 // Unnormalised DFT (forward: exp(-2*pi*i*jk/N), inverse: exp(+...)) of the row
 // in buf0[cpad(.)]; returns the buffer holding the result.  Ends with a barrier.
+// The caller builds the twiddle tables (build_twiddles) before the barrier
+// that precedes this call.
 template <bool PP, int BIG>
 __device__ __forceinline__ float2 *fft_row(float2 *buf0, float2 *buf1, Twiddles &tw, const FftPlan &p,
                                            bool inverse) {
-  build_twiddles(tw, p.N);
-  __syncthreads();
   float2 *src = buf0, *dst = buf1;
   int Ns = 1;
   for (int s = 0; s < p.nst; ++s) {
@@ -397,10 +397,12 @@ __global__ void __launch_bounds__(PP ? 512 : 1024) rfft_rows_kernel(
   const int esz = dtype == QS_F32 ? 4 : 2;
   const void *xr = static_cast<const char *>(x) + row * ld_x * esz;
   void *yr = static_cast<char *>(y) + row * ld_y * esz;
+  build_twiddles(tw, N);
   batched_rows<8, float4>(N, [&](int i) {
     return make_float4(load_as_float(xr, 2 * i, dtype), load_as_float(xr, 2 * i + 1, dtype),
                        inverse ? 1.f : phase[i].x, inverse ? 0.f : phase[i].y);
   }, [&](int i, float4 v) { csm[cpad(i)] = cmul(make_float2(v.x, v.y), make_float2(v.z, v.w)); });
+  __syncthreads();
   const float2 *res = fft_row<PP, BIG>(csm, buf1, tw, plan, inverse != 0);
   batched_rows<8, float2>(N, [&](int i) { return inverse ? conjf2(phase[i]) : make_float2(1.f, 0.f); },
                           [&](int i, float2 ph) {
@@ -423,6 +425,9 @@ __global__ void __launch_bounds__(PP ? 512 : 1024) linear_input_rfft_kernel(
   float2 *buf1 = csm + fft_buf_elems(plan.N);
   const int N = plan.N;
   const int64_t row = blockIdx.x;
+  pdl_launch_dependents();
+  build_twiddles(tw, N);
+  pdl_wait();  // x may be the previous kernel's output; y1 may still be read by it
   for (int64_t i = threadIdx.x; i < m_local; i += blockDim.x) y1[row * m_local + i] = 0.f;
   if (dtype == QS_F16 || dtype == QS_BF16) {
     const uint32_t *xr = reinterpret_cast<const uint32_t *>(static_cast<const char *>(x) + row * 4 * N);
@@ -441,6 +446,7 @@ __global__ void __launch_bounds__(PP ? 512 : 1024) linear_input_rfft_kernel(
       return make_float4(z.x, z.y, ph.x, ph.y);
     }, [&](int i, float4 v) { csm[cpad(i)] = cmul(make_float2(v.x, v.y), make_float2(v.z, v.w)); });
   }
+  __syncthreads();
   const float2 *res = fft_row<PP, BIG>(csm, buf1, tw, plan, false);
   float amax = 0.f;
   for (int i = threadIdx.x; i < N; i += blockDim.x) {
@@ -471,9 +477,13 @@ __global__ void __launch_bounds__(PP ? 512 : 1024) linear_output_rfft_kernel(
   const int N = plan.N;
   const int64_t mp = 2 * N / shards;
   const int64_t row = blockIdx.x;
+  pdl_launch_dependents();
+  build_twiddles(tw, N);
+  pdl_wait();  // y1 comes from the matmul (or the all-gather)
   batched_rows<8, float2>(N, [&](int i) {
     return *reinterpret_cast<const float2 *>(y1 + y1_offset(row, 2 * i, ld_y1, shards, mp, batch));
   }, [&](int i, float2 v) { csm[cpad(i)] = v; });
+  __syncthreads();
   const float2 *res = fft_row<PP, BIG>(csm, buf1, tw, plan, true);
   batched_rows<8, float4>(N, [&](int i) {
     const float2 ph = phase[i];
@@ -525,9 +535,8 @@ int run_linear_output_rfft(const float *y1, int64_t ld_y1, int64_t shards, int64
                                      cudaStream_t s) {                                                    \
     QS_CUDA_TRY(cudaFuncSetAttribute(linear_input_rfft_kernel<PP, BIG>,                                   \
                                      cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));            \
-    linear_input_rfft_kernel<PP, BIG><<<batch, p.threads, smem, s>>>(x, dtype, p, phase, scale, x2h,      \
-                                                                     rowscale, n_pad, y1, m_local, resbuf); \
-    return check_launch("linear_input_rfft");                                                             \
+    return launch_pdl("linear_input_rfft", linear_input_rfft_kernel<PP, BIG>, dim3(batch), dim3(p.threads), \
+                      smem, s, x, dtype, p, phase, scale, x2h, rowscale, n_pad, y1, m_local, resbuf);       \
   }                                                                                                       \
   template <>                                                                                             \
   int run_linear_output_rfft<PP, BIG>(const float *y1, int64_t ld_y1, int64_t shards, int64_t batch,      \
@@ -535,9 +544,8 @@ int run_linear_output_rfft(const float *y1, int64_t ld_y1, int64_t shards, int64
                                       float scale, void *y, int dtype, size_t smem, cudaStream_t s) {     \
     QS_CUDA_TRY(cudaFuncSetAttribute(linear_output_rfft_kernel<PP, BIG>,                                  \
                                      cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));            \
-    linear_output_rfft_kernel<PP, BIG><<<batch, p.threads, smem, s>>>(y1, ld_y1, shards, batch, p, phase, \
-                                                                      bias, scale, y, dtype);             \
-    return check_launch("linear_output_rfft");                                                            \
+    return launch_pdl("linear_output_rfft", linear_output_rfft_kernel<PP, BIG>, dim3(batch),                \
+                      dim3(p.threads), smem, s, y1, ld_y1, shards, batch, p, phase, bias, scale, y, dtype); \
   }
 
 }  // namespace qs

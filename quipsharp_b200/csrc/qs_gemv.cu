@@ -35,11 +35,17 @@ struct GemvArgs {
   int tok0, ntok;
 };
 
+// Fill the replicated table: thread i < 256 owns table row i, reads its E8P
+// and 1-bit entries once and writes the 16 replicas of each.
 __device__ __forceinline__ void load_table(uint8_t *tbl) {
-  for (int k = threadIdx.x; k < 256 * 32; k += blockDim.x) {
-    const int row = k >> 5, slot = k & 31;
-    const uint2 v = slot < 16 ? kE8pHiBytes[row] : kE81BitHiBytes[row];
-    *reinterpret_cast<uint2 *>(tbl + row * 256 + slot * 8) = v;
+  for (int row = threadIdx.x; row < 256; row += blockDim.x) {
+    const uint2 e = kE8pHiBytes[row], o = kE81BitHiBytes[row];
+    uint2 *dst = reinterpret_cast<uint2 *>(tbl + row * 256);
+#pragma unroll
+    for (int r = 0; r < 16; ++r) {
+      dst[(r + row) & 15] = e;          // rotate the write order to spread banks
+      dst[16 + ((r + row) & 15)] = o;
+    }
   }
 }
 
@@ -176,17 +182,21 @@ __device__ __forceinline__ void load_activations(const GemvArgs &a, int64_t kc, 
 template <int K0, int K1, int NST>
 __global__ void __launch_bounds__(kGemvThreads, 2) gemv_kernel(GemvArgs a) {
   extern __shared__ __align__(256) uint8_t gsm[];
+  pdl_launch_dependents();
   // 256-byte aligned table rows: the row index is multiplied by 256 and the
   // lane replica offset (< 256) added in one integer multiply-add
   uint8_t *tbl = gsm + ((256u - (smem_u32(gsm) & 255u)) & 255u);
-  load_table(tbl);
-  __syncthreads();
-
   const int lane = threadIdx.x & 31;
   const int64_t warp = blockIdx.x * (kGemvThreads / 32) + (threadIdx.x >> 5);
   const int64_t nwarps = static_cast<int64_t>(gridDim.x) * (kGemvThreads / 32);
   const int64_t start = warp * a.items / nwarps, end = (warp + 1) * a.items / nwarps;
+  // prologue, independent of the previous kernel: first weights in flight, table fill
+  uint4 q[4], nq[4];
+  if (start < end) load_item<K0, K1, NST>(a, start, lane, q);
+  load_table(tbl);
+  __syncthreads();
   if (start >= end) return;
+  pdl_wait();  // x2h, rowscale and the zeroed y1 come from the input-transform kernel
 
   const uint32_t off_e8p = (lane & 15) * 8;        // E8P replicas: bytes [0, 128) of a row
   const uint32_t off_1b = 128 + (lane & 15) * 8;   // 1-bit replicas: bytes [128, 256)
@@ -199,8 +209,6 @@ __global__ void __launch_bounds__(kGemvThreads, 2) gemv_kernel(GemvArgs a) {
   uint32_t bf[32], sf[4];
   int64_t kc = start / a.RT, rt = start % a.RT;
   load_activations(a, kc, g, t, bf, sf);
-  uint4 q[4], nq[4];
-  load_item<K0, K1, NST>(a, start, lane, q);
   for (int64_t it = start; it < end; ++it) {
     if (it + 1 < end) load_item<K0, K1, NST>(a, it + 1, lane, nq);
 
@@ -266,8 +274,7 @@ static int run_gemv(GemvArgs &a, int64_t batch, cudaStream_t s) {
   for (int64_t tok0 = 0; tok0 < batch; tok0 += 8) {
     a.tok0 = static_cast<int>(tok0);
     a.ntok = static_cast<int>(batch - tok0 < 8 ? batch - tok0 : 8);
-    kern<<<grid, kGemvThreads, kTblBytes + 256, s>>>(a);
-    int st = check_launch("gemv");
+    int st = launch_pdl("gemv", kern, dim3(grid), dim3(kGemvThreads), kTblBytes + 256, s, a);
     if (st) return st;
   }
   return QS_OK;

@@ -223,6 +223,8 @@ __global__ void __launch_bounds__(1024) linear_input_rht_kernel(
     float *rowscale, int n_pad, float *y1, int64_t m_local) {
   extern __shared__ float fsm[];
   __shared__ float red[32];
+  pdl_launch_dependents();
+  pdl_wait();  // x may be the previous kernel's output; y1 may still be read by it
   const int n = 1 << L;
   const int64_t row = blockIdx.x;
   for (int64_t i = threadIdx.x; i < m_local; i += blockDim.x) y1[row * m_local + i] = 0.f;
@@ -257,10 +259,9 @@ int launch_linear_input(const void *x, int x_dtype, int64_t batch, int64_t n, in
   if (transform == QS_RHT) {
     FwhtGeom g = fwht_geom(n);
     if ((st = set_smem(linear_input_rht_kernel, g.smem))) return st;
-    linear_input_rht_kernel<<<batch, g.threads, g.smem, s>>>(x, x_dtype, g.L, g.E, sv,
-                                                            inv_sqrt_f32(n), x2h, rowscale,
-                                                            static_cast<int>(n_pad), y1, m_local);
-    return check_launch("linear_input_rht");
+    return launch_pdl("linear_input_rht", linear_input_rht_kernel, dim3(batch), dim3(g.threads), g.smem, s,
+                      x, x_dtype, g.L, g.E, sv, inv_sqrt_f32(n), x2h, rowscale, static_cast<int>(n_pad), y1,
+                      m_local);
   }
   FftPlan p;
   if ((st = make_plan(n / 2, p))) return st;
@@ -285,6 +286,8 @@ __global__ void __launch_bounds__(1024) linear_output_rht_kernel(const float *y1
                                                                  const float *bias, float scale,
                                                                  void *y, int dtype) {
   extern __shared__ float fsm[];
+  pdl_launch_dependents();
+  pdl_wait();  // y1 comes from the matmul kernel
   const int m = 1 << L;
   const int64_t mp = m / shards;
   const int64_t row = blockIdx.x;
@@ -304,9 +307,8 @@ int launch_linear_output(const float *y1, int64_t ld_y1, int64_t shards, int64_t
   if (transform == QS_RHT) {
     FwhtGeom g = fwht_geom(m);
     if ((st = set_smem(linear_output_rht_kernel, g.smem))) return st;
-    linear_output_rht_kernel<<<batch, g.threads, g.smem, s>>>(y1, ld_y1, shards, batch, g.L, g.E, su,
-                                                             bias, inv_sqrt_f32(m), y, y_dtype);
-    return check_launch("linear_output_rht");
+    return launch_pdl("linear_output_rht", linear_output_rht_kernel, dim3(batch), dim3(g.threads), g.smem, s,
+                      y1, ld_y1, shards, batch, g.L, g.E, su, bias, inv_sqrt_f32(m), y, y_dtype);
   }
   if (ld_y1 % 2) return fail(QS_ERR_ALIGNMENT, "RFFT y1 row stride must be even");
   FftPlan p;
