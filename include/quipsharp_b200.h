@@ -38,7 +38,8 @@ typedef enum qs_status {
   QS_ERR_UNSUPPORTED = 5, /* size beyond what the kernels handle                  */
   QS_ERR_ALIGNMENT = 6,   /* pointer not aligned as the kernel requires           */
   QS_ERR_CUDA = 7,        /* a CUDA runtime call or launch failed                 */
-  QS_ERR_WORKSPACE = 8    /* workspace missing or smaller than *_bytes() asked for */
+  QS_ERR_WORKSPACE = 8,   /* workspace missing or smaller than *_bytes() asked for */
+  QS_ERR_TIMEOUT = 9      /* a kernel gave up a bounded pipeline wait (see qs_device_status) */
 } qs_status;
 
 /* Codebook kinds (one per RVQ stage). */
@@ -57,6 +58,13 @@ typedef enum qs_transform { QS_RHT = 0, QS_RFFT = 1 } qs_transform;
 
 const char *qs_version(void);
 const char *qs_last_error(void);
+
+/* Synchronises the stream and reports whether any kernel of this library gave
+ * up a bounded wait inside its pipeline since the last call (QS_ERR_TIMEOUT;
+ * the results of that launch are invalid).  The kernels never spin without a
+ * limit: a stalled pipeline ends the kernel with this flag set instead of
+ * hanging the GPU.  No counterpart in the reference (pure Python). */
+int qs_device_status(qs_stream_t stream);
 
 /* Host-only.  Writes the 256x8 float32 table of `kind` (row-major) to host
  * memory: E8P = build_abs_table() (quipsharp/codebooks/e8p.py:84-89),
@@ -157,6 +165,8 @@ int qs_linear_fwd_noalloc(const void *x, int x_dtype, int64_t batch, int64_t n, 
  * each rank runs qs_linear_input + qs_linear_matmul on its rows of the
  * weight, the y1 shards are all-gathered, then every rank runs
  * qs_linear_output on the full y1).
+ * Batches above 16 tokens run the prefill matmul (fused decode + tcgen05
+ * tensor-core GEMM); smaller ones the decode-regime kernel.
  *  - qs_linear_input: x -> x2 (fp16 tiles + per-row scale in workspace) and
  *    zeroes y1 (batch, m_local) float32.
  *  - qs_linear_matmul: y1 += x2 @ What_local^T * scales (rows m_local).

@@ -23,6 +23,7 @@ QS_ERR_UNSUPPORTED = 5
 QS_ERR_ALIGNMENT = 6
 QS_ERR_CUDA = 7
 QS_ERR_WORKSPACE = 8
+QS_ERR_TIMEOUT = 9
 
 QS_CB_E8P = 0
 QS_CB_E8_1BIT = 1
@@ -40,6 +41,7 @@ _L = ctypes.c_int64
 _SIGS = {
     "qs_version": (ctypes.c_char_p, []),
     "qs_last_error": (ctypes.c_char_p, []),
+    "qs_device_status": (_I, [_P]),
     "qs_codebook_table": (_I, [_I, _P]),
     "qs_decode": (_I, [_I, _P, _I, _L, _P, _P]),
     "qs_rvq_decode": (_I, [_I, _P, _P, _I, _P, _L, _P, _P]),

@@ -56,6 +56,8 @@ QS_API const char *qs_version(void) { return "quipsharp_b200 0.1 (sm_100a)"; }
 
 QS_API const char *qs_last_error(void) { return g_last_error; }
 
+QS_API int qs_device_status(qs_stream_t stream) { return device_status((cudaStream_t)stream); }
+
 QS_API int qs_codebook_table(int kind, float *out_host) {
   if (!out_host) return fail(QS_ERR_INVALID_ARG, "null output");
   if (kind == QS_CB_E8P) memcpy(out_host, kE8pAbsF32Host, sizeof(kE8pAbsF32Host));
@@ -244,7 +246,9 @@ QS_API int qs_linear_fwd(const void *x, int x_dtype, int64_t batch, int64_t n, i
   const int64_t x2b = ws_align(linear_input_bytes(batch, n));
   float *y1 = reinterpret_cast<float *>(static_cast<char *>(workspace) + x2b);
   cudaStream_t s = (cudaStream_t)stream;
-  st = launch_linear_input(x, x_dtype, batch, n, transform, sv, phase_v, workspace, y1, m, s);
+  // the prefill matmul writes every y1 element; only the decode-regime kernel accumulates
+  const bool tc = batch >= kTcMinBatch;
+  st = launch_linear_input(x, x_dtype, batch, n, transform, sv, phase_v, workspace, tc ? nullptr : y1, m, s);
   if (st) return st;
   st = launch_matmul(workspace, batch, n, m, packed, stages, kinds, stage_scales, layer_scale, y1, s);
   if (st) return st;

@@ -1,0 +1,385 @@
+// Fused codebook decode + tcgen05 GEMM for prefill-sized batches:
+//   y1[tok, row] = layer_scale * rowscale[tok] * sum_s s_s * sum_k x2h[tok, k] * What_s[row, k]
+//
+// CTA tile: 128 weight rows (M, TMEM lanes) x 256 tokens (N, TMEM columns),
+// K in steps of 64 input features (one 128-byte swizzled row per operand row).
+// Warp roles (192 threads):
+//   warp 0      TMA producer: the activation tile (256 tokens x 64 fp16) of each
+//               K step into a 4- (3-) stage ring, 128-byte swizzle;
+//   warp 1      allocates TMEM; lane 0 issues tcgen05.mma (M=128, N=256, K=16,
+//               fp16 x fp16 -> fp32) and tcgen05.commit to free ring stages;
+//   warps 2..5  decode: thread r decodes weight row r of the tile for each K step
+//               (8 codes, read from the same packed stream as the decode-regime
+//               kernel) into the A tile of the ring stage, in the UMMA
+//               K-major 128-byte-swizzle layout; then the epilogue: TMEM ->
+//               registers -> scales -> y1 (float32, coalesced per token).
+// Decoded weights are exact in fp16 (the E8P shift is added with an f16x2 add),
+// RVQ stages accumulate in separate TMEM accumulators and meet their float32
+// stage scales in the epilogue.  Every mbarrier wait is bounded: on timeout the
+// kernel records an error (read by qs_device_status) and winds down.
+#include <cuda.h>
+
+#include <mutex>
+
+#include "qs_common.cuh"
+#include "qs_launch.h"
+#include "qs_sm100.cuh"
+
+namespace qs {
+
+static __device__ int g_tc_error;  // set by a bounded wait that ran out
+
+namespace {
+
+constexpr int kBM = 128;
+constexpr int kBN = 256;
+constexpr int kBK = 64;
+constexpr int kThreads = 192;
+constexpr int kATile = kBM * kBK * 2;  // 16 KB
+constexpr int kBTile = kBN * kBK * 2;  // 32 KB
+constexpr uint64_t kWaitLimitNs = 4000000000ull;  // 4 s: far beyond any legitimate wait
+
+template <int NST>
+struct Cfg {
+  static constexpr int stages = NST == 1 ? 4 : 3;
+  static constexpr int stage_bytes = NST * kATile + kBTile;
+  static constexpr int ring_bytes = stages * stage_bytes;
+  static constexpr int tables_bytes = 2 * 256 * 8;
+  static constexpr int bar_bytes = 256;
+  static constexpr int smem_bytes = 1024 /*align slack*/ + ring_bytes + tables_bytes + bar_bytes;
+  static constexpr uint32_t tmem_cols = NST * kBN;
+};
+
+struct TcArgs {
+  const uint8_t *stage[2];
+  float sscale[2];
+  const float *layer_scale;
+  const float *rowscale;
+  float *y1;
+  int64_t m, m_pad, RT, batch;
+  int ksteps;
+};
+
+__device__ __forceinline__ void set_error() { atomicExch(&g_tc_error, 1); }
+
+// E8P: 8 codes of one row (a packed quad) -> 8 x 16-byte chunks of fp16
+// weights (shift included), written to the row's swizzled positions.
+__device__ __forceinline__ void decode_e8p_row(const uint4 &q, const uint2 *tbl, uint8_t *arow, int rsw) {
+  const uint32_t flo = q.z ^ (q.z << 8);
+  const uint32_t fhi = (q.w & 0x00FFFFFFu) ^ shf_l_wrap(q.z, q.w, 8);
+#pragma unroll
+  for (int c = 0; c < 8; ++c) {
+    const uint32_t src = c < 4 ? q.x : q.y;
+    const uint32_t idx = (src >> (8 * (c & 3))) & 0xFFu;
+    const uint2 T = tbl[idx];
+    const uint32_t tl = T.x ^ ((flo << c) & 0x80808080u);
+    const uint32_t th = T.y ^ ((fhi << c) & 0x80808080u);
+    const uint32_t sw = 0x34003400u ^ (prmt(q.w << c, 0u, 0xB4B4u) & 0x80008000u);
+    uint4 w;
+    w.x = hadd2_u32(prmt(tl, 0u, 0x1404u), sw);
+    w.y = hadd2_u32(prmt(tl, 0u, 0x3424u), sw);
+    w.z = hadd2_u32(prmt(th, 0u, 0x1404u), sw);
+    w.w = hadd2_u32(prmt(th, 0u, 0x3424u), sw);
+    *reinterpret_cast<uint4 *>(arow + ((c ^ rsw) << 4)) = w;
+  }
+}
+
+// 1-bit: 8 index bytes of one row -> 8 chunks.
+__device__ __forceinline__ void decode_1bit_row(const uint2 &q, const uint2 *tbl, uint8_t *arow, int rsw) {
+#pragma unroll
+  for (int c = 0; c < 8; ++c) {
+    const uint32_t src = c < 4 ? q.x : q.y;
+    const uint2 T = tbl[(src >> (8 * (c & 3))) & 0xFFu];
+    uint4 w;
+    w.x = prmt(T.x, 0u, 0x1404u);
+    w.y = prmt(T.x, 0u, 0x3424u);
+    w.z = prmt(T.y, 0u, 0x1404u);
+    w.w = prmt(T.y, 0u, 0x3424u);
+    *reinterpret_cast<uint4 *>(arow + ((c ^ rsw) << 4)) = w;
+  }
+}
+
+// Per-row codes of one 32-code chunk (4 K steps) of a stage: a 16-byte quad per
+// K step for E8P, 8 index bytes per K step for 1-bit.
+template <int K>
+struct RowChunk;
+template <>
+struct RowChunk<QS_CB_E8P> {
+  uint4 q[4];
+};
+template <>
+struct RowChunk<QS_CB_E8_1BIT> {
+  uint2 q[4];
+};
+
+template <int K>
+__device__ __forceinline__ void load_row_chunk(const uint8_t *stage, int64_t RT, int64_t kc, int64_t R,
+                                               bool valid, RowChunk<K> &rc) {
+  const int64_t rtg = R >> 4, rr = R & 15, half = rr >> 3, g = rr & 7;
+  if constexpr (K == QS_CB_E8P) {
+    const uint8_t *p = stage + (kc * RT + rtg) * 1024 + half * 512 + g * 64;
+#pragma unroll
+    for (int t = 0; t < 4; ++t) rc.q[t] = valid ? ldg_nc_v4(p + 16 * t) : make_uint4(0u, 0u, 0u, 0u);
+  } else {
+    const uint8_t *p = stage + (kc * RT + rtg) * 512 + g * 64 + half * 8;
+#pragma unroll
+    for (int t = 0; t < 4; ++t)
+      rc.q[t] = valid ? __ldg(reinterpret_cast<const uint2 *>(p + 16 * t)) : make_uint2(0u, 0u);
+  }
+}
+
+template <int K>
+__device__ __forceinline__ void decode_row(const RowChunk<K> &rc, int t, const uint2 *tbl_e8p,
+                                           const uint2 *tbl_1b, uint8_t *arow, int rsw) {
+  if constexpr (K == QS_CB_E8P) decode_e8p_row(rc.q[t], tbl_e8p, arow, rsw);
+  else decode_1bit_row(rc.q[t], tbl_1b, arow, rsw);
+}
+
+template <int K0, int K1, int NST>
+__global__ void __launch_bounds__(kThreads, 1) gemm_tc_kernel(const __grid_constant__ CUtensorMap tmap_x,
+                                                               TcArgs a) {
+  using C = Cfg<NST>;
+  constexpr int S = C::stages;
+  extern __shared__ __align__(1024) uint8_t dsm[];
+  pdl_launch_dependents();
+  // 1024-byte aligned ring (the swizzle atom); tables and barriers after it.
+  uint8_t *base = dsm + ((1024u - (smem_u32(dsm) & 1023u)) & 1023u);
+  uint8_t *ring = base;
+  uint2 *tbl_e8p = reinterpret_cast<uint2 *>(base + C::ring_bytes);
+  uint2 *tbl_1b = tbl_e8p + 256;
+  uint64_t *bars = reinterpret_cast<uint64_t *>(base + C::ring_bytes + C::tables_bytes);
+  // bars: full_a[S], full_b[S], empty[S], acc_full, then the TMEM address holder
+  const uint32_t bar0 = smem_u32(bars);
+  auto full_a = [&](int s) { return bar0 + 8u * s; };
+  auto full_b = [&](int s) { return bar0 + 8u * (S + s); };
+  auto empty = [&](int s) { return bar0 + 8u * (2 * S + s); };
+  const uint32_t acc_full = bar0 + 8u * (3 * S);
+  uint32_t *tmem_holder = reinterpret_cast<uint32_t *>(bars + 3 * S + 1);
+
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int64_t m0 = static_cast<int64_t>(blockIdx.x) * kBM;
+  const int n0 = blockIdx.y * kBN;
+
+  // ---- setup (independent of the previous kernel)
+  for (int i = threadIdx.x; i < 256; i += blockDim.x) {
+    tbl_e8p[i] = kE8pHiBytes[i];
+    tbl_1b[i] = kE81BitHiBytes[i];
+  }
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < S; ++s) {
+      sm100::mbar_init(full_a(s), 128);
+      sm100::mbar_init(full_b(s), 1);
+      sm100::mbar_init(empty(s), 1);
+    }
+    sm100::mbar_init(acc_full, 1);
+    sm100::fence_barrier_init();
+    sm100::prefetch_tmap(&tmap_x);
+  }
+  if (warp == 1) sm100::tmem_alloc(smem_u32(tmem_holder), C::tmem_cols);
+  sm100::tc_fence_before_sync();
+  __syncthreads();
+  sm100::tc_fence_after_sync();
+  const uint32_t tmem = *tmem_holder;
+  pdl_wait();  // x2h / rowscale come from the input-transform kernel
+
+  const int K = a.ksteps;
+  if (warp == 0) {
+    // ---- TMA producer
+    if (lane == 0) {
+      int issued = 0;
+      for (int ks = 0; ks < K; ++ks) {
+        const int s = ks % S, use = ks / S;
+        if (use > 0 && !sm100::mbar_wait_bounded(empty(s), (use - 1) & 1, kWaitLimitNs)) {
+          set_error();
+          break;
+        }
+        uint8_t *bt = ring + s * C::stage_bytes + NST * kATile;
+        sm100::mbar_arrive_expect_tx(full_b(s), kBTile);
+        sm100::tma_load_2d(smem_u32(bt), &tmap_x, ks * kBK, n0, full_b(s));
+        issued = ks + 1;
+      }
+      // wind down: every load this thread issued must have landed before the CTA exits
+      for (int ks = issued > S ? issued - S : 0; ks < issued; ++ks)
+        if (!sm100::mbar_wait_bounded(full_b(ks % S), (ks / S) & 1, kWaitLimitNs)) set_error();
+    }
+  } else if (warp == 1) {
+    // ---- MMA issuer
+    if (lane == 0) {
+      constexpr uint32_t idesc = sm100::idesc_f16_f32(kBM, kBN);
+      bool ok = true;
+      for (int ks = 0; ks < K && ok; ++ks) {
+        const int s = ks % S, use = ks / S;
+        ok = sm100::mbar_wait_bounded(full_a(s), use & 1, kWaitLimitNs) &&
+             sm100::mbar_wait_bounded(full_b(s), use & 1, kWaitLimitNs);
+        if (!ok) {
+          set_error();
+          break;
+        }
+        sm100::tc_fence_after_sync();
+        uint8_t *st = ring + s * C::stage_bytes;
+        const uint64_t bdesc = sm100::sw128_kmajor_desc(smem_u32(st + NST * kATile));
+#pragma unroll
+        for (int j = 0; j < NST; ++j) {
+          const uint64_t adesc = sm100::sw128_kmajor_desc(smem_u32(st + j * kATile));
+#pragma unroll
+          for (int k = 0; k < kBK / 16; ++k)  // +32 bytes per K=16 slice inside the swizzled row
+            sm100::umma_f16(tmem + j * kBN, adesc + 2 * k, bdesc + 2 * k, idesc, (ks | k) != 0);
+        }
+        sm100::umma_commit(empty(s));
+      }
+      sm100::umma_commit(acc_full);
+    }
+  } else {
+    // ---- decode producers (128 threads, thread r <-> tile row r)
+    const int r = threadIdx.x - 64;
+    const int64_t R = m0 + r;
+    const bool valid = R < a.m_pad;
+    const int rsw = r & 7;
+    RowChunk<K0> c0, n0c;
+    RowChunk<K1> c1, n1c;
+    load_row_chunk<K0>(a.stage[0], a.RT, 0, R, valid, c0);
+    if constexpr (NST == 2) load_row_chunk<K1>(a.stage[1], a.RT, 0, R, valid, c1);
+    const int rowoff = (r >> 3) * 1024 + (r & 7) * 128;
+    bool ok = true;
+    for (int kc = 0; kc < K / 4 && ok; ++kc) {  // one 32-code chunk = 4 K steps
+      if (kc + 1 < K / 4) {  // prefetch the next chunk's codes
+        load_row_chunk<K0>(a.stage[0], a.RT, kc + 1, R, valid, n0c);
+        if constexpr (NST == 2) load_row_chunk<K1>(a.stage[1], a.RT, kc + 1, R, valid, n1c);
+      }
+#pragma unroll
+      for (int t = 0; t < 4; ++t) {
+        const int ks = kc * 4 + t, s = ks % S, use = ks / S;
+        if (use > 0 && !sm100::mbar_wait_bounded(empty(s), (use - 1) & 1, kWaitLimitNs)) {
+          set_error();
+          ok = false;
+          break;
+        }
+        uint8_t *st = ring + s * C::stage_bytes;
+        decode_row<K0>(c0, t, tbl_e8p, tbl_1b, st + rowoff, rsw);
+        if constexpr (NST == 2) decode_row<K1>(c1, t, tbl_e8p, tbl_1b, st + kATile + rowoff, rsw);
+        sm100::fence_proxy_async_smem();
+        sm100::mbar_arrive(full_a(s));
+      }
+      c0 = n0c;
+      if constexpr (NST == 2) c1 = n1c;
+    }
+    // ---- epilogue
+    if (ok && sm100::mbar_wait_bounded(acc_full, 0, kWaitLimitNs)) {
+      sm100::tc_fence_after_sync();
+      const int quarter = warp & 3;
+      const int64_t row = m0 + quarter * 32 + lane;
+      const uint32_t lane_addr = tmem + (static_cast<uint32_t>(quarter * 32) << 16);
+      const float ls = *a.layer_scale;
+      for (int c = 0; c < kBN; c += 16) {
+        uint32_t v0[16], v1[16];
+        sm100::tmem_ld_16(lane_addr + c, v0);
+        if constexpr (NST == 2) sm100::tmem_ld_16(lane_addr + kBN + c, v1);
+        sm100::tmem_ld_wait();
+#pragma unroll
+        for (int j = 0; j < 16; ++j) {
+          const int64_t tok = n0 + c + j;
+          if (tok < a.batch && row < a.m) {
+            float v = a.sscale[0] * __uint_as_float(v0[j]);
+            if constexpr (NST == 2) v = fmaf(a.sscale[1], __uint_as_float(v1[j]), v);
+            a.y1[tok * a.m + row] = v * ls * a.rowscale[tok];
+          }
+        }
+      }
+    } else if (ok) {
+      set_error();
+    }
+  }
+  // ---- teardown
+  sm100::tc_fence_before_sync();
+  __syncthreads();
+  if (warp == 1) {
+    sm100::tc_fence_after_sync();
+    sm100::tmem_dealloc(tmem, C::tmem_cols);
+  }
+}
+
+// ---- tensor map for the fp16 activation tiles ----------------------------
+using EncodeTiledFn = CUresult (*)(CUtensorMap *, CUtensorMapDataType, cuuint32_t, void *, const cuuint64_t *,
+                                   const cuuint64_t *, const cuuint32_t *, const cuuint32_t *, CUtensorMapInterleave,
+                                   CUtensorMapSwizzle, CUtensorMapL2promotion, CUtensorMapFloatOOBfill);
+
+int encode_x_map(CUtensorMap *map, const void *x2h, int64_t n_pad, int64_t batch) {
+  static EncodeTiledFn fn = nullptr;
+  static std::mutex mu;
+  {
+    std::lock_guard<std::mutex> lock(mu);
+    if (!fn) {
+      void *p = nullptr;
+      cudaDriverEntryPointQueryResult q;
+      QS_CUDA_TRY(cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &p, cudaEnableDefault, &q));
+      if (!p || q != cudaDriverEntryPointSuccess) return fail(QS_ERR_CUDA, "cuTensorMapEncodeTiled unavailable");
+      fn = reinterpret_cast<EncodeTiledFn>(p);
+    }
+  }
+  const cuuint64_t dims[2] = {static_cast<cuuint64_t>(n_pad), static_cast<cuuint64_t>(batch)};
+  const cuuint64_t strides[1] = {static_cast<cuuint64_t>(n_pad * 2)};
+  const cuuint32_t box[2] = {kBK, kBN};
+  const cuuint32_t estr[2] = {1, 1};
+  CUresult r = fn(map, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2, const_cast<void *>(x2h), dims, strides, box, estr,
+                  CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                  CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  if (r != CUDA_SUCCESS) return fail(QS_ERR_CUDA, "cuTensorMapEncodeTiled failed (%d)", static_cast<int>(r));
+  return QS_OK;
+}
+
+template <int K0, int K1, int NST>
+int run_gemm(const CUtensorMap &map, const TcArgs &a, cudaStream_t s) {
+  using C = Cfg<NST>;
+  auto kern = gemm_tc_kernel<K0, K1, NST>;
+  QS_CUDA_TRY(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, C::smem_bytes));
+  const dim3 grid(static_cast<unsigned>(ceil_div(a.m, kBM)), static_cast<unsigned>(ceil_div(a.batch, kBN)));
+  return launch_pdl("gemm_tc", kern, grid, dim3(kThreads), C::smem_bytes, s, map, a);
+}
+
+}  // namespace
+
+int launch_matmul_tc(const void *x2ws, int64_t batch, int64_t n, int64_t m, const void *packed, int stages,
+                     const int *kinds, const float *stage_scales, const float *layer_scale, float *y1,
+                     cudaStream_t s) {
+  const int64_t n_pad = padded_T(n) * 8;
+  TcArgs a{};
+  a.rowscale = reinterpret_cast<const float *>(static_cast<const char *>(x2ws) + round_up(batch * n_pad * 2, 256));
+  a.layer_scale = layer_scale;
+  a.y1 = y1;
+  a.m = m;
+  a.m_pad = padded_m(m);
+  a.RT = padded_m(m) / kRowsPerTile;
+  a.batch = batch;
+  a.ksteps = static_cast<int>(n_pad / kBK);
+  const uint8_t *p = static_cast<const uint8_t *>(packed);
+  for (int st = 0; st < stages; ++st) {
+    a.stage[st] = p;
+    a.sscale[st] = stage_scales ? stage_scales[st] : 1.f;
+    p += round_up(stage_bytes(kinds[st], m, n), 256);
+  }
+  CUtensorMap map;
+  int st = encode_x_map(&map, x2ws, n_pad, batch);
+  if (st) return st;
+  const int k0 = kinds[0], k1 = stages == 2 ? kinds[1] : 0;
+  if (stages == 1)
+    return k0 == QS_CB_E8P ? run_gemm<QS_CB_E8P, 0, 1>(map, a, s) : run_gemm<QS_CB_E8_1BIT, 0, 1>(map, a, s);
+  if (k0 == QS_CB_E8P && k1 == QS_CB_E8_1BIT) return run_gemm<QS_CB_E8P, QS_CB_E8_1BIT, 2>(map, a, s);
+  if (k0 == QS_CB_E8P && k1 == QS_CB_E8P) return run_gemm<QS_CB_E8P, QS_CB_E8P, 2>(map, a, s);
+  if (k0 == QS_CB_E8_1BIT && k1 == QS_CB_E8P) return run_gemm<QS_CB_E8_1BIT, QS_CB_E8P, 2>(map, a, s);
+  return run_gemm<QS_CB_E8_1BIT, QS_CB_E8_1BIT, 2>(map, a, s);
+}
+
+int device_status(cudaStream_t s) {
+  int flag = 0;
+  static const int zero = 0;
+  QS_CUDA_TRY(cudaMemcpyFromSymbolAsync(&flag, g_tc_error, sizeof(int), 0, cudaMemcpyDeviceToHost, s));
+  QS_CUDA_TRY(cudaStreamSynchronize(s));
+  if (flag) {
+    QS_CUDA_TRY(cudaMemcpyToSymbolAsync(g_tc_error, &zero, sizeof(int), 0, cudaMemcpyHostToDevice, s));
+    QS_CUDA_TRY(cudaStreamSynchronize(s));
+    return fail(QS_ERR_TIMEOUT, "a pipeline wait in the prefill matmul timed out; its results are invalid");
+  }
+  return QS_OK;
+}
+
+}  // namespace qs

@@ -283,6 +283,8 @@ static int run_gemv(GemvArgs &a, int64_t batch, cudaStream_t s) {
 int launch_matmul(const void *x2ws, int64_t batch, int64_t n, int64_t m, const void *packed,
                   int stages, const int *kinds, const float *stage_scales,
                   const float *layer_scale, float *y1, cudaStream_t s) {
+  if (batch >= kTcMinBatch)
+    return launch_matmul_tc(x2ws, batch, n, m, packed, stages, kinds, stage_scales, layer_scale, y1, s);
   GemvArgs a{};
   a.n_pad = padded_T(n) * 8;
   a.x2h = static_cast<const __half *>(x2ws);

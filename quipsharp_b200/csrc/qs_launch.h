@@ -38,4 +38,11 @@ int launch_matmul(const void *x2ws, int64_t batch, int64_t n, int64_t m, const v
                   int stages, const int *kinds, const float *stage_scales,
                   const float *layer_scale, float *y1, cudaStream_t s);
 
+// qs_gemm_tc.cu
+int launch_matmul_tc(const void *x2ws, int64_t batch, int64_t n, int64_t m, const void *packed, int stages,
+                     const int *kinds, const float *stage_scales, const float *layer_scale, float *y1,
+                     cudaStream_t s);
+int device_status(cudaStream_t s);
+constexpr int64_t kTcMinBatch = 17;  // batches of at least this many tokens use the tcgen05 GEMM
+
 }  // namespace qs
