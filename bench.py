@@ -117,11 +117,10 @@ class ClockSampler:
 
 
 def config_spec(name):
+    """(layers [(name, m, n)], kinds, dtype) of a BASELINE configuration."""
     from quipsharp_b200 import synthetic as syn
     spec = syn.CONFIGS[name]
-    assert len(spec["layers"]) == 1, "bench workload is a single-layer-shape config"
-    _, m, n = spec["layers"][0]
-    return m, n, spec["kinds"], spec["dtype"]
+    return spec["layers"], spec["kinds"], spec["dtype"]
 
 
 def algorithmic_bytes(m, n, kinds, batch, elem=2):
@@ -170,15 +169,18 @@ def run_reference(args):
     world, rank, local = dist_env()
     if rank != 0:
         return
-    m, n, kinds, dtype = config_spec(args.config)
-    run = cpu_oracle_forward(m, n, kinds, args.batch, dtype)
+    layers, kinds, dtype = config_spec(args.config)
+    runs = [cpu_oracle_forward(m, n, kinds, args.batch, dtype) for _, m, n in layers]
     for _ in range(args.warmup):
-        run()
+        for run in runs:
+            run()
     per_step = []
     for _ in range(args.steps):
         t0 = time.perf_counter()
-        run()
+        for run in runs:
+            run()
         per_step.append(time.perf_counter() - t0)
+    m, n = layers[0][1], layers[0][2]
     total = sum(per_step)
     value = args.batch * len(per_step) / total
     cores = os.cpu_count()
@@ -187,11 +189,11 @@ def run_reference(args):
         "value": value, "unit": "tokens/s", "n_gpus": args.gpus, "steps": args.steps, "warmup": args.warmup,
         "ms_per_step": 1000 * total / len(per_step), "higher_is_better": True, "scaling": "weak",
         "vs_baseline": None, "dtype": "f32", "data": "synthetic",
-        "config": {"workload": args.config, "batch": args.batch, "m": m, "n": n, "kinds": list(kinds),
-                   "step": "one full forward of one layer on the host CPU"},
+        "config": {"workload": args.config, "batch": args.batch, "layers": [list(l) for l in layers],
+                   "kinds": list(kinds), "step": "one full forward of every layer of the set on the host CPU"},
         "cpu_baseline": {"value": value, "unit": "tokens/s", "cores": cores, "kind": "port",
-                         "sample": f"{len(per_step)} full forwards (numpy port of the reference algorithm, "
-                                   f"oracle/quipsharp_oracle.py), BLAS threads = all {cores} host cores"},
+                         "sample": f"{len(per_step)} passes over the layer set (numpy port of the reference "
+                                   f"algorithm, oracle/quipsharp_oracle.py), BLAS threads = all {cores} host cores"},
         "e2e": {"value": value, "unit": "tokens/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
     }
     print(json.dumps(line), flush=True)
@@ -213,68 +215,81 @@ def run_ours(args):
         dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120))
     torch.cuda.set_device(local)
     dev = torch.device("cuda", local)
-    m, n, kinds, dtype = config_spec(args.config)
+    layers, kinds, dtype = config_spec(args.config)
     B = args.batch
-
-    # ---- L distinct layer copies whose packed weights exceed 2x L2
-    base = syn.make_layer(m, n, kinds, seed=1)
+    prefill = B >= 17
+    chained = len(layers) > 1
     karr = N.int_array([N.QS_CB_E8P if k == "e8p" else N.QS_CB_E8_1BIT for k in kinds])
-    packed_bytes = N.lib().qs_packed_bytes(len(kinds), karr, m, n)
-    L = max(2, math.ceil(2 * L2_BYTES / packed_bytes))
+    set_bytes = sum(N.lib().qs_packed_bytes(len(kinds), karr, m, n) for _, m, n in layers)
+    # decode regime: cycle distinct copies of the layer set so weights always come from HBM
+    L = 1 if prefill else max(1, math.ceil(2 * L2_BYTES / set_bytes))
     cb = lambda k: E8PCodebook() if k == "e8p" else E8OneBitCodebook()
-    codebook = cb(kinds[0]) if len(kinds) == 1 else RVQCodebookAdapter(
-        [RVQStage(cb(k), s) for k, s in zip(kinds, base.stage_scales)])
-    codes0 = base.codes.to(dev)
-    mods = []
-    for l in range(L):
-        mod = QuantizedLinear(n, m, 8, base.transform_kind, num_stages=len(kinds)).to(dev)
-        with torch.no_grad():
-            c = codes0.clone()
-            if c.dim() == 2:
-                c ^= (l * 0x9E37 + rank * 0x3B1) & 0x7FFF
-            else:
-                c[0] ^= (l * 0x9E37 + rank * 0x3B1) & 0x7FFF
-                c[1] ^= (l * 37 + rank) & 0xFF if kinds[1] == "e8_1bit" else (l * 0x9E37) & 0x7FFF
-            mod.codes.copy_(c)
-            mod.scale.fill_(base.layer_scale)
-            if base.transform_kind == "rht":
-                mod.su.copy_(base.su)
-                mod.sv.copy_(base.sv)
-            else:
-                mod.phase_u.copy_(base.phase_u)
-                mod.phase_v.copy_(base.phase_v)
-        mod.codebook = codebook
-        mod.kernel()  # pack once, outside every timed region
-        mods.append(mod)
-    del codes0
-    kern = [md.kernel() for md in mods]
-    S = args.stack
-    R = max(1, S // L)
-    S = R * L
-    stream = torch.cuda.Stream(dev)
-    x_host = syn.make_activations(B, n, dtype=dtype, seed=2).pin_memory()
-    x_dev = torch.empty(B, n, dtype=dtype, device=dev)
-    x_dev.copy_(x_host)
-    y_dev = torch.empty(L, B, m, dtype=dtype, device=dev)
-    y_host = torch.empty(L, B, m, dtype=dtype).pin_memory()
 
-    # ---- direct C-ABI pass (value): input -> matmul -> output per layer
-    ws_in_b = N.lib().qs_linear_input_bytes(B, n)
-    ws_in = torch.empty(ws_in_b, dtype=torch.uint8, device=dev)
-    y1 = torch.empty(B, m, dtype=torch.float32, device=dev)
-    kc = [(k, k._kinds_c, k._ss_c) for k in kern]
+    mods = []  # [copy][layer]
+    for l in range(L):
+        row = []
+        for li, (name, m, n) in enumerate(layers):
+            base = syn.make_layer(m, n, kinds, seed=1 + li,
+                                  layer_scale=(1.0 / math.sqrt(1.2 * n)) if chained else None)
+            mod = QuantizedLinear(n, m, 8, base.transform_kind, num_stages=len(kinds)).to(dev)
+            with torch.no_grad():
+                c = base.codes.to(dev)
+                if c.dim() == 2:
+                    c ^= (l * 0x9E37 + rank * 0x3B1) & 0x7FFF
+                else:
+                    c[0] ^= (l * 0x9E37 + rank * 0x3B1) & 0x7FFF
+                    c[1] ^= (l * 37 + rank) & 0xFF if kinds[1] == "e8_1bit" else (l * 0x9E37) & 0x7FFF
+                mod.codes.copy_(c)
+                mod.scale.fill_(base.layer_scale)
+                if base.transform_kind == "rht":
+                    mod.su.copy_(base.su)
+                    mod.sv.copy_(base.sv)
+                else:
+                    mod.phase_u.copy_(base.phase_u)
+                    mod.phase_v.copy_(base.phase_v)
+            mod.codebook = cb(kinds[0]) if len(kinds) == 1 else RVQCodebookAdapter(
+                [RVQStage(cb(k), sc) for k, sc in zip(kinds, base.stage_scales)])
+            mod.kernel()  # pack once, outside every timed region
+            row.append(mod)
+        mods.append(row)
+    # layers per step: whole passes over the copies, at least --stack layer forwards
+    R = max(1, math.ceil(args.stack / (L * len(layers)))) if not prefill else max(1, args.stack // 8192)
+    passes = R * L
+    n_in = layers[0][2]
+    stream = torch.cuda.Stream(dev)
+    x_host = syn.make_activations(B, n_in, dtype=dtype, seed=2).pin_memory()
+    x_dev = torch.empty(B, n_in, dtype=dtype, device=dev)
+    x_dev.copy_(x_host)
     io = N.IO_DTYPES[dtype]
 
-    def one_pass(s, matmul_only=False):
-        for k, kinds_c, ss_c in kc:
+    # ---- buffers of the direct C-ABI pass (value): chain each layer's input by dimension
+    max_in = max(n for _, _, n in layers)
+    max_out = max(m for _, m, _ in layers)
+    ws_in_b = max(N.lib().qs_linear_input_bytes(B, n) for _, _, n in layers)
+    ws_in = torch.empty(ws_in_b, dtype=torch.uint8, device=dev)
+    y1 = torch.empty(B * max_out, dtype=torch.float32, device=dev)
+    outs = {}
+    plan = []  # (kernel, input tensor, output tensor)
+    for li, (name, m, n) in enumerate(layers):
+        src = x_dev if n == n_in and li == 0 else outs.get(n, x_dev if n == n_in else None)
+        if src is None:
+            src = syn.make_activations(B, n, dtype=dtype, seed=10 + li).to(dev)
+        out = torch.empty(B, m, dtype=dtype, device=dev)
+        outs[m] = out
+        plan.append((li, src, out, m, n))
+    result = plan[-1][2]
+
+    def one_pass(copy, s, matmul_only=False):
+        for li, src, out, m, n in plan:
+            k = mods[copy][li].kernel()
             if not matmul_only:
-                N.check(N.lib().qs_linear_input(N.ptr(x_dev), io, B, n, k.transform, N.ptr(k.sv), N.ptr(k.phase_v),
-                                                N.ptr(ws_in), ws_in_b, N.ptr(y1), m, s))
-            N.check(N.lib().qs_linear_matmul(N.ptr(ws_in), B, n, m, N.ptr(k.packed), len(k.kinds), kinds_c, ss_c,
-                                             N.ptr(k.scale), N.ptr(y1), s))
+                N.check(N.lib().qs_linear_input(N.ptr(src), io, B, n, k.transform, N.ptr(k.sv), N.ptr(k.phase_v),
+                                                N.ptr(ws_in), ws_in_b, None if prefill else N.ptr(y1), m, s))
+            N.check(N.lib().qs_linear_matmul(N.ptr(ws_in), B, n, m, N.ptr(k.packed), len(k.kinds), k._kinds_c,
+                                             k._ss_c, N.ptr(k.scale), N.ptr(y1), s))
             if not matmul_only:
-                N.check(N.lib().qs_linear_output(N.ptr(y1), m, 1, B, m, k.transform, N.ptr(k.su), N.ptr(k.phase_u),
-                                                 N.ptr(k.bias), N.ptr(y_dev[0]), io, s))
+                N.check(N.lib().qs_linear_output(N.ptr(y1), m, 1, B, m, k.transform, N.ptr(k.su),
+                                                 N.ptr(k.phase_u), N.ptr(k.bias), N.ptr(out), io, s))
 
     def capture(fn):
         g = torch.cuda.CUDAGraph()
@@ -286,8 +301,8 @@ def run_ours(args):
         torch.cuda.synchronize(dev)
         return g
 
-    g_pass = capture(lambda s: one_pass(s))
-    g_mm = capture(lambda s: one_pass(s, matmul_only=True))
+    g_pass = capture(lambda s: [one_pass(c, s) for c in range(L)])
+    g_mm = capture(lambda s: [one_pass(c, s, matmul_only=True) for c in range(L)])
 
     def barrier():
         if world > 1:
@@ -316,87 +331,121 @@ def run_ours(args):
             for _ in range(R):
                 g_pass.replay()
 
-    # ---- value: device-resident inputs, graph of L layers x R passes per step
+    # ---- value: device-resident inputs
     with ClockSampler(local) as clk:
         ms_total = timed(step_value, args.steps, args.warmup)
     ms_step = ms_total / args.steps
-    tokens = B * S * args.steps * world
+    tokens = B * passes * args.steps * world
     value = tokens / (ms_total / 1e3)
+    flops_set = sum(2.0 * B * m * n for _, m, n in layers)
 
-    # ---- dominant kernel: fused decode+matmul, timed alone on the same stream
+    # ---- dominant kernel, timed alone on the same stream
     def step_mm():
         with torch.cuda.stream(stream):
             for _ in range(R):
                 g_mm.replay()
     mm_steps = max(3, args.steps // 2)
     ms_mm = timed(step_mm, mm_steps, 2)
-    mm_launches = mm_steps * R * L * math.ceil(B / 8)
-    us_per_mm = 1e3 * ms_mm / (mm_steps * R * L)
-    hbm_peak, _, peak_kind = measured_peaks()
-    gb = gemv_bytes(m, n, kinds, B)
-    achieved = gb / (us_per_mm * 1e-6) / 1e9
-    traffic = None
-    tfile = os.path.join(ROOT, "profiles", f"traffic_{args.config}_b{B}.json")
-    if os.path.exists(tfile):
-        with open(tfile) as f:
-            traffic = json.load(f).get("dram_bytes_per_launch")
+    launches_mm = mm_steps * R * L * len(layers)
+    us_per_mm = 1e3 * ms_mm / launches_mm
+    hbm_peak, tc_peak, peak_kind = measured_peaks()
+    if prefill:
+        achieved = flops_set * mm_steps * R * L / (ms_mm / 1e3) / 1e12
+        try:
+            with open(os.path.join(ROOT, "MEASURED_PEAKS.json")) as f:
+                tc_sust = float(json.load(f)["bf16_tflops_sustained"])
+        except Exception:
+            tc_sust = 1400.0
+        roofline = {"bound": "tensor", "achieved": achieved, "peak": tc_sust, "unit": "TFLOP/s",
+                    "frac": achieved / tc_sust, "traffic": None,
+                    "kernel": "qs::gemm_tc_kernel (fused decode + tcgen05 GEMM, 128x256 tiles)",
+                    "algorithmic_flops_per_layer_set": flops_set, "us_per_launch": us_per_mm,
+                    "peak_source": f"{peak_kind} (MEASURED_PEAKS.json bf16_tflops_sustained; burst {tc_peak})"}
+    else:
+        gb = sum(gemv_bytes(m, n, kinds, B) for _, m, n in layers)
+        achieved = gb * mm_steps * R * L / (ms_mm / 1e3) / 1e9
+        traffic = None
+        tfile = os.path.join(ROOT, "profiles", f"traffic_{args.config}_b{B}.json")
+        if os.path.exists(tfile):
+            with open(tfile) as f:
+                traffic = json.load(f).get("dram_bytes_per_launch")
+        roofline = {"bound": "hbm", "achieved": achieved, "peak": hbm_peak, "unit": "GB/s",
+                    "frac": achieved / hbm_peak, "traffic": traffic,
+                    "kernel": "qs::gemv_kernel (fused decode + mma.sync matmul)",
+                    "algorithmic_bytes_per_layer_set": gb, "us_per_launch": us_per_mm,
+                    "peak_source": f"{peak_kind} (MEASURED_PEAKS.json hbm_gbs)"}
 
-    # ---- e2e: public module API, pinned host input in / all outputs back per step
+    # ---- e2e: public module API; pinned host input in, the chain's result out, every step
     def fwd_all(s):
-        for l, md in enumerate(mods):
-            y_dev[l].copy_(md(x_dev))
+        o = None
+        for c in range(L):
+            cur = {n_in: x_dev}
+            for li, (name, m, n) in enumerate(layers):
+                inp = cur.get(n)
+                if inp is None:
+                    inp = plan[li][1]
+                cur[m] = mods[c][li](inp)
+            o = cur[layers[-1][1]]
+        return o
 
     g_api = torch.cuda.CUDAGraph()
     with torch.cuda.stream(stream):
         fwd_all(None)
         torch.cuda.synchronize(dev)
         with torch.cuda.graph(g_api, stream=stream):
-            fwd_all(None)
+            api_out = fwd_all(None)
     torch.cuda.synchronize(dev)
+    y_host = torch.empty(api_out.shape, dtype=api_out.dtype).pin_memory()
 
     def step_e2e():
         with torch.cuda.stream(stream):
             x_dev.copy_(x_host, non_blocking=True)
             for _ in range(R):
                 g_api.replay()
-            y_host.copy_(y_dev, non_blocking=True)
+            y_host.copy_(api_out, non_blocking=True)
     ms_e2e = timed(step_e2e, args.steps, args.warmup)
     e2e_value = tokens / (ms_e2e / 1e3)
 
     cpu = None
-    if rank == 0 and world == 1:
-        t, cnt = cpu_oracle_forward_time(m, n, kinds, B, dtype, budget_s=args.cpu_sample_s)
-        cpu = {"value": B / t, "unit": "tokens/s", "cores": os.cpu_count(), "kind": "port",
-               "sample": f"{cnt} full forwards of one {m}x{n} layer, batch {B} (numpy port of the reference "
-                         f"algorithm, oracle/quipsharp_oracle.py), median time {t:.3f} s"}
+    if rank == 0 and world == 1 and args.cpu_sample_s > 0:
+        t_set, cnt = 0.0, 0
+        budget = args.cpu_sample_s / len(layers)
+        for _, m, n in layers:
+            t, c_ = cpu_oracle_forward_time(m, n, kinds, B, dtype, budget_s=budget)
+            t_set += t
+            cnt += c_
+        cpu = {"value": B / t_set, "unit": "tokens/s", "cores": os.cpu_count(), "kind": "port",
+               "sample": f"{cnt} full layer forwards over the {len(layers)}-layer set, batch {B} (numpy port of the "
+                         f"reference algorithm, oracle/quipsharp_oracle.py); median per layer summed = {t_set:.3f} s"}
 
     if rank == 0:
         c = clk.summary()
         bits = sum(2 if k == "e8p" else 1 for k in kinds)
+        metric = (f"quantized-linear prefill tokens/s ({args.config}, batch {B})" if prefill
+                  else f"quantized-linear tokens/s ({args.config}, batch {B})")
         line = {
-            "metric": f"quantized-linear tokens/s ({args.config}, batch {B})",
-            "value": value, "unit": "tokens/s", "n_gpus": world, "steps": args.steps, "warmup": args.warmup,
-            "ms_per_step": ms_step, "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
-            "dtype": "f16", "data": "synthetic",
-            "config": {"workload": args.config, "batch": B, "m": m, "n": n, "kinds": list(kinds),
-                       "transform": base.transform_kind, "layers_per_step": S, "distinct_layer_copies": L,
-                       "weight_bytes_cycled": L * packed_bytes,
-                       "l2": f"inputs larger than L2: {L} distinct layer copies = {L * packed_bytes / 1e6:.0f} MB "
-                             f"of packed weights cycled per pass (L2 126 MB)",
+            "metric": metric, "value": value, "unit": "tokens/s", "n_gpus": world, "steps": args.steps,
+            "warmup": args.warmup, "ms_per_step": ms_step, "higher_is_better": True, "scaling": "weak",
+            "vs_baseline": None, "dtype": "f16" if dtype == torch.float16 else "bf16", "data": "synthetic",
+            "config": {"workload": args.config, "batch": B, "layers": [list(l) for l in layers], "kinds": list(kinds),
+                       "layer_set_passes_per_step": passes, "distinct_copies": L,
+                       "weight_bytes_per_copy": set_bytes,
+                       "l2": (f"inputs larger than L2: {L} distinct copies = {L * set_bytes / 1e6:.0f} MB of packed "
+                              f"weights cycled per pass (L2 126 MB)") if not prefill else
+                             "inputs larger than L2: per-layer y1 / activations of the batch exceed 126 MB",
                        "bits_per_weight": bits},
-            "hbm_gbs_per_layer_forward": algorithmic_bytes(m, n, kinds, B) * S * args.steps / (ms_total / 1e3) / 1e9,
-            "us_per_layer_forward": 1e3 * ms_step / S,
-            "roofline": {"bound": "hbm", "achieved": achieved, "peak": hbm_peak, "unit": "GB/s",
-                         "frac": achieved / hbm_peak, "traffic": traffic,
-                         "kernel": "qs::gemv_kernel (fused decode + mma.sync matmul)",
-                         "algorithmic_bytes_per_launch": gb, "us_per_launch": us_per_mm,
-                         "peak_source": f"{peak_kind} (MEASURED_PEAKS.json hbm_gbs)"},
+            "us_per_layer_set": 1e3 * ms_step / passes,
+            "hbm_gbs_per_forward": sum(algorithmic_bytes(m, n, kinds, B) for _, m, n in layers) * passes * args.steps
+                                   / (ms_total / 1e3) / 1e9,
+            "tflops": flops_set * passes * args.steps / (ms_total / 1e3) / 1e12,
+            "roofline": roofline,
             "cpu_baseline": cpu,
-            "e2e": {"value": e2e_value, "unit": "tokens/s", "h2d_bytes_per_step": B * n * 2,
-                    "d2h_bytes_per_step": L * B * m * 2,
-                    "path": "QuantizedLinear.forward (public module) x layers per step, replayed as a CUDA graph; "
-                            "pinned host input copied in and all layer outputs copied out each step"},
-            "gpu_launches": args.steps * R * L * (2 + math.ceil(B / 8)),
+            "e2e": {"value": e2e_value, "unit": "tokens/s", "h2d_bytes_per_step": B * n_in * x_host.element_size(),
+                    "d2h_bytes_per_step": y_host.numel() * y_host.element_size(),
+                    "path": "QuantizedLinear.forward (public module) over the layer set x passes per step, replayed "
+                            "as a CUDA graph; pinned host input copied in and the last layer's output copied out "
+                            "each step"},
+            "gpu_launches": args.steps * R * L * sum(2 + (1 if prefill else math.ceil(B / 8)) for _ in layers),
             "clocks": {"sm_mhz": c["sm_mhz"], "sm_max_mhz": c["sm_max_mhz"], "reasons": c["reasons"]},
         }
         print(json.dumps(line), flush=True)
