@@ -108,7 +108,8 @@ QS_API int qs_fwht(const void *x, int64_t ld_x, void *y, int64_t ld_y, int dtype
   if (!valid_io_dtype(dtype)) return fail(QS_ERR_INVALID_ARG, "bad dtype %d", dtype);
   if (n <= 0 || (n & (n - 1)))
     return fail(QS_ERR_NOT_POW2, "fwht requires a power-of-two size along dim, got %lld", (long long)n);
-  if (n > 32768) return fail(QS_ERR_UNSUPPORTED, "fwht size %lld exceeds 32768", (long long)n);
+  int st = check_fwht_size(n);
+  if (st) return st;
   if (rows < 0 || ld_x < n || ld_y < n) return fail(QS_ERR_INVALID_ARG, "bad rows/strides");
   if (rows == 0) return QS_OK;
   if (!x || !y) return fail(QS_ERR_INVALID_ARG, "null pointer");
@@ -164,7 +165,9 @@ static int check_transform_args(int transform, int64_t m, int64_t n, const float
   if (transform == QS_RHT) {
     if (n <= 0 || (n & (n - 1)) || m <= 0 || (m & (m - 1)))
       return fail(QS_ERR_NOT_POW2, "RHT needs power-of-two dims, got (%lld, %lld)", (long long)m, (long long)n);
-    if (n > 32768 || m > 32768) return fail(QS_ERR_UNSUPPORTED, "RHT dims above 32768");
+    int st = check_fwht_size(n);
+    if (st) return st;
+    if ((st = check_fwht_size(m))) return st;
     if (!su || !sv) return fail(QS_ERR_INVALID_ARG, "RHT needs su and sv");
   } else if (transform == QS_RFFT) {
     if (n % 2 || m % 2) return fail(QS_ERR_ODD_DIM, "RFFT needs even dims, got (%lld, %lld)", (long long)m, (long long)n);

@@ -28,6 +28,7 @@ int launch_linear_output(const float *y1, int64_t ld_y1, int64_t shards, int64_t
                          int transform, const float *su, const void *phase_u, const float *bias,
                          void *y, int y_dtype, cudaStream_t s);
 int check_fft_size(int64_t n_complex);
+int check_fwht_size(int64_t n);
 
 // qs_pack.cu
 int launch_pack(const int16_t *codes, int stages, const int *kinds, int64_t m, int64_t n,

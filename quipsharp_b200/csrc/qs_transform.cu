@@ -1,204 +1,223 @@
-// Incoherence transforms on rows held in shared memory:
-//   * FWHT (quipsharp/hadamard.py:17-40) for the randomized Hadamard transform
-//     (quipsharp/incoherence.py:86-93);
-//   * mixed-radix Stockham FFT for the RFFT transform (quipsharp/rfft.py:37-60).
-// One CTA owns one row; the whole row lives in shared memory, so every pass
-// runs at shared-memory speed and the row is read and written in HBM once.
-// The "linear" kernels fuse the transforms with the producer/consumer steps of
-// the quantized-linear forward: input cast + sign/phase + transform + fp16
-// packing for the matmul (with a per-row power-of-two scale) + zeroing of the
-// y1 accumulator; and y1 -> transform -> sign/conj-phase -> bias -> cast.
+// Host side of the incoherence transforms: plans (stage radices, cluster
+// size, threads, shared memory) and dispatch of the qs_xform.cuh kernels for
+//   * the standalone FWHT (quipsharp/hadamard.py:17-40) and RFFT transform
+//     (quipsharp/rfft.py:37-60) entry points;
+//   * the input / output steps of the quantized-linear forward
+//     (quipsharp/incoherence.py:86-115, quipsharp/rfft.py:62-100): input cast +
+//     sign / phase + transform + fp16 packing for the matmul (per-row power-of-two
+//     scale) + zeroing of the y1 accumulator; and y1 -> transform -> sign /
+//     conjugate phase -> bias -> cast.
+#include <algorithm>
 #include <cmath>
 
-#include "qs_fft.cuh"
+#include "qs_xform.cuh"
 
 namespace qs {
 
-// ============================================================================
-// FWHT
-// ============================================================================
-constexpr int kFwhtMaxE = 32;  // elements per thread per pass (upper bound)
+// Largest dynamic shared memory a plan may ask for (two row buffers); the
+// kernels' static shared memory (twiddle tables, reductions) is below 4 KB.
+constexpr size_t kXSmemCap = 220 * 1024;
 
-__device__ __forceinline__ int fpad(int i) { return i + (i >> 5); }
-
-template <typename Load, typename Store>
-__device__ __forceinline__ void fwht_pass(Load load, Store store, int n, int lo, int w) {
-  const int G = 1 << w;
-  const int groups = n >> w;
-  for (int gi = threadIdx.x; gi < groups; gi += blockDim.x) {
-    const int base = (gi & ((1 << lo) - 1)) | ((gi >> lo) << (lo + w));
-    float v[kFwhtMaxE];
-#pragma unroll
-    for (int j = 0; j < kFwhtMaxE; ++j)
-      if (j < G) v[j] = load(base + (j << lo));
-#pragma unroll
-    for (int h = 1; h < kFwhtMaxE; h <<= 1) {
-      if (h < G) {
-#pragma unroll
-        for (int j = 0; j < kFwhtMaxE; ++j) {
-          if (j < G && !(j & h)) {
-            const float a = v[j], b = v[j + h];
-            v[j] = a + b;
-            v[j + h] = a - b;
-          }
-        }
-      }
-    }
-#pragma unroll
-    for (int j = 0; j < kFwhtMaxE; ++j)
-      if (j < G) store(base + (j << lo), v[j]);
-  }
-}
-
-// Unnormalised Walsh-Hadamard transform of the row gload(i), i < 2^L, handed
-// to gstore(i, v).  Index bits are processed in passes of log2(E) bits; in a
-// pass each thread owns groups of E elements that differ only in those bits
-// and transforms them in registers.  The first pass reads global memory, the
-// last writes through gstore; passes in between use buf[fpad(.)].
-template <typename GLoad, typename GStore>
-__device__ __forceinline__ void fwht_row(GLoad gload, GStore gstore, float *buf, int L, int E) {
-  const int n = 1 << L;
-  const int e = 31 - __clz(E);
-  auto sload = [&](int i) { return buf[fpad(i)]; };
-  auto sstore = [&](int i, float v) { buf[fpad(i)] = v; };
-  if (L <= e) {  // one pass (also n == 1)
-    fwht_pass(gload, gstore, n, 0, L);
-    return;
-  }
-  fwht_pass(gload, sstore, n, 0, e);
-  __syncthreads();
-  int lo = e;
-  for (; lo + e < L; lo += e) {
-    fwht_pass(sload, sstore, n, lo, e);
-    __syncthreads();
-  }
-  fwht_pass(sload, gstore, n, lo, L - lo);
-}
-
-struct FwhtGeom {
-  int L, E, threads;
-  size_t smem;
-};
-
-static FwhtGeom fwht_geom(int64_t n) {
-  FwhtGeom g;
-  g.L = 0;
-  while ((int64_t(1) << g.L) < n) ++g.L;
-  int threads = static_cast<int>(std::min<int64_t>(1024, std::max<int64_t>(32, n / 16)));
-  g.threads = threads;
-  // 16 (or 32 for the largest rows) elements per group; tiny rows use one group.
-  g.E = static_cast<int>(std::min<int64_t>(n, std::max<int64_t>(16, std::min<int64_t>(kFwhtMaxE, n / threads))));
-  g.smem = static_cast<size_t>(n + (n >> 5) + 1) * sizeof(float);
-  return g;
-}
-
-__global__ void __launch_bounds__(1024) fwht_rows_kernel(const void *x, int64_t ld_x, void *y,
-                                                         int64_t ld_y, int dtype, int L, int E,
-                                                         const float *pre, const float *post,
-                                                         float scale) {
-  extern __shared__ float fsm[];
-  const int64_t row = blockIdx.x;
-  const void *xr = static_cast<const char *>(x) + row * ld_x * (dtype == QS_F32 ? 4 : 2);
-  void *yr = static_cast<char *>(y) + row * ld_y * (dtype == QS_F32 ? 4 : 2);
-  auto gload = [&](int i) {
-    float v = load_as_float(xr, i, dtype);
-    return pre ? v * pre[i] : v;
-  };
-  auto gstore = [&](int i, float v) {
-    v *= scale;
-    if (post) v *= post[i];
-    store_from_float(yr, i, dtype, v);
-  };
-  fwht_row(gload, gstore, fsm, L, E);
-}
-
-template <typename K>
-static int set_smem(K kern, size_t bytes) {
-  QS_CUDA_TRY(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                   static_cast<int>(bytes)));
-  return QS_OK;
+static int xnum_sms() {
+  static int cached[64] = {0};
+  int dev = 0;
+  cudaGetDevice(&dev);
+  if (dev < 64 && cached[dev]) return cached[dev];
+  int n = 148;
+  cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, dev);
+  if (dev < 64) cached[dev] = n;
+  return n;
 }
 
 static float inv_sqrt_f32(int64_t n) { return static_cast<float>(1.0 / std::sqrt(static_cast<double>(n))); }
 
-int launch_fwht(const void *x, int64_t ld_x, void *y, int64_t ld_y, int dtype, int64_t rows,
-                int64_t n, const float *pre, const float *post, cudaStream_t s) {
-  FwhtGeom g = fwht_geom(n);
-  QS_CUDA_TRY(cudaFuncSetAttribute(fwht_rows_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                   static_cast<int>(g.smem)));
-  fwht_rows_kernel<<<rows, g.threads, g.smem, s>>>(x, ld_x, y, ld_y, dtype, g.L, g.E, pre, post,
-                                                  inv_sqrt_f32(n));
-  return check_launch("fwht");
+static size_t plan_smem(int N, int C, int elem_bytes) {
+  const int E = N / C;
+  return 2 * static_cast<size_t>(elem_bytes) *
+         static_cast<size_t>(elem_bytes == 8 ? xbuf_elems<float2>(E) : xbuf_elems<float>(E));
 }
 
-// ============================================================================
-// FFT plans and dispatch (kernels: qs_fft.cuh, instantiated in qs_fft_*.cu)
-// ============================================================================
-static int make_plan(int64_t N, FftPlan &p) {
-  if (N < 1 || N > kFftMaxN) return fail(QS_ERR_UNSUPPORTED, "FFT length %lld outside [1, %d]", (long long)N, kFftMaxN);
-  p.N = static_cast<int>(N);
-  p.nst = 0;
-  int64_t rem = N;
-  int big = 0;
+// Points per CTA above which a few-row transform is spread over a cluster:
+// one CTA is fastest while its share stays small (a cluster costs barriers
+// and leaves each SM a single warp or two).
+constexpr int kXLatencyPointsFft = 2048;
+constexpr int kXLatencyPointsFwht = 4096;
+
+// CTAs per row wanted before the stages are known: the fewest whose share of
+// the two row buffers fits kXSmemCap; then, while the rows alone leave SMs
+// idle, doubled until each CTA's share is at most `latency_points` (<= 16).
+static int wanted_cluster(int N, int elem_bytes, int64_t rows, int latency_points) {
+  int C = 1;
+  while (plan_smem(N, C, elem_bytes) > kXSmemCap && C < kXMaxCluster) C *= 2;
+  const int64_t sms = xnum_sms();
+  while (C < kXMaxCluster && rows * 2 * C <= sms && N / C > latency_points) C *= 2;
+  return C;
+}
+
+// Fixes C (at most `want`, a power of two dividing every stage's butterfly
+// count, so each butterfly's inputs sit in one CTA), then the per-CTA task
+// counts and the launch shape.
+static int finish_plan(XPlan &p, XLaunch &L, int elem_bytes, int64_t rows, int want) {
+  int C = want;
+  for (bool ok = false; !ok && C > 1;) {
+    ok = true;
+    for (int s = 0; s < p.nst; ++s) ok = ok && (p.st[s].nb % C == 0);
+    if (!ok) C /= 2;
+  }
+  if (plan_smem(p.N, C, elem_bytes) > kXSmemCap)
+    return fail(QS_ERR_UNSUPPORTED, "transform of %d points does not fit the shared memory of %d CTAs", p.N, C);
+  p.C = C;
+  p.cl = 0;
+  while ((1 << p.cl) < C) ++p.cl;
+  p.E = p.N / C;
+  int most = 128;
+  for (int s = 0; s < p.nst; ++s) {
+    XStage &S = p.st[s];
+    // odd radices: one output pair per task in cluster (compact) kernels,
+    // groups of up to six pairs in one-CTA kernels
+    if ((S.R & 1) && S.R > 1) S.G = C > 1 ? (S.R - 1) / 2 : xodd_groups(S.R);
+    S.nbC = S.nb / C;
+    S.dnbC = make_fastdiv(static_cast<uint32_t>(S.nbC));
+    most = std::max(most, S.nbC * S.G);
+  }
+  L.threads = std::min(kXMaxThreads, (most + 31) / 32 * 32);
+  L.smem = plan_smem(p.N, C, elem_bytes);
+  L.rows = rows;
+  return QS_OK;
+}
+
+// Complex FFT of N points: the prime >= 11 (at most one, once), 7 / 5 / 3, then
+// the power-of-two part in balanced stages (radices up to 16 for one CTA per
+// row, up to 8 across a cluster); a copy stage follows an odd last radix (the
+// last stage writes the sink).
+static int make_fft_plan(int64_t N64, int64_t rows, XPlan &p, XLaunch &L) {
+  if (N64 < 1 || N64 > kXMaxN)
+    return fail(QS_ERR_UNSUPPORTED, "FFT length %lld outside [1, %d]", (long long)N64, kXMaxN);
+  const int N = static_cast<int>(N64);
+  int rem = N, big = 0, nr = 0;
+  int radix[kXMaxStages];
   for (int P : {43, 41, 37, 31, 29, 23, 19, 17, 13, 11}) {
-    while (rem % P == 0) {
-      if (big) return fail(QS_ERR_UNSUPPORTED, "FFT length %lld has two prime factors >= 11", (long long)N);
+    if (rem % P == 0) {
+      if (big || (rem / P) % P == 0)
+        return fail(QS_ERR_UNSUPPORTED, "FFT length %lld has more than one prime factor >= 11", (long long)N);
       big = P;
       rem /= P;
     }
   }
-  p.big = big;
-  if (big) p.radix[p.nst++] = big;
+  if (big) radix[nr++] = big;
   for (int P : {7, 5, 3}) {
     while (rem % P == 0) {
-      p.radix[p.nst++] = P;
+      if (nr >= kXMaxStages - 1) return fail(QS_ERR_UNSUPPORTED, "FFT plan too deep");
+      radix[nr++] = P;
       rem /= P;
     }
   }
-  for (int P : {16, 8, 4, 2}) {
-    while (rem % P == 0) {
-      p.radix[p.nst++] = P;
-      rem /= P;
-    }
+  int a = 0;
+  while (rem % 2 == 0) {
+    rem /= 2;
+    ++a;
   }
-  if (rem != 1)
-    return fail(QS_ERR_UNSUPPORTED, "FFT length %lld has a prime factor above 43", (long long)N);
-  if (p.nst == 0) p.radix[p.nst++] = 1;  // N == 1
-  if (p.nst > kMaxStages) return fail(QS_ERR_UNSUPPORTED, "FFT plan too deep");
-  p.pingpong = N <= kFftPingPongMax;
-  if (p.pingpong) {
-    int threads = 64;
-    while (threads < 512 && threads * 8 < N) threads *= 2;
-    p.threads = threads;
+  if (rem != 1) return fail(QS_ERR_UNSUPPORTED, "FFT length %lld has a prime factor above 43", (long long)N);
+  const int want = wanted_cluster(N, 8, rows, kXLatencyPointsFft);
+  if (a > 0) {
+    const int maxlog = want > 1 ? 3 : 4;
+    const int ns = (a + maxlog - 1) / maxlog, base = a / ns, extra = a % ns;
+    if (nr + ns >= kXMaxStages) return fail(QS_ERR_UNSUPPORTED, "FFT plan too deep");
+    for (int i = 0; i < ns; ++i) radix[nr++] = 1 << (base + (i < extra ? 1 : 0));
+  }
+  if (nr == 0) radix[nr++] = 1;              // N == 1
+  if (radix[nr - 1] & 1 && radix[nr - 1] > 1) radix[nr++] = 1;
+  p.N = N;
+  p.nst = nr;
+  p.big = big;
+  int Ns = 1;
+  for (int s = 0; s < nr; ++s) {
+    XStage &S = p.st[s];
+    S.R = radix[s];
+    S.G = 1;
+    S.Ns = Ns;
+    S.nb = N / S.R;
+    S.twstep = N / (Ns * S.R);
+    S.dNs = make_fastdiv(static_cast<uint32_t>(Ns));
+    Ns *= S.R;
+  }
+  return finish_plan(p, L, 8, rows, want);
+}
+
+// FWHT of n = 2^Lb points: balanced passes of the rotating form, up to 5 bits
+// each for one CTA per row, up to 3 across a cluster.
+static int make_fwht_plan(int64_t n, int64_t rows, XPlan &p, XLaunch &L) {
+  if (n < 1 || (n & (n - 1)))
+    return fail(QS_ERR_NOT_POW2, "fwht requires a power-of-two size along dim, got %lld", (long long)n);
+  if (n > kXMaxN) return fail(QS_ERR_UNSUPPORTED, "fwht size %lld exceeds %d", (long long)n, kXMaxN);
+  int Lb = 0;
+  while ((int64_t(1) << Lb) < n) ++Lb;
+  const int want = wanted_cluster(static_cast<int>(n), 4, rows, kXLatencyPointsFwht);
+  int widths[kXMaxStages], np = 0;
+  if (Lb == 0) {
+    widths[np++] = 0;
   } else {
-    if (big) return fail(QS_ERR_UNSUPPORTED, "FFT length %lld: prime factors >= 11 need N <= %d", (long long)N, kFftPingPongMax);
-    p.threads = 1024;  // N / 1024 <= kFftIpE values per thread
+    const int maxw = want > 1 ? 3 : 5;
+    const int ns = (Lb + maxw - 1) / maxw, base = Lb / ns, extra = Lb % ns;
+    for (int i = 0; i < ns; ++i) widths[np++] = base + (i < extra ? 1 : 0);
   }
-  return QS_OK;
+  p.N = static_cast<int>(n);
+  p.nst = np;
+  p.big = 0;
+  for (int s = 0; s < np; ++s) {
+    XStage &S = p.st[s];
+    S.R = 1 << widths[s];
+    S.G = 1;
+    S.Ns = 1;
+    S.nb = p.N / S.R;
+    S.twstep = 0;
+    S.dNs = make_fastdiv(1);
+  }
+  return finish_plan(p, L, 4, rows, want);
 }
 
 int check_fft_size(int64_t n_complex) {
-  FftPlan p;
-  return make_plan(n_complex, p);
+  XPlan p;
+  XLaunch L;
+  return make_fft_plan(n_complex, 1, p, L);
 }
 
-static size_t fft_smem_bytes(const FftPlan &p) {
-  return (p.pingpong ? 2 : 1) * static_cast<size_t>(fft_buf_elems(p.N)) * sizeof(float2);
+int check_fwht_size(int64_t n) {
+  XPlan p;
+  XLaunch L;
+  return make_fwht_plan(n, 1, p, L);
 }
 
-int launch_rfft(int inverse, const void *x, int64_t ld_x, void *y, int64_t ld_y, int dtype,
-                int64_t rows, int64_t n, const void *phase, cudaStream_t s) {
-  FftPlan p;
-  int st = make_plan(n / 2, p);
+// ============================================================================
+// Standalone transforms
+// ============================================================================
+int launch_fwht(const void *x, int64_t ld_x, void *y, int64_t ld_y, int dtype, int64_t rows, int64_t n,
+                const float *pre, const float *post, cudaStream_t s) {
+  XPlan p;
+  XLaunch L;
+  int st = make_fwht_plan(n, rows, p, L);
   if (st) return st;
-  const size_t smem = fft_smem_bytes(p);
+  if (rows == 0) return QS_OK;
+  const float sc = inv_sqrt_f32(n);
+  return p.C > 1 ? run_xfwht_rows<true>(L, s, x, ld_x, y, ld_y, dtype, p, pre, post, sc)
+                 : run_xfwht_rows<false>(L, s, x, ld_x, y, ld_y, dtype, p, pre, post, sc);
+}
+
+int launch_rfft(int inverse, const void *x, int64_t ld_x, void *y, int64_t ld_y, int dtype, int64_t rows, int64_t n,
+                const void *phase, cudaStream_t s) {
+  XPlan p;
+  XLaunch L;
+  int st = make_fft_plan(n / 2, rows, p, L);
+  if (st) return st;
+  if (rows == 0) return QS_OK;
   const float2 *ph = static_cast<const float2 *>(phase);
   const float sc = inv_sqrt_f32(n / 2);
-  if (!p.pingpong) return run_rfft_rows<false, 0>(inverse, x, ld_x, y, ld_y, dtype, rows, p, ph, sc, smem, s);
   switch (p.big) {
-#define QS_CASE(B) \
-  case B: return run_rfft_rows<true, B>(inverse, x, ld_x, y, ld_y, dtype, rows, p, ph, sc, smem, s);
-    QS_FOR_EACH_BIG(QS_CASE)
+#define QS_CASE(B)                                                                                   \
+  case B:                                                                                            \
+    return p.C > 1 ? run_xrfft_rows<B, true>(L, s, inverse, x, ld_x, y, ld_y, dtype, p, ph, sc)     \
+                   : run_xrfft_rows<B, false>(L, s, inverse, x, ld_x, y, ld_y, dtype, p, ph, sc);
+    QS_FOR_EACH_XBIG(QS_CASE)
 #undef QS_CASE
     default: return fail(QS_ERR_UNSUPPORTED, "bad FFT plan");
   }
@@ -218,110 +237,58 @@ int64_t linear_input_bytes(int64_t batch, int64_t n) {
   return round_up(batch * n_padded(n) * 2, 256) + round_up(batch * 4, 256);
 }
 
-__global__ void __launch_bounds__(1024) linear_input_rht_kernel(
-    const void *x, int dtype, int L, int E, const float *sv, float scale, __half *x2h,
-    float *rowscale, int n_pad, float *y1, int64_t m_local) {
-  extern __shared__ float fsm[];
-  __shared__ float red[32];
-  pdl_launch_dependents();
-  pdl_wait();  // x may be the previous kernel's output; y1 may still be read by it
-  const int n = 1 << L;
-  const int64_t row = blockIdx.x;
-  for (int64_t i = threadIdx.x; i < m_local; i += blockDim.x) y1[row * m_local + i] = 0.f;
-  float amax = 0.f;
-  auto gload = [&](int i) { return load_as_float(x, row * n + i, dtype) * sv[i]; };
-  auto rstore = [&](int i, float v) {
-    v *= scale;
-    amax = fmaxf(amax, fabsf(v));
-    fsm[fpad(i)] = v;
-  };
-  fwht_row(gload, rstore, fsm, L, E);
-  __syncthreads();
-  emit_x2h([&](int i) { return fsm[fpad(i)]; }, amax, n, n_pad, x2h + row * n_pad, rowscale + row, red);
-}
-
-// Buffer (0/1) that receives the result of fft_row when its store functor
-// writes shared memory: the one the last stage does not read.
-static int fft_result_buf(const FftPlan &p) {
-  if (!p.pingpong) return 0;
-  if (p.nst == 1) return 0;
-  return ((p.nst - 2) % 2) ^ 1;
-}
-
-int launch_linear_input(const void *x, int x_dtype, int64_t batch, int64_t n, int transform,
-                        const float *sv, const void *phase_v, void *x2ws, float *y1,
-                        int64_t m_local, cudaStream_t s) {
+int launch_linear_input(const void *x, int x_dtype, int64_t batch, int64_t n, int transform, const float *sv,
+                        const void *phase_v, void *x2ws, float *y1, int64_t m_local, cudaStream_t s) {
   const int64_t n_pad = n_padded(n);
   __half *x2h = static_cast<__half *>(x2ws);
   float *rowscale = reinterpret_cast<float *>(static_cast<char *>(x2ws) + round_up(batch * n_pad * 2, 256));
   if (!y1) m_local = 0;
+  const int np = static_cast<int>(n_pad);
+  XPlan p;
+  XLaunch L;
   int st;
   if (transform == QS_RHT) {
-    FwhtGeom g = fwht_geom(n);
-    if ((st = set_smem(linear_input_rht_kernel, g.smem))) return st;
-    return launch_pdl("linear_input_rht", linear_input_rht_kernel, dim3(batch), dim3(g.threads), g.smem, s,
-                      x, x_dtype, g.L, g.E, sv, inv_sqrt_f32(n), x2h, rowscale, static_cast<int>(n_pad), y1,
-                      m_local);
+    if ((st = make_fwht_plan(n, batch, p, L))) return st;
+    const float sc = inv_sqrt_f32(n);
+    return p.C > 1 ? run_xinput_rht<true>(L, s, x, x_dtype, p, sv, sc, x2h, rowscale, np, y1, m_local)
+                   : run_xinput_rht<false>(L, s, x, x_dtype, p, sv, sc, x2h, rowscale, np, y1, m_local);
   }
-  FftPlan p;
-  if ((st = make_plan(n / 2, p))) return st;
-  const size_t smem = fft_smem_bytes(p);
+  if ((st = make_fft_plan(n / 2, batch, p, L))) return st;
   const float2 *ph = static_cast<const float2 *>(phase_v);
   const float sc = inv_sqrt_f32(n / 2);
-  const int rb = fft_result_buf(p), np = static_cast<int>(n_pad);
-  if (!p.pingpong)
-    return run_linear_input_rfft<false, 0>(x, x_dtype, batch, p, ph, sc, x2h, rowscale, np, y1, m_local, rb, smem, s);
   switch (p.big) {
-#define QS_CASE(B) \
-  case B: return run_linear_input_rfft<true, B>(x, x_dtype, batch, p, ph, sc, x2h, rowscale, np, y1, m_local, rb, smem, s);
-    QS_FOR_EACH_BIG(QS_CASE)
+#define QS_CASE(B)                                                                                             \
+  case B:                                                                                                      \
+    return p.C > 1 ? run_xinput_rfft<B, true>(L, s, x, x_dtype, p, ph, sc, x2h, rowscale, np, y1, m_local)    \
+                   : run_xinput_rfft<B, false>(L, s, x, x_dtype, p, ph, sc, x2h, rowscale, np, y1, m_local);
+    QS_FOR_EACH_XBIG(QS_CASE)
 #undef QS_CASE
     default: return fail(QS_ERR_UNSUPPORTED, "bad FFT plan");
   }
 }
 
-__global__ void __launch_bounds__(1024) linear_output_rht_kernel(const float *y1, int64_t ld_y1,
-                                                                 int64_t shards, int64_t batch,
-                                                                 int L, int E, const float *su,
-                                                                 const float *bias, float scale,
-                                                                 void *y, int dtype) {
-  extern __shared__ float fsm[];
-  pdl_launch_dependents();
-  pdl_wait();  // y1 comes from the matmul kernel
-  const int m = 1 << L;
-  const int64_t mp = m / shards;
-  const int64_t row = blockIdx.x;
-  auto gload = [&](int i) { return y1[y1_offset(row, i, ld_y1, shards, mp, batch)]; };
-  auto gstore = [&](int i, float v) {
-    v = v * scale * su[i];
-    if (bias) v += bias[i];
-    store_from_float(y, row * m + i, dtype, v);
-  };
-  fwht_row(gload, gstore, fsm, L, E);
-}
-
-int launch_linear_output(const float *y1, int64_t ld_y1, int64_t shards, int64_t batch, int64_t m,
-                         int transform, const float *su, const void *phase_u, const float *bias,
-                         void *y, int y_dtype, cudaStream_t s) {
+int launch_linear_output(const float *y1, int64_t ld_y1, int64_t shards, int64_t batch, int64_t m, int transform,
+                         const float *su, const void *phase_u, const float *bias, void *y, int y_dtype,
+                         cudaStream_t s) {
+  XPlan p;
+  XLaunch L;
   int st;
   if (transform == QS_RHT) {
-    FwhtGeom g = fwht_geom(m);
-    if ((st = set_smem(linear_output_rht_kernel, g.smem))) return st;
-    return launch_pdl("linear_output_rht", linear_output_rht_kernel, dim3(batch), dim3(g.threads), g.smem, s,
-                      y1, ld_y1, shards, batch, g.L, g.E, su, bias, inv_sqrt_f32(m), y, y_dtype);
+    if ((st = make_fwht_plan(m, batch, p, L))) return st;
+    const float sc = inv_sqrt_f32(m);
+    return p.C > 1 ? run_xoutput_rht<true>(L, s, y1, ld_y1, shards, batch, p, su, bias, sc, y, y_dtype)
+                   : run_xoutput_rht<false>(L, s, y1, ld_y1, shards, batch, p, su, bias, sc, y, y_dtype);
   }
   if (ld_y1 % 2) return fail(QS_ERR_ALIGNMENT, "RFFT y1 row stride must be even");
-  FftPlan p;
-  if ((st = make_plan(m / 2, p))) return st;
-  const size_t smem = fft_smem_bytes(p);
+  if ((st = make_fft_plan(m / 2, batch, p, L))) return st;
   const float2 *ph = static_cast<const float2 *>(phase_u);
   const float sc = inv_sqrt_f32(m / 2);
-  if (!p.pingpong)
-    return run_linear_output_rfft<false, 0>(y1, ld_y1, shards, batch, p, ph, bias, sc, y, y_dtype, smem, s);
   switch (p.big) {
-#define QS_CASE(B) \
-  case B: return run_linear_output_rfft<true, B>(y1, ld_y1, shards, batch, p, ph, bias, sc, y, y_dtype, smem, s);
-    QS_FOR_EACH_BIG(QS_CASE)
+#define QS_CASE(B)                                                                                                \
+  case B:                                                                                                         \
+    return p.C > 1 ? run_xoutput_rfft<B, true>(L, s, y1, ld_y1, shards, batch, p, ph, bias, sc, y, y_dtype)      \
+                   : run_xoutput_rfft<B, false>(L, s, y1, ld_y1, shards, batch, p, ph, bias, sc, y, y_dtype);
+    QS_FOR_EACH_XBIG(QS_CASE)
 #undef QS_CASE
     default: return fail(QS_ERR_UNSUPPORTED, "bad FFT plan");
   }

@@ -1,0 +1,981 @@
+// Row transforms of the incoherence processing -- the RFFT transform's
+// complex FFT (quipsharp/rfft.py:37-60) and the randomized Hadamard
+// transform's FWHT (quipsharp/hadamard.py:17-40) -- as one engine of
+// register-resident Stockham stages.
+//
+// Execution model
+//  * One row of N points is transformed by a group of C CTAs (C = 1, or a
+//    thread-block cluster of 2..16 CTAs exchanging data through distributed
+//    shared memory).  Few rows (decode) spread each row over a cluster so the
+//    transform's latency is divided over up to 16 SMs; many rows (prefill) run
+//    one CTA per row, or a small cluster when a row does not fit one SM's
+//    shared memory twice.
+//  * The row lives in two shared buffers (ping-pong), distributed over the
+//    group: element e sits in CTA e / E at offset e % E, E = N / C.
+//  * A stage is a set of independent tasks (butterflies, or parts of one); the
+//    group's CTAs split the task range.  A thread loads the values of a task
+//    from the source buffer, transforms them in registers, and stores them to
+//    the destination buffer; a barrier (CTA or cluster) separates stages.
+//  * The first stage reads the row from global memory (with the cast and the
+//    sign / phase multiply fused into the load) and, for the output steps, the
+//    last stage writes global memory (scale, sign / conjugate phase, bias and
+//    cast fused into the store), so HBM sees the row once in and once out.
+//
+// FFT: mixed-radix Stockham, radices {16, 8, 4, 2} (in-register DIT), odd
+// primes 3..43.  Stage order: the prime >= 11 (at most one, first, read from
+// global), then 7 / 5 / 3, then the power-of-two stages.  The odd-prime DFT
+// uses the conjugate-pair form X_k, X_{P-k} = A_k -+ i B_k; its (P-1)/2 output
+// pairs are split into G groups that run as separate tasks (warp-uniform), each
+// with compile-time cos / sin operands.  Twiddles W_N^e come from two small
+// shared tables (W_N^e = C[e >> 7] * F[e & 127]); the powers a butterfly needs
+// are formed by repeated complex multiplication.
+//
+// FWHT: passes of W <= 5 index bits (groups of 2^W values in registers).
+#pragma once
+
+#include "qs_common.cuh"
+#include "qs_launch.h"
+
+namespace qs {
+
+// ---- limits ------------------------------------------------------------------
+constexpr int kXMaxStages = 16;
+constexpr int kXMaxN = 32768;            // complex FFT points / FWHT points per row
+constexpr int kXFine = 128;
+constexpr int kXCoarse = kXMaxN / kXFine;
+constexpr int kXMaxCluster = 16;
+constexpr int kXMaxThreads = 512;
+
+// ---- division by a runtime constant (x < 2^31) -------------------------------
+// q = (umulhi(x, m) + x) >> l with l = ceil(log2 d), m = floor(2^32 (2^l - d) / d) + 1.
+struct FastDiv {
+  uint32_t d, m, l;
+};
+
+inline FastDiv make_fastdiv(uint32_t d) {
+  FastDiv f;
+  f.d = d;
+  uint32_t l = 0;
+  while ((uint64_t(1) << l) < d) ++l;
+  f.l = l;
+  f.m = static_cast<uint32_t>(((uint64_t(1) << 32) * ((uint64_t(1) << l) - d)) / d + 1);
+  return f;
+}
+
+__device__ __forceinline__ int fdiv(int x, const FastDiv &f) {
+  return static_cast<int>((__umulhi(static_cast<uint32_t>(x), f.m) + static_cast<uint32_t>(x)) >> f.l);
+}
+
+// ---- plans ----------------------------------------------------------------
+struct XStage {
+  int R;       // radix (FFT: 1 = copy, 2..16 powers of two, odd primes; FWHT: 2^W, 1 = copy)
+  int G;       // task groups per butterfly (odd radices), else 1
+  int Ns;      // FFT: product of the previous radices (FWHT: unused)
+  int nb;      // butterflies: N / R
+  int nbC;     // butterflies per CTA: nb / C
+  int twstep;  // N / (Ns * R)
+  FastDiv dNs, dnbC;
+};
+
+struct XPlan {
+  int N;     // points (complex for the FFT, real for the FWHT)
+  int nst;   // stages (>= 1)
+  int C;     // CTAs per row (power of two, divides every stage's nb)
+  int cl;    // log2(C)
+  int E;     // points per CTA (N / C)
+  int big;   // prime >= 11 of the FFT (0: none)
+  XStage st[kXMaxStages];
+};
+
+// ---- small complex helpers -----------------------------------------------------
+__device__ __forceinline__ float2 xcmul(float2 a, float2 b) {
+  return make_float2(a.x * b.x - a.y * b.y, a.x * b.y + a.y * b.x);
+}
+__device__ __forceinline__ float2 xcadd(float2 a, float2 b) { return make_float2(a.x + b.x, a.y + b.y); }
+__device__ __forceinline__ float2 xcsub(float2 a, float2 b) { return make_float2(a.x - b.x, a.y - b.y); }
+__device__ __forceinline__ float2 xconj(float2 a) { return make_float2(a.x, -a.y); }
+
+// Padded shared offsets (break the power-of-two strides of the butterflies).
+__device__ __forceinline__ int xpad(int i, float2) { return i + (i >> 4); }
+__device__ __forceinline__ int xpad(int i, float) { return i + (i >> 5); }
+template <typename T>
+__host__ __device__ constexpr int xbuf_elems(int E) {
+  return sizeof(T) == 8 ? E + (E >> 4) + 1 : E + (E >> 5) + 1;
+}
+
+// ---- cluster primitives --------------------------------------------------------
+__device__ __forceinline__ uint32_t cluster_rank() {
+  uint32_t r;
+  asm volatile("mov.u32 %0, %%cluster_ctarank;" : "=r"(r));
+  return r;
+}
+
+__device__ __forceinline__ void cluster_sync() {
+  asm volatile("barrier.cluster.arrive.release.aligned;\n\tbarrier.cluster.wait.acquire.aligned;" ::: "memory");
+}
+
+__device__ __forceinline__ uint32_t mapa_shared(uint32_t addr, uint32_t rank) {
+  uint32_t r;
+  asm volatile("mapa.shared::cluster.u32 %0, %1, %2;" : "=r"(r) : "r"(addr), "r"(rank));
+  return r;
+}
+
+__device__ __forceinline__ float2 ld_dsmem(uint32_t addr, float2) {
+  float2 v;
+  asm volatile("ld.shared::cluster.v2.f32 {%0, %1}, [%2];" : "=f"(v.x), "=f"(v.y) : "r"(addr) : "memory");
+  return v;
+}
+__device__ __forceinline__ float ld_dsmem(uint32_t addr, float) {
+  float v;
+  asm volatile("ld.shared::cluster.f32 %0, [%1];" : "=f"(v) : "r"(addr) : "memory");
+  return v;
+}
+__device__ __forceinline__ void st_dsmem(uint32_t addr, float2 v) {
+  asm volatile("st.shared::cluster.v2.f32 [%0], {%1, %2};" ::"r"(addr), "f"(v.x), "f"(v.y) : "memory");
+}
+__device__ __forceinline__ void st_dsmem(uint32_t addr, float v) {
+  asm volatile("st.shared::cluster.f32 [%0], %1;" ::"r"(addr), "f"(v) : "memory");
+}
+
+template <bool CL>
+__device__ __forceinline__ void xsync() {
+  if constexpr (CL) cluster_sync();
+  else __syncthreads();
+}
+
+// Row layout: element e lives in CTA e & (C - 1) at local index e >> cl
+// (cyclic), so a butterfly j whose inputs are j + r * nb (C divides nb) finds
+// all of them in CTA j & (C - 1).  Stages read their own CTA's buffer and
+// write the owners' buffers (remote stores through distributed shared memory,
+// which do not stall the thread).
+template <typename T, bool CL>
+struct XSrc {  // elements owned by this CTA
+  const T *p;
+  int cl;
+  __device__ __forceinline__ T operator()(int e) const { return p[xpad(CL ? (e >> cl) : e, T())]; }
+};
+
+template <typename T, bool CL>
+struct XDst {  // any element: stored into its owner's buffer
+  T *p;
+  int cl;
+  __device__ __forceinline__ void operator()(int e, T v) const {
+    if constexpr (CL) {
+      const uint32_t a = mapa_shared(smem_u32(p + xpad(e >> cl, T())), static_cast<uint32_t>(e & ((1 << cl) - 1)));
+      st_dsmem(a, v);
+    } else {
+      p[xpad(e, T())] = v;
+    }
+  }
+};
+
+// ---- twiddles ----------------------------------------------------------------
+struct XTw {
+  float2 fine[kXFine];
+  float2 coarse[kXCoarse];
+};
+
+__device__ __forceinline__ void build_xtw(XTw &tw, int N) {
+  const int nc = (N + kXFine - 1) / kXFine;
+  for (int j = threadIdx.x; j < kXFine + nc; j += blockDim.x) {
+    const int e = j < kXFine ? j : (j - kXFine) * kXFine;
+    float s, c;
+    sincospif(2.0f * static_cast<float>(e % N) / static_cast<float>(N), &s, &c);
+    if (j < kXFine) tw.fine[j] = make_float2(c, -s);
+    else tw.coarse[j - kXFine] = make_float2(c, -s);
+  }
+}
+
+// W_N^e (forward) or its conjugate (inverse), 0 <= e < N.
+__device__ __forceinline__ float2 xtw(const XTw &tw, int e, bool inverse) {
+  const float2 w = xcmul(tw.coarse[e >> 7], tw.fine[e & (kXFine - 1)]);
+  return inverse ? xconj(w) : w;
+}
+
+// ---- in-register DFTs ----------------------------------------------------------
+__host__ __device__ constexpr float xcos16(int k) {
+  return (k & 15) == 0 ? 1.0f : (k & 15) == 1 ? 0.92387953251128674f : (k & 15) == 2 ? 0.70710678118654752f
+       : (k & 15) == 3 ? 0.38268343236508977f : (k & 15) == 4 ? 0.0f : (k & 15) == 5 ? -0.38268343236508977f
+       : (k & 15) == 6 ? -0.70710678118654752f : (k & 15) == 7 ? -0.92387953251128674f : (k & 15) == 8 ? -1.0f
+       : (k & 15) == 9 ? -0.92387953251128674f : (k & 15) == 10 ? -0.70710678118654752f
+       : (k & 15) == 11 ? -0.38268343236508977f : (k & 15) == 12 ? 0.0f : (k & 15) == 13 ? 0.38268343236508977f
+       : (k & 15) == 14 ? 0.70710678118654752f : 0.92387953251128674f;
+}
+
+// Multiplies by W_16^K (forward) / W_16^-K (inverse); the K = 4 (-+i) case is a swap.
+template <int K>
+__device__ __forceinline__ float2 xrot16(float2 v, bool inverse) {
+  constexpr int k = K & 15;
+  if constexpr (k == 0) return v;
+  else if constexpr (k == 4) return inverse ? make_float2(-v.y, v.x) : make_float2(v.y, -v.x);
+  else {
+    constexpr float cs = xcos16(k), sn = xcos16(k + 12);  // sin(2 pi k / 16)
+    const float2 w = make_float2(cs, inverse ? sn : -sn);
+    return xcmul(w, v);
+  }
+}
+
+template <int R, int LEN, int K>
+__device__ __forceinline__ void xpow2_butterflies(float2 (&v)[R], bool inverse) {
+  if constexpr (K < LEN / 2) {
+#pragma unroll
+    for (int i = 0; i < R; i += LEN) {
+      const float2 u = v[i + K];
+      const float2 t = xrot16<K * (16 / LEN)>(v[i + K + LEN / 2], inverse);
+      v[i + K] = xcadd(u, t);
+      v[i + K + LEN / 2] = xcsub(u, t);
+    }
+    xpow2_butterflies<R, LEN, K + 1>(v, inverse);
+  }
+}
+
+template <int R, int LEN>
+__device__ __forceinline__ void xpow2_levels(float2 (&v)[R], bool inverse) {
+  if constexpr (LEN <= R) {
+    xpow2_butterflies<R, LEN, 0>(v, inverse);
+    xpow2_levels<R, LEN * 2>(v, inverse);
+  }
+}
+
+// DFT of R = 2^k points in registers (natural order in and out), radix-2 DIT.
+template <int R>
+__device__ __forceinline__ void xdft_pow2(float2 (&v)[R], bool inverse) {
+#pragma unroll
+  for (int i = 0; i < R; ++i) {
+    int j = 0;
+#pragma unroll
+    for (int b = 1, t = i; b < R; b <<= 1, t >>= 1) j = (j << 1) | (t & 1);
+    if (i < j) {
+      const float2 tmp = v[i];
+      v[i] = v[j];
+      v[j] = tmp;
+    }
+  }
+  xpow2_levels<R, 2>(v, inverse);
+}
+
+// ---- FFT stages ----------------------------------------------------------------
+// Butterfly j of this CTA: j = rank + C * i, i < nbC.
+
+// Power-of-two (or copy, R = 1) Stockham stage: butterfly j reads
+// src[j + r*nb], twiddles by W_{Ns*R}^{r*k} (k = j mod Ns), transforms, writes
+// dst[(j - k)*R + k + r*Ns].
+template <int R, typename Src, typename Dst>
+__device__ __forceinline__ void xstage_pow2(const XStage &S, const Src &src, const Dst &dst, const XTw &tw,
+                                            bool inverse, int rank, int C) {
+  for (int i = threadIdx.x; i < S.nbC; i += blockDim.x) {
+    const int j = rank + C * i;
+    float2 v[R];
+#pragma unroll
+    for (int r = 0; r < R; ++r) v[r] = src(j + r * S.nb);
+    int k = 0;
+    if (S.Ns > 1) {
+      k = j - fdiv(j, S.dNs) * S.Ns;
+      if constexpr (R > 1) {
+        // powers w^r by a product tree (depth log2 R): w^r = w^(r/2) * w^(r - r/2)
+        float2 pw[R];
+        pw[1] = xtw(tw, k * S.twstep, inverse);
+#pragma unroll
+        for (int r = 2; r < R; ++r) pw[r] = xcmul(pw[r / 2], pw[r - r / 2]);
+#pragma unroll
+        for (int r = 1; r < R; ++r) v[r] = xcmul(v[r], pw[r]);
+      }
+    }
+    if constexpr (R > 1) xdft_pow2<R>(v, inverse);
+    const int base = (j - k) * R + k;
+#pragma unroll
+    for (int r = 0; r < R; ++r) dst(base + r * S.Ns, v[r]);
+  }
+}
+
+__host__ __device__ constexpr int xodd_groups(int P) {
+  return ((P - 1) / 2 + 5) / 6;  // at most 6 output pairs per task
+}
+__host__ __device__ constexpr int xodd_per(int P) {
+  return ((P - 1) / 2 + xodd_groups(P) - 1) / xodd_groups(P);
+}
+
+// Writes the outputs of output group (klo .. klo + per - 1) of an odd-prime
+// butterfly: X_k = A - iB, X_{P-k} = A + iB (forward; swapped for the inverse).
+template <int P, typename Dst>
+__device__ __forceinline__ void xodd_store(const Dst &dst, int base, int Ns, int klo, const float2 (&A)[xodd_per(P)],
+                                           const float2 (&B)[xodd_per(P)], bool inverse) {
+  constexpr int H = (P - 1) / 2;
+#pragma unroll
+  for (int q = 0; q < xodd_per(P); ++q) {
+    const int kk = klo + q;
+    if (kk <= H) {
+      const float2 miB = make_float2(B[q].y, -B[q].x);  // -iB
+      dst(base + kk * Ns, inverse ? xcsub(A[q], miB) : xcadd(A[q], miB));
+      dst(base + (P - kk) * Ns, inverse ? xcadd(A[q], miB) : xcsub(A[q], miB));
+    }
+  }
+}
+
+// Output group g of butterfly j, fully unrolled: cos / sin are compile-time
+// constant-bank operands (throughput variant, one CTA per row).
+template <int P, int g, typename Src, typename Dst>
+__device__ __forceinline__ void xodd_group_unrolled(const XStage &S, const Src &src, const Dst &dst, int j, int k,
+                                                    float2 w1, float2 wP, bool tw_on, bool inverse) {
+  constexpr int H = (P - 1) / 2;
+  constexpr int per = xodd_per(P);
+  constexpr int klo = g * per + 1;
+  constexpr int off = prime_offset(P);
+  const float2 x0 = src(j);
+  float2 A[per], B[per];
+#pragma unroll
+  for (int q = 0; q < per; ++q) {
+    A[q] = x0;
+    B[q] = make_float2(0.f, 0.f);
+  }
+  float2 s0 = x0;
+  float2 tr = w1;
+#pragma unroll
+  for (int r = 1; r <= H; ++r) {
+    float2 xa = src(j + r * S.nb), xb = src(j + (P - r) * S.nb);
+    if (tw_on) {
+      if (r > 1) tr = xcmul(tr, w1);
+      xa = xcmul(xa, tr);
+      xb = xcmul(xb, xcmul(wP, xconj(tr)));
+    }
+    const float2 a = xcadd(xa, xb), b = xcsub(xa, xb);
+    if constexpr (g == 0) s0 = xcadd(s0, a);
+#pragma unroll
+    for (int q = 0; q < per; ++q) {
+      if (klo + q <= H) {
+        const float c = kDftCos[off + (r * (klo + q)) % P];
+        const float s = kDftSin[off + (r * (klo + q)) % P];
+        A[q].x = fmaf(a.x, c, A[q].x);
+        A[q].y = fmaf(a.y, c, A[q].y);
+        B[q].x = fmaf(b.x, s, B[q].x);
+        B[q].y = fmaf(b.y, s, B[q].y);
+      }
+    }
+  }
+  const int base = (j - k) * P + k;
+  xodd_store<P>(dst, base, S.Ns, klo, A, B, inverse);
+  if constexpr (g == 0) dst(base, s0);
+}
+
+template <int P, int g, typename Src, typename Dst>
+__device__ __forceinline__ void xodd_dispatch(int gi, const XStage &S, const Src &src, const Dst &dst, int j,
+                                              int k, float2 w1, float2 wP, bool tw_on, bool inverse) {
+  if constexpr (g < xodd_groups(P)) {
+    if (gi == g) xodd_group_unrolled<P, g>(S, src, dst, j, k, w1, wP, tw_on, inverse);
+    else xodd_dispatch<P, g + 1>(gi, S, src, dst, j, k, w1, wP, tw_on, inverse);
+  }
+}
+
+// Output pair k = g + 1 of butterfly j, compact: the loop over the inputs is
+// rolled (by 3) and cos / sin come from the constant table (latency variant:
+// a cluster per row runs this code once, so its length and the per-thread
+// dependency chain, not the instruction count, set the time).
+template <int P, typename Src, typename Dst>
+__device__ __forceinline__ void xodd_pair_compact(int g, const XStage &S, const Src &src, const Dst &dst, int j,
+                                                  int k, float2 w1, float2 wP, bool tw_on, bool inverse) {
+  constexpr int H = (P - 1) / 2;
+  constexpr int off = prime_offset(P);
+  const int kk = g + 1;
+  const float2 x0 = src(j);
+  float2 A = x0, B = make_float2(0.f, 0.f), s0 = x0, tr = w1;
+  int idx = 0;
+#pragma unroll 3
+  for (int r = 1; r <= H; ++r) {
+    float2 xa = src(j + r * S.nb), xb = src(j + (P - r) * S.nb);
+    if (tw_on) {
+      if (r > 1) tr = xcmul(tr, w1);
+      xa = xcmul(xa, tr);
+      xb = xcmul(xb, xcmul(wP, xconj(tr)));
+    }
+    const float2 a = xcadd(xa, xb), b = xcsub(xa, xb);
+    s0 = xcadd(s0, a);
+    idx += kk;  // (r * k) mod P, kept incrementally
+    if (idx >= P) idx -= P;
+    const float c = kDftCos[off + idx];
+    const float sn = kDftSin[off + idx];
+    A.x = fmaf(a.x, c, A.x);
+    A.y = fmaf(a.y, c, A.y);
+    B.x = fmaf(b.x, sn, B.x);
+    B.y = fmaf(b.y, sn, B.y);
+  }
+  const int base = (j - k) * P + k;
+  const float2 miB = make_float2(B.y, -B.x);  // -iB
+  dst(base + kk * S.Ns, inverse ? xcsub(A, miB) : xcadd(A, miB));
+  dst(base + (P - kk) * S.Ns, inverse ? xcadd(A, miB) : xcsub(A, miB));
+  if (g == 0) dst(base, s0);
+}
+
+// Odd-prime stage: task t = g * nbC + i (output group g of butterfly
+// j = rank + C * i; COMPACT: output pair g + 1, G = (P - 1) / 2 groups);
+// tasks of a warp share g except at group boundaries.
+template <int P, bool COMPACT, typename Src, typename Dst>
+__device__ __forceinline__ void xstage_odd(const XStage &S, const Src &src, const Dst &dst, const XTw &tw,
+                                           bool inverse, int rank, int C) {
+  const int tasks = S.nbC * S.G;
+  for (int t = threadIdx.x; t < tasks; t += blockDim.x) {
+    const int g = fdiv(t, S.dnbC);
+    const int j = rank + C * (t - g * S.nbC);
+    int k = 0;
+    float2 w1 = make_float2(1.f, 0.f), wP = w1;
+    const bool tw_on = S.Ns > 1;
+    if (tw_on) {
+      k = j - fdiv(j, S.dNs) * S.Ns;
+      w1 = xtw(tw, k * S.twstep, inverse);
+      wP = xtw(tw, k * S.twstep * P, inverse);
+    }
+    if constexpr (COMPACT) xodd_pair_compact<P>(g, S, src, dst, j, k, w1, wP, tw_on, inverse);
+    else xodd_dispatch<P, 0>(g, S, src, dst, j, k, w1, wP, tw_on, inverse);
+  }
+}
+
+// One stage, any radix of the plan (the prime >= 11 only as stage 0, odd radices
+// never last: the host plan guarantees both).
+template <int BIG, bool COMPACT, bool FIRST, bool LAST, typename Src, typename Dst>
+__device__ __forceinline__ void xfft_stage(const XStage &S, const Src &src, const Dst &dst, const XTw &tw,
+                                           bool inverse, int rank, int C) {
+  switch (S.R) {
+    case 1: xstage_pow2<1>(S, src, dst, tw, inverse, rank, C); break;
+    case 2: xstage_pow2<2>(S, src, dst, tw, inverse, rank, C); break;
+    case 4: xstage_pow2<4>(S, src, dst, tw, inverse, rank, C); break;
+    case 8: xstage_pow2<8>(S, src, dst, tw, inverse, rank, C); break;
+    case 16: xstage_pow2<16>(S, src, dst, tw, inverse, rank, C); break;
+    default:
+      if constexpr (!LAST) {
+        if (S.R == 3) xstage_odd<3, COMPACT>(S, src, dst, tw, inverse, rank, C);
+        else if (S.R == 5) xstage_odd<5, COMPACT>(S, src, dst, tw, inverse, rank, C);
+        else if (S.R == 7) xstage_odd<7, COMPACT>(S, src, dst, tw, inverse, rank, C);
+        else if constexpr (FIRST && BIG != 0) xstage_odd<BIG, COMPACT>(S, src, dst, tw, inverse, rank, C);
+      }
+      break;
+  }
+}
+
+// Power-of-two (or copy) stage only: the first stage when it reads global memory.
+template <bool CL, typename Src, typename Dst>
+__device__ __forceinline__ void xfft_stage_pow2(const XStage &S, const Src &src, const Dst &dst, const XTw &tw,
+                                                bool inverse, int rank, int C) {
+  switch (S.R) {
+    case 1: xstage_pow2<1>(S, src, dst, tw, inverse, rank, C); break;
+    case 2: xstage_pow2<2>(S, src, dst, tw, inverse, rank, C); break;
+    case 4: xstage_pow2<4>(S, src, dst, tw, inverse, rank, C); break;
+    case 8: xstage_pow2<8>(S, src, dst, tw, inverse, rank, C); break;
+    case 16: xstage_pow2<16>(S, src, dst, tw, inverse, rank, C); break;
+    default: break;
+  }
+}
+
+// Loads the row into buffer 0: this CTA reads the contiguous range
+// [rank * E, (rank + 1) * E) (coalesced, U loads in flight per thread) and
+// stores each element into its owner's buffer.
+template <int U, typename T, typename GSrc, typename Dst>
+__device__ __forceinline__ void xload_row(const GSrc &gsrc, const Dst &dst, int E, int rank) {
+  const int e0 = rank * E;
+  for (int base = threadIdx.x; base < E; base += U * blockDim.x) {
+    T v[U];
+#pragma unroll
+    for (int u = 0; u < U; ++u) {
+      const int i = base + u * blockDim.x;
+      if (i < E) v[u] = gsrc(e0 + i);
+    }
+#pragma unroll
+    for (int u = 0; u < U; ++u) {
+      const int i = base + u * blockDim.x;
+      if (i < E) dst(e0 + i, v[u]);
+    }
+  }
+}
+
+// Unnormalised DFT of the row (forward exp(-2 pi i jk/N), inverse exp(+...)):
+// gsrc(e) -> sink(e, v).  Group barriers separate the load pass and the
+// stages; ends after the last stage's stores, without a barrier.
+template <int BIG, bool CL, typename GSrc, typename Sink>
+__device__ __forceinline__ void xfft_row(const XPlan &p, float2 *buf0, float2 *buf1, const XTw &tw, bool inverse,
+                                         int rank, const GSrc &gsrc, const Sink &sink) {
+  const XSrc<float2, CL> s0{buf0, p.cl}, s1{buf1, p.cl};
+  const XDst<float2, CL> d0{buf0, p.cl}, d1{buf1, p.cl};
+  // A power-of-two first stage reads the row straight from global memory (its
+  // R loads per thread are independent); an odd first stage, whose loop
+  // consumes its inputs one pair at a time, reads a shared copy made by a
+  // coalesced load pass.
+  const bool direct = !(p.st[0].R & 1) || p.st[0].R == 1;
+  if (!direct) {
+    xload_row<8, float2>(gsrc, d0, p.E, rank);
+    xsync<CL>();
+  }
+  if (p.nst == 1) {
+    if (direct) xfft_stage_pow2<CL>(p.st[0], gsrc, sink, tw, inverse, rank, p.C);
+    else xfft_stage<BIG, CL, true, true>(p.st[0], s0, sink, tw, inverse, rank, p.C);
+    return;
+  }
+  if (direct) xfft_stage_pow2<CL>(p.st[0], gsrc, d1, tw, inverse, rank, p.C);
+  else xfft_stage<BIG, CL, true, false>(p.st[0], s0, d1, tw, inverse, rank, p.C);
+  xsync<CL>();
+  for (int s = 1; s + 1 < p.nst; ++s) {
+    if (s & 1) xfft_stage<BIG, CL, false, false>(p.st[s], s1, d0, tw, inverse, rank, p.C);
+    else xfft_stage<BIG, CL, false, false>(p.st[s], s0, d1, tw, inverse, rank, p.C);
+    xsync<CL>();
+  }
+  if ((p.nst - 1) & 1) xfft_stage<BIG, CL, false, true>(p.st[p.nst - 1], s1, sink, tw, inverse, rank, p.C);
+  else xfft_stage<BIG, CL, false, true>(p.st[p.nst - 1], s0, sink, tw, inverse, rank, p.C);
+}
+
+// Buffer the last stage reads (the other one receives its results when the
+// sink is a buffer): stage s >= 1 reads buffer (s + 1) & 1 ... stage 0 reads
+// global memory or, after the load pass, buffer 0.
+__device__ __forceinline__ int xresult_buf(const XPlan &p) {
+  if (p.nst == 1) return 1;
+  return (p.nst - 1) & 1 ? 0 : 1;
+}
+
+// ---- FWHT passes ------------------------------------------------------------
+// Pass of W bits on the top of the index, rotating them to the bottom:
+// butterfly j reads src[j + r*nb] (r < 2^W), writes dst[j*2^W + r].  After
+// passes whose widths sum to log2(N) every bit has been transformed once and
+// rotated back to its place.
+template <int W, typename Src, typename Dst>
+__device__ __forceinline__ void xfwht_pass(const XStage &S, const Src &src, const Dst &dst, int rank, int C) {
+  constexpr int R = 1 << W;
+  for (int i = threadIdx.x; i < S.nbC; i += blockDim.x) {
+    const int j = rank + C * i;
+    float v[R];
+#pragma unroll
+    for (int r = 0; r < R; ++r) v[r] = src(j + r * S.nb);
+#pragma unroll
+    for (int h = 1; h < R; h <<= 1) {
+#pragma unroll
+      for (int q = 0; q < R; ++q) {
+        if (!(q & h)) {
+          const float a = v[q], b = v[q + h];
+          v[q] = a + b;
+          v[q + h] = a - b;
+        }
+      }
+    }
+#pragma unroll
+    for (int r = 0; r < R; ++r) dst(j * R + r, v[r]);
+  }
+}
+
+template <typename Src, typename Dst>
+__device__ __forceinline__ void xfwht_stage(const XStage &S, const Src &src, const Dst &dst, int rank, int C) {
+  switch (S.R) {
+    case 1: xfwht_pass<0>(S, src, dst, rank, C); break;
+    case 2: xfwht_pass<1>(S, src, dst, rank, C); break;
+    case 4: xfwht_pass<2>(S, src, dst, rank, C); break;
+    case 8: xfwht_pass<3>(S, src, dst, rank, C); break;
+    case 16: xfwht_pass<4>(S, src, dst, rank, C); break;
+    case 32: xfwht_pass<5>(S, src, dst, rank, C); break;
+    default: break;
+  }
+}
+
+// Unnormalised Walsh-Hadamard transform of the row gsrc(i) -> sink(i, v).
+template <bool CL, typename GSrc, typename Sink>
+__device__ __forceinline__ void xfwht_row(const XPlan &p, float *buf0, float *buf1, int rank, const GSrc &gsrc,
+                                          const Sink &sink) {
+  const XSrc<float, CL> s0{buf0, p.cl}, s1{buf1, p.cl};
+  const XDst<float, CL> d0{buf0, p.cl}, d1{buf1, p.cl};
+  if (p.nst == 1) {  // the first pass reads global memory directly
+    xfwht_stage(p.st[0], gsrc, sink, rank, p.C);
+    return;
+  }
+  xfwht_stage(p.st[0], gsrc, d1, rank, p.C);
+  xsync<CL>();
+  for (int s = 1; s + 1 < p.nst; ++s) {
+    if (s & 1) xfwht_stage(p.st[s], s1, d0, rank, p.C);
+    else xfwht_stage(p.st[s], s0, d1, rank, p.C);
+    xsync<CL>();
+  }
+  if ((p.nst - 1) & 1) xfwht_stage(p.st[p.nst - 1], s1, sink, rank, p.C);
+  else xfwht_stage(p.st[p.nst - 1], s0, sink, rank, p.C);
+}
+
+// ---- row epilogue of the linear input step ------------------------------------------
+// Row |max| over the group: block reduction, then (cluster) every CTA posts its
+// value into every CTA's slot table.  Ends with a group barrier, after which
+// every remote store made before it is visible.
+template <bool CL>
+__device__ __forceinline__ float xgroup_absmax(float v, float *red, float *slots, int rank, int C) {
+  for (int o = 16; o > 0; o >>= 1) v = fmaxf(v, __shfl_xor_sync(0xffffffffu, v, o));
+  const int w = threadIdx.x >> 5, nw = (blockDim.x + 31) >> 5;
+  if ((threadIdx.x & 31) == 0) red[w] = v;
+  __syncthreads();
+  float r = 0.f;
+  for (int i = 0; i < nw; ++i) r = fmaxf(r, red[i]);
+  if constexpr (CL) {
+    if (static_cast<int>(threadIdx.x) < C) st_dsmem(mapa_shared(smem_u32(slots + rank), threadIdx.x), r);
+    cluster_sync();
+    r = 0.f;
+    for (int i = 0; i < C; ++i) r = fmaxf(r, slots[i]);
+  }
+  return r;
+}
+
+__device__ __forceinline__ void xpow2_scale(float amax, float &scale, float &inv) {
+  if (!(amax > 0.f) || !isfinite(amax)) {
+    scale = 1.f;
+    inv = 1.f;
+    return;
+  }
+  int e;
+  frexpf(amax, &e);  // amax = f * 2^e, f in [0.5, 1)
+  scale = ldexpf(1.f, 12 - e);
+  inv = ldexpf(1.f, e - 12);
+}
+
+// Offset of y1 element (row, col): plain row-major with stride ld_y1 when
+// shards == 1, else the rank-major layout of an all-gather of `shards` column
+// blocks of (batch, mp): ((col / mp) * batch + row) * mp + col % mp.
+__device__ __forceinline__ int64_t xy1_offset(int64_t row, int64_t col, int64_t ld_y1, int64_t shards,
+                                              int64_t mp, int64_t batch) {
+  if (shards == 1) return row * ld_y1 + col;
+  return ((col / mp) * batch + row) * mp + col % mp;
+}
+
+// ---- kernels -----------------------------------------------------------------
+// Grid: CL ? (C, rows) with cluster (C, 1, 1) : (rows).  Dynamic shared memory:
+// two buffers of xbuf_elems<T>(E) elements.
+struct XRowArgs {
+  int64_t row_base;
+  int C;
+};
+
+__device__ __forceinline__ int64_t xrow(const XRowArgs &a, bool cl) {
+  return a.row_base + (cl ? blockIdx.y : blockIdx.x);
+}
+
+// Standalone RFFT rows (quipsharp/rfft.py:37-60): forward y = FFT(x * phase) * scale,
+// inverse y = IFFT(x) * scale * conj(phase); x, y viewed as N complex values.
+template <int BIG, bool CL>
+__global__ void __launch_bounds__(kXMaxThreads, 1) xrfft_rows_kernel(
+    int inverse, const void *x, int64_t ld_x, void *y, int64_t ld_y, int dtype, XPlan plan, const float2 *phase,
+    float scale, XRowArgs ra) {
+  extern __shared__ float2 xsm[];
+  __shared__ XTw tw;
+  const int rank = CL ? static_cast<int>(blockIdx.x) : 0;
+  const int64_t row = xrow(ra, CL);
+  float2 *b0 = xsm, *b1 = xsm + xbuf_elems<float2>(plan.E);
+  build_xtw(tw, plan.N);
+  pdl_wait();  // launched with programmatic serialization: x may be the previous kernel's output
+  __syncthreads();
+  const int esz = dtype == QS_F32 ? 4 : 2;
+  const void *xr = static_cast<const char *>(x) + row * ld_x * esz;
+  void *yr = static_cast<char *>(y) + row * ld_y * esz;
+  auto gsrc = [&](int e) {
+    const float2 z = make_float2(load_as_float(xr, 2 * e, dtype), load_as_float(xr, 2 * e + 1, dtype));
+    return inverse ? z : xcmul(z, phase[e]);
+  };
+  auto sink = [&](int e, float2 z) {
+    z.x *= scale;
+    z.y *= scale;
+    if (inverse) z = xcmul(z, xconj(phase[e]));
+    store_from_float(yr, 2 * e, dtype, z.x);
+    store_from_float(yr, 2 * e + 1, dtype, z.y);
+  };
+  xfft_row<BIG, CL>(plan, b0, b1, tw, inverse != 0, rank, gsrc, sink);
+  if constexpr (CL) cluster_sync();  // peers may still read this CTA's buffers
+}
+
+// Input step, RFFT: x2 = FFT(x * phase_v) * scale -> x2h (fp16, per-row
+// power-of-two scale) + rowscale; zeroes the row's y1 accumulator (y1 != null).
+template <int BIG, bool CL>
+__global__ void __launch_bounds__(kXMaxThreads, 1) xinput_rfft_kernel(
+    const void *x, int dtype, XPlan plan, const float2 *phase, float scale, __half *x2h, float *rowscale,
+    int n_pad, float *y1, int64_t m_local, XRowArgs ra) {
+  extern __shared__ float2 xsm[];
+  __shared__ XTw tw;
+  __shared__ float red[32];
+  __shared__ float slots[kXMaxCluster];
+  const int rank = CL ? static_cast<int>(blockIdx.x) : 0;
+  const int C = plan.C;
+  const int64_t row = xrow(ra, CL);
+  float2 *const b0 = xsm, *const b1 = xsm + xbuf_elems<float2>(plan.E);
+  pdl_launch_dependents();
+  build_xtw(tw, plan.N);
+  pdl_wait();  // x may be the previous kernel's output; y1 may still be read by it
+  if (y1) {
+    const int64_t z0 = m_local * rank / C, z1 = m_local * (rank + 1) / C;
+    for (int64_t i = z0 + threadIdx.x; i < z1; i += blockDim.x) y1[row * m_local + i] = 0.f;
+  }
+  const int N = plan.N;
+  auto gsrc_h = [&](int e) {
+    const uint32_t w = reinterpret_cast<const uint32_t *>(static_cast<const char *>(x) + row * 4 * N)[e];
+    const float2 z = dtype == QS_F16 ? __half22float2(*reinterpret_cast<const __half2 *>(&w))
+                                     : __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162 *>(&w));
+    return xcmul(z, phase[e]);
+  };
+  auto gsrc_f = [&](int e) {
+    return xcmul(reinterpret_cast<const float2 *>(static_cast<const char *>(x) + row * 8 * N)[e], phase[e]);
+  };
+  float amax = 0.f;
+  const int rb = xresult_buf(plan);
+  float2 *const rbuf = rb ? b1 : b0;
+  const XDst<float2, CL> res{rbuf, plan.cl};
+  auto sink = [&](int e, float2 z) {
+    z.x *= scale;
+    z.y *= scale;
+    amax = fmaxf(amax, fmaxf(fabsf(z.x), fabsf(z.y)));
+    res(e, z);
+  };
+  __syncthreads();  // twiddle tables (the first stage may use them)
+  if (dtype == QS_F32) xfft_row<BIG, CL>(plan, b0, b1, tw, false, rank, gsrc_f, sink);
+  else xfft_row<BIG, CL>(plan, b0, b1, tw, false, rank, gsrc_h, sink);
+  const float row_max = xgroup_absmax<CL>(amax, red, slots, rank, C);
+  float sc, inv;
+  xpow2_scale(row_max, sc, inv);
+  const float2 *mine = rbuf;
+  __half2 *out = reinterpret_cast<__half2 *>(x2h + row * n_pad);
+  for (int i = threadIdx.x; i < plan.E; i += blockDim.x) {
+    const float2 z = mine[xpad(i, float2())];
+    out[rank + C * i] = __floats2half2_rn(z.x * sc, z.y * sc);
+  }
+  if (rank == C - 1) {
+    for (int i = 2 * N + threadIdx.x; i < n_pad; i += blockDim.x) x2h[row * n_pad + i] = __float2half_rn(0.f);
+  }
+  if (rank == 0 && threadIdx.x == 0) rowscale[row] = inv;
+}
+
+// Output step, RFFT: y = IFFT(y1) * scale * conj(phase_u) + bias, cast.
+template <int BIG, bool CL>
+__global__ void __launch_bounds__(kXMaxThreads, 1) xoutput_rfft_kernel(
+    const float *y1, int64_t ld_y1, int64_t shards, int64_t batch, XPlan plan, const float2 *phase,
+    const float *bias, float scale, void *y, int dtype, XRowArgs ra) {
+  extern __shared__ float2 xsm[];
+  __shared__ XTw tw;
+  const int rank = CL ? static_cast<int>(blockIdx.x) : 0;
+  const int64_t row = xrow(ra, CL);
+  float2 *b0 = xsm, *b1 = xsm + xbuf_elems<float2>(plan.E);
+  const int N = plan.N;
+  const int64_t mp = 2 * static_cast<int64_t>(N) / shards;
+  pdl_launch_dependents();
+  build_xtw(tw, N);
+  pdl_wait();  // y1 comes from the matmul (or the all-gather)
+  auto gsrc = [&](int e) {
+    return *reinterpret_cast<const float2 *>(y1 + xy1_offset(row, 2 * e, ld_y1, shards, mp, batch));
+  };
+  auto sink = [&](int e, float2 z) {
+    z.x *= scale;
+    z.y *= scale;
+    z = xcmul(z, xconj(phase[e]));
+    if (bias) {
+      const float2 bb = reinterpret_cast<const float2 *>(bias)[e];
+      z.x += bb.x;
+      z.y += bb.y;
+    }
+    if (dtype == QS_F16) reinterpret_cast<__half2 *>(y)[row * N + e] = __floats2half2_rn(z.x, z.y);
+    else if (dtype == QS_BF16) reinterpret_cast<__nv_bfloat162 *>(y)[row * N + e] = __floats2bfloat162_rn(z.x, z.y);
+    else reinterpret_cast<float2 *>(y)[row * N + e] = z;
+  };
+  __syncthreads();  // twiddle tables
+  xfft_row<BIG, CL>(plan, b0, b1, tw, true, rank, gsrc, sink);
+  if constexpr (CL) cluster_sync();
+}
+
+// Standalone FWHT rows: y = FWHT(x * pre) * scale * post (pre / post optional).
+template <bool CL>
+__global__ void __launch_bounds__(kXMaxThreads, 1) xfwht_rows_kernel(
+    const void *x, int64_t ld_x, void *y, int64_t ld_y, int dtype, XPlan plan, const float *pre,
+    const float *post, float scale, XRowArgs ra) {
+  extern __shared__ float fsm_x[];
+  const int rank = CL ? static_cast<int>(blockIdx.x) : 0;
+  const int64_t row = xrow(ra, CL);
+  float *b0 = fsm_x, *b1 = fsm_x + xbuf_elems<float>(plan.E);
+  pdl_wait();  // launched with programmatic serialization: x may be the previous kernel's output
+  const int esz = dtype == QS_F32 ? 4 : 2;
+  const void *xr = static_cast<const char *>(x) + row * ld_x * esz;
+  void *yr = static_cast<char *>(y) + row * ld_y * esz;
+  auto gsrc = [&](int i) {
+    const float v = load_as_float(xr, i, dtype);
+    return pre ? v * pre[i] : v;
+  };
+  auto sink = [&](int i, float v) {
+    v *= scale;
+    if (post) v *= post[i];
+    store_from_float(yr, i, dtype, v);
+  };
+  xfwht_row<CL>(plan, b0, b1, rank, gsrc, sink);
+  if constexpr (CL) cluster_sync();
+}
+
+// Input step, RHT: x2 = FWHT(x * sv) * scale -> x2h + rowscale; zeroes y1.
+template <bool CL>
+__global__ void __launch_bounds__(kXMaxThreads, 1) xinput_rht_kernel(
+    const void *x, int dtype, XPlan plan, const float *sv, float scale, __half *x2h, float *rowscale, int n_pad,
+    float *y1, int64_t m_local, XRowArgs ra) {
+  extern __shared__ float fsm_x[];
+  __shared__ float red[32];
+  __shared__ float slots[kXMaxCluster];
+  const int rank = CL ? static_cast<int>(blockIdx.x) : 0;
+  const int C = plan.C;
+  const int64_t row = xrow(ra, CL);
+  const int n = plan.N;
+  float *const b0 = fsm_x, *const b1 = fsm_x + xbuf_elems<float>(plan.E);
+  pdl_launch_dependents();
+  pdl_wait();
+  if (y1) {
+    const int64_t z0 = m_local * rank / C, z1 = m_local * (rank + 1) / C;
+    for (int64_t i = z0 + threadIdx.x; i < z1; i += blockDim.x) y1[row * m_local + i] = 0.f;
+  }
+  auto gsrc = [&](int i) { return load_as_float(x, row * n + i, dtype) * sv[i]; };
+  float amax = 0.f;
+  const int rb = xresult_buf(plan);
+  float *const rbuf = rb ? b1 : b0;
+  const XDst<float, CL> res{rbuf, plan.cl};
+  auto sink = [&](int i, float v) {
+    v *= scale;
+    amax = fmaxf(amax, fabsf(v));
+    res(i, v);
+  };
+  xfwht_row<CL>(plan, b0, b1, rank, gsrc, sink);
+  const float row_max = xgroup_absmax<CL>(amax, red, slots, rank, C);
+  float sc, inv;
+  xpow2_scale(row_max, sc, inv);
+  const float *mine = rbuf;
+  for (int i = threadIdx.x; i < plan.E; i += blockDim.x)
+    x2h[row * n_pad + rank + C * i] = __float2half_rn(mine[xpad(i, float())] * sc);
+  if (rank == C - 1) {
+    for (int i = n + threadIdx.x; i < n_pad; i += blockDim.x) x2h[row * n_pad + i] = __float2half_rn(0.f);
+  }
+  if (rank == 0 && threadIdx.x == 0) rowscale[row] = inv;
+}
+
+// Output step, RHT: y = FWHT(y1) * scale * su + bias, cast.
+template <bool CL>
+__global__ void __launch_bounds__(kXMaxThreads, 1) xoutput_rht_kernel(
+    const float *y1, int64_t ld_y1, int64_t shards, int64_t batch, XPlan plan, const float *su, const float *bias,
+    float scale, void *y, int dtype, XRowArgs ra) {
+  extern __shared__ float fsm_x[];
+  const int rank = CL ? static_cast<int>(blockIdx.x) : 0;
+  const int64_t row = xrow(ra, CL);
+  const int m = plan.N;
+  const int64_t mp = m / shards;
+  float *b0 = fsm_x, *b1 = fsm_x + xbuf_elems<float>(plan.E);
+  pdl_launch_dependents();
+  pdl_wait();
+  auto gsrc = [&](int i) { return y1[xy1_offset(row, i, ld_y1, shards, mp, batch)]; };
+  auto sink = [&](int i, float v) {
+    v = v * scale * su[i];
+    if (bias) v += bias[i];
+    store_from_float(y, row * m + i, dtype, v);
+  };
+  xfwht_row<CL>(plan, b0, b1, rank, gsrc, sink);
+  if constexpr (CL) cluster_sync();
+}
+
+// ---- host launchers (instantiated per big prime in qs_xform_*.cu) ------------------
+struct XLaunch {
+  int threads;
+  size_t smem;
+  int64_t rows;
+};
+
+template <int BIG, bool CL>
+int run_xrfft_rows(const XLaunch &L, cudaStream_t s, int inverse, const void *x, int64_t ld_x, void *y,
+                   int64_t ld_y, int dtype, const XPlan &p, const float2 *phase, float scale);
+template <int BIG, bool CL>
+int run_xinput_rfft(const XLaunch &L, cudaStream_t s, const void *x, int dtype, const XPlan &p, const float2 *phase,
+                    float scale, __half *x2h, float *rowscale, int n_pad, float *y1, int64_t m_local);
+template <int BIG, bool CL>
+int run_xoutput_rfft(const XLaunch &L, cudaStream_t s, const float *y1, int64_t ld_y1, int64_t shards,
+                     int64_t batch, const XPlan &p, const float2 *phase, const float *bias, float scale, void *y,
+                     int dtype);
+template <bool CL>
+int run_xfwht_rows(const XLaunch &L, cudaStream_t s, const void *x, int64_t ld_x, void *y, int64_t ld_y, int dtype,
+                   const XPlan &p, const float *pre, const float *post, float scale);
+template <bool CL>
+int run_xinput_rht(const XLaunch &L, cudaStream_t s, const void *x, int dtype, const XPlan &p, const float *sv,
+                   float scale, __half *x2h, float *rowscale, int n_pad, float *y1, int64_t m_local);
+template <bool CL>
+int run_xoutput_rht(const XLaunch &L, cudaStream_t s, const float *y1, int64_t ld_y1, int64_t shards,
+                    int64_t batch, const XPlan &p, const float *su, const float *bias, float scale, void *y,
+                    int dtype);
+
+template <typename... KArgs, typename... Args>
+cudaError_t xlaunch_ex(const cudaLaunchConfig_t &cfg, void (*kern)(KArgs...), Args... args) {
+  return cudaLaunchKernelEx(&cfg, kern, static_cast<KArgs>(args)...);
+}
+
+// Launches `kern` over L.rows rows (grid chunks of at most 65535 rows along y
+// for clusters) with programmatic stream serialization, and a (C, 1, 1)
+// cluster when CL.
+template <bool CL, typename... KArgs, typename... Args>
+int xlaunch(const char *what, void (*kern)(KArgs...), const XLaunch &L, int C, cudaStream_t s, Args... args) {
+  QS_CUDA_TRY(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(L.smem)));
+  if (CL && C > 8) QS_CUDA_TRY(cudaFuncSetAttribute(kern, cudaFuncAttributeNonPortableClusterSizeAllowed, 1));
+  const int64_t chunk = CL ? 65535 : (int64_t(1) << 31) - 1;
+  for (int64_t r0 = 0; r0 < L.rows; r0 += chunk) {
+    const int64_t nr = L.rows - r0 < chunk ? L.rows - r0 : chunk;
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = CL ? dim3(C, static_cast<unsigned>(nr)) : dim3(static_cast<unsigned>(nr));
+    cfg.blockDim = dim3(L.threads);
+    cfg.dynamicSmemBytes = L.smem;
+    cfg.stream = s;
+    cudaLaunchAttribute attr[2];
+    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[0].val.programmaticStreamSerializationAllowed = 1;
+    int na = 1;
+    if (CL) {
+      attr[1].id = cudaLaunchAttributeClusterDimension;
+      attr[1].val.clusterDim.x = C;
+      attr[1].val.clusterDim.y = 1;
+      attr[1].val.clusterDim.z = 1;
+      na = 2;
+    }
+    cfg.attrs = attr;
+    cfg.numAttrs = na;
+    XRowArgs ra{r0, C};
+    const cudaError_t e = xlaunch_ex(cfg, kern, args..., ra);
+    if (e != cudaSuccess) return fail(QS_ERR_CUDA, "%s launch failed: %s", what, cudaGetErrorString(e));
+  }
+  return QS_OK;
+}
+
+#define QS_DEFINE_XFFT_RUNNERS(BIG, CL)                                                                        \
+  template <>                                                                                                  \
+  int run_xrfft_rows<BIG, CL>(const XLaunch &L, cudaStream_t s, int inverse, const void *x, int64_t ld_x,     \
+                              void *y, int64_t ld_y, int dtype, const XPlan &p, const float2 *phase,           \
+                              float scale) {                                                                   \
+    return xlaunch<CL>("rfft", xrfft_rows_kernel<BIG, CL>, L, p.C, s, inverse, x, ld_x, y, ld_y, dtype, p,    \
+                       phase, scale);                                                                          \
+  }                                                                                                            \
+  template <>                                                                                                  \
+  int run_xinput_rfft<BIG, CL>(const XLaunch &L, cudaStream_t s, const void *x, int dtype, const XPlan &p,     \
+                               const float2 *phase, float scale, __half *x2h, float *rowscale, int n_pad,      \
+                               float *y1, int64_t m_local) {                                                   \
+    return xlaunch<CL>("linear_input_rfft", xinput_rfft_kernel<BIG, CL>, L, p.C, s, x, dtype, p, phase,       \
+                       scale, x2h, rowscale, n_pad, y1, m_local);                                              \
+  }                                                                                                            \
+  template <>                                                                                                  \
+  int run_xoutput_rfft<BIG, CL>(const XLaunch &L, cudaStream_t s, const float *y1, int64_t ld_y1,             \
+                                int64_t shards, int64_t batch, const XPlan &p, const float2 *phase,            \
+                                const float *bias, float scale, void *y, int dtype) {                          \
+    return xlaunch<CL>("linear_output_rfft", xoutput_rfft_kernel<BIG, CL>, L, p.C, s, y1, ld_y1, shards,      \
+                       batch, p, phase, bias, scale, y, dtype);                                                \
+  }
+
+#define QS_DEFINE_XFWHT_RUNNERS(CL)                                                                            \
+  template <>                                                                                                  \
+  int run_xfwht_rows<CL>(const XLaunch &L, cudaStream_t s, const void *x, int64_t ld_x, void *y,              \
+                         int64_t ld_y, int dtype, const XPlan &p, const float *pre, const float *post,         \
+                         float scale) {                                                                        \
+    return xlaunch<CL>("fwht", xfwht_rows_kernel<CL>, L, p.C, s, x, ld_x, y, ld_y, dtype, p, pre, post,       \
+                       scale);                                                                                 \
+  }                                                                                                            \
+  template <>                                                                                                  \
+  int run_xinput_rht<CL>(const XLaunch &L, cudaStream_t s, const void *x, int dtype, const XPlan &p,           \
+                         const float *sv, float scale, __half *x2h, float *rowscale, int n_pad, float *y1,     \
+                         int64_t m_local) {                                                                    \
+    return xlaunch<CL>("linear_input_rht", xinput_rht_kernel<CL>, L, p.C, s, x, dtype, p, sv, scale, x2h,     \
+                       rowscale, n_pad, y1, m_local);                                                          \
+  }                                                                                                            \
+  template <>                                                                                                  \
+  int run_xoutput_rht<CL>(const XLaunch &L, cudaStream_t s, const float *y1, int64_t ld_y1, int64_t shards,   \
+                          int64_t batch, const XPlan &p, const float *su, const float *bias, float scale,      \
+                          void *y, int dtype) {                                                                \
+    return xlaunch<CL>("linear_output_rht", xoutput_rht_kernel<CL>, L, p.C, s, y1, ld_y1, shards, batch, p,   \
+                       su, bias, scale, y, dtype);                                                             \
+  }
+
+#define QS_FOR_EACH_XBIG(X) X(0) X(11) X(13) X(17) X(19) X(23) X(29) X(31) X(37) X(41) X(43)
+
+}  // namespace qs

@@ -60,10 +60,12 @@ def test_rfft_golden(golden, n):
     assert rel_l2(from_transformed_space(x, ph).cpu().numpy(), golden[f"rfft_from_{n}"]) < 5e-6
 
 
-# half-lengths covering every radix path: primes 11..43 (ping-pong), 3/5/7,
-# powers of two, and the in-place path for half-lengths above 12288
+# half-lengths covering every radix: primes 11..43, 3/5/7, powers of two,
+# lengths whose two row buffers need a cluster of CTAs even for many rows
+# (above 12800 points), and the largest supported length (32768)
 @pytest.mark.parametrize("n", [22, 26, 34, 38, 46, 58, 62, 74, 82, 86, 30, 98, 250, 1792, 3584, 5504 * 2,
-                               9472 * 2, 2 * 14336, 2 * 16384, 2 * 12288, 2 * 4096 * 3])
+                               9472 * 2, 2 * 14336, 2 * 16384, 2 * 12288, 2 * 4096 * 3, 2 * 43 * 512,
+                               2 * 32768])
 def test_rfft_sizes_vs_oracle(n):
     from quipsharp_b200.rfft import to_transformed_space, from_transformed_space
     g = torch.Generator().manual_seed(n)
@@ -77,6 +79,29 @@ def test_rfft_sizes_vs_oracle(n):
     # round trip (tests/test_rfft.py:11-19 of the reference)
     rt = from_transformed_space(to_transformed_space(x.to(DEV), ph.to(DEV)), ph.to(DEV)).cpu().numpy()
     assert rel_l2(rt, x.numpy()) < 5e-6
+
+
+# Many rows: one CTA per row (or a 2-CTA cluster for the largest rows) instead
+# of a cluster per row.
+@pytest.mark.parametrize("n", [3584, 11008, 18944, 8192, 2 * 14336, 2 * 43 * 512])
+def test_rfft_many_rows_vs_oracle(n):
+    from quipsharp_b200.rfft import to_transformed_space, from_transformed_space
+    g = torch.Generator().manual_seed(n + 1)
+    x = torch.randn(300, n, generator=g)
+    th = torch.rand(n // 2, generator=g) * 6.283185307179586
+    ph = torch.polar(torch.ones_like(th), th)
+    fw = to_transformed_space(x.to(DEV), ph.to(DEV)).cpu().numpy()
+    assert rel_l2(fw, O.rfft_to_transformed(x.numpy(), ph.numpy())) < 5e-6
+    bw = from_transformed_space(x.to(DEV), ph.to(DEV)).cpu().numpy()
+    assert rel_l2(bw, O.rfft_from_transformed(x.numpy(), ph.numpy())) < 5e-6
+
+
+@pytest.mark.parametrize("n", [32, 4096, 32768])
+def test_fwht_many_rows_vs_oracle(n):
+    from quipsharp_b200.hadamard import fwht
+    g = torch.Generator().manual_seed(n + 2)
+    x = torch.randn(300, n, generator=g)
+    assert rel_l2(fwht(x.to(DEV)).cpu().numpy(), O.fwht(x.numpy())) < 1e-6
 
 
 def test_rfft_unsupported_and_errors():
