@@ -54,6 +54,18 @@ static int wanted_cluster(int N, int elem_bytes, int64_t rows, int latency_point
   return C;
 }
 
+// Largest power-of-two radix (log2) of a plan.  Many rows: `cap` (few stages,
+// each thread a long independent chain; other rows fill the SM).  Few rows:
+// small enough that every stage still has kXLatencyTasks butterflies per CTA,
+// so the SM runs several warps per scheduler while one row is in flight.
+constexpr int kXLatencyTasks = 256;
+static int max_radix_log(int N, int C, int64_t rows, int cap) {
+  if (rows * 2 > xnum_sms()) return cap;
+  int w = 1;
+  while (w < cap && (N / C) >> (w + 1) >= kXLatencyTasks) ++w;
+  return w;
+}
+
 // Fixes C (at most `want`, a power of two dividing every stage's butterfly
 // count, so each butterfly's inputs sit in one CTA), then the per-CTA task
 // counts and the launch shape.
@@ -120,7 +132,7 @@ static int make_fft_plan(int64_t N64, int64_t rows, XPlan &p, XLaunch &L) {
   if (rem != 1) return fail(QS_ERR_UNSUPPORTED, "FFT length %lld has a prime factor above 43", (long long)N);
   const int want = wanted_cluster(N, 8, rows, kXLatencyPointsFft);
   if (a > 0) {
-    const int maxlog = want > 1 ? 3 : 4;
+    const int maxlog = max_radix_log(N, want, rows, 4);
     const int ns = (a + maxlog - 1) / maxlog, base = a / ns, extra = a % ns;
     if (nr + ns >= kXMaxStages) return fail(QS_ERR_UNSUPPORTED, "FFT plan too deep");
     for (int i = 0; i < ns; ++i) radix[nr++] = 1 << (base + (i < extra ? 1 : 0));
@@ -157,7 +169,7 @@ static int make_fwht_plan(int64_t n, int64_t rows, XPlan &p, XLaunch &L) {
   if (Lb == 0) {
     widths[np++] = 0;
   } else {
-    const int maxw = want > 1 ? 3 : 5;
+    const int maxw = max_radix_log(static_cast<int>(n), want, rows, 5);
     const int ns = (Lb + maxw - 1) / maxw, base = Lb / ns, extra = Lb % ns;
     for (int i = 0; i < ns; ++i) widths[np++] = base + (i < extra ? 1 : 0);
   }

@@ -623,6 +623,21 @@ __device__ __forceinline__ void xpow2_scale(float amax, float &scale, float &inv
   inv = ldexpf(1.f, e - 12);
 }
 
+// Zeroes floats [z0, z1) of row `row` of the (rows, m) matrix y1 with this
+// CTA's threads (16-byte stores when the row is 16-byte aligned).
+__device__ __forceinline__ void xzero_row(float *y1, int64_t row, int64_t m, int64_t z0, int64_t z1) {
+  float *r = y1 + row * m;
+  if ((m & 3) == 0 && (reinterpret_cast<uintptr_t>(y1) & 15) == 0) {
+    const int v0 = static_cast<int>((z0 + 3) >> 2), v1 = static_cast<int>(z1 >> 2);
+    float4 *r4 = reinterpret_cast<float4 *>(r);
+    for (int i = v0 + threadIdx.x; i < v1; i += blockDim.x) r4[i] = make_float4(0.f, 0.f, 0.f, 0.f);
+    for (int i = static_cast<int>(z0) + threadIdx.x; i < v0 * 4 && i < z1; i += blockDim.x) r[i] = 0.f;
+    for (int i = v1 * 4 + threadIdx.x; i < z1; i += blockDim.x) r[i] = 0.f;
+  } else {
+    for (int i = static_cast<int>(z0) + threadIdx.x; i < z1; i += blockDim.x) r[i] = 0.f;
+  }
+}
+
 // Offset of y1 element (row, col): plain row-major with stride ld_y1 when
 // shards == 1, else the rank-major layout of an all-gather of `shards` column
 // blocks of (batch, mp): ((col / mp) * batch + row) * mp + col % mp.
@@ -693,20 +708,17 @@ __global__ void __launch_bounds__(kXMaxThreads, 1) xinput_rfft_kernel(
   pdl_launch_dependents();
   build_xtw(tw, plan.N);
   pdl_wait();  // x may be the previous kernel's output; y1 may still be read by it
-  if (y1) {
-    const int64_t z0 = m_local * rank / C, z1 = m_local * (rank + 1) / C;
-    for (int64_t i = z0 + threadIdx.x; i < z1; i += blockDim.x) y1[row * m_local + i] = 0.f;
-  }
+  if (y1) xzero_row(y1, row, m_local, m_local * rank / C, m_local * (rank + 1) / C);
   const int N = plan.N;
+  const uint32_t *xh = reinterpret_cast<const uint32_t *>(static_cast<const char *>(x) + row * 4 * N);
+  const float2 *xf = reinterpret_cast<const float2 *>(static_cast<const char *>(x) + row * 8 * N);
   auto gsrc_h = [&](int e) {
-    const uint32_t w = reinterpret_cast<const uint32_t *>(static_cast<const char *>(x) + row * 4 * N)[e];
+    const uint32_t w = xh[e];
     const float2 z = dtype == QS_F16 ? __half22float2(*reinterpret_cast<const __half2 *>(&w))
                                      : __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162 *>(&w));
     return xcmul(z, phase[e]);
   };
-  auto gsrc_f = [&](int e) {
-    return xcmul(reinterpret_cast<const float2 *>(static_cast<const char *>(x) + row * 8 * N)[e], phase[e]);
-  };
+  auto gsrc_f = [&](int e) { return xcmul(xf[e], phase[e]); };
   float amax = 0.f;
   const int rb = xresult_buf(plan);
   float2 *const rbuf = rb ? b1 : b0;
@@ -812,10 +824,7 @@ __global__ void __launch_bounds__(kXMaxThreads, 1) xinput_rht_kernel(
   float *const b0 = fsm_x, *const b1 = fsm_x + xbuf_elems<float>(plan.E);
   pdl_launch_dependents();
   pdl_wait();
-  if (y1) {
-    const int64_t z0 = m_local * rank / C, z1 = m_local * (rank + 1) / C;
-    for (int64_t i = z0 + threadIdx.x; i < z1; i += blockDim.x) y1[row * m_local + i] = 0.f;
-  }
+  if (y1) xzero_row(y1, row, m_local, m_local * rank / C, m_local * (rank + 1) / C);
   auto gsrc = [&](int i) { return load_as_float(x, row * n + i, dtype) * sv[i]; };
   float amax = 0.f;
   const int rb = xresult_buf(plan);
