@@ -3,16 +3,19 @@
 //
 // CTA tile: 128 weight rows (M, TMEM lanes) x 256 tokens (N, TMEM columns),
 // K in steps of 64 input features (one 128-byte swizzled row per operand row).
-// Warp roles (192 threads):
+// Warp roles (64 + 128 G threads, G decode groups: 4 for one-stage codebooks,
+// 2 for two-stage RVQ):
 //   warp 0      TMA producer: the activation tile (256 tokens x 64 fp16) of each
 //               K step into a 4- (3-) stage ring, 128-byte swizzle;
 //   warp 1      allocates TMEM; lane 0 issues tcgen05.mma (M=128, N=256, K=16,
 //               fp16 x fp16 -> fp32) and tcgen05.commit to free ring stages;
-//   warps 2..5  decode: thread r decodes weight row r of the tile for each K step
-//               (8 codes, read from the same packed stream as the decode-regime
-//               kernel) into the A tile of the ring stage, in the UMMA
-//               K-major 128-byte-swizzle layout; then the epilogue: TMEM ->
-//               registers -> scales -> y1 (float32, coalesced per token).
+//   warps 2..   decode, in G groups of four warps taking alternate K steps:
+//               thread r of a group decodes weight row r of the tile (8 codes,
+//               read from the same packed stream as the decode-regime kernel)
+//               into the A tile of the ring stage, in the UMMA K-major
+//               128-byte-swizzle layout; then the epilogue, each group over
+//               1/G of the token columns: TMEM -> registers -> scales -> y1
+//               (float32, coalesced per token).
 // Decoded weights are exact in fp16 (the E8P shift is added with an f16x2 add),
 // RVQ stages accumulate in separate TMEM accumulators and meet their float32
 // stage scales in the epilogue.  Every mbarrier wait is bounded: on timeout the
@@ -34,14 +37,20 @@ namespace {
 constexpr int kBM = 128;
 constexpr int kBN = 256;
 constexpr int kBK = 64;
-constexpr int kThreads = 192;
 constexpr int kATile = kBM * kBK * 2;  // 16 KB
 constexpr int kBTile = kBN * kBK * 2;  // 32 KB
 constexpr uint64_t kWaitLimitNs = 4000000000ull;  // 4 s: far beyond any legitimate wait
 
+// Ring stages and decode groups.  A decode group waiting for the MMA to free
+// stage s for its K step ks relies on the MMA having consumed ks - 2S already
+// (otherwise the parity wait could pass one phase early); its own previous
+// wait, at ks - G, guarantees consumption of ks - G - S, so G <= S is required.
 template <int NST>
 struct Cfg {
   static constexpr int stages = NST == 1 ? 4 : 3;
+  static constexpr int groups = NST == 1 ? 4 : 2;  // <= stages, divides the 4 K steps of a code chunk
+  static constexpr int threads = 64 + 128 * groups;
+  static_assert(groups <= stages && 4 % groups == 0, "decode groups vs ring stages");
   static constexpr int stage_bytes = NST * kATile + kBTile;
   static constexpr int ring_bytes = stages * stage_bytes;
   static constexpr int tables_bytes = 2 * 256 * 8;
@@ -99,47 +108,48 @@ __device__ __forceinline__ void decode_1bit_row(const uint2 &q, const uint2 *tbl
   }
 }
 
-// Per-row codes of one 32-code chunk (4 K steps) of a stage: a 16-byte quad per
-// K step for E8P, 8 index bytes per K step for 1-bit.
-template <int K>
+// Per-row codes of one decode group's K steps within a 32-code chunk (4 K
+// steps; group dg of G takes steps dg, dg + G, ...): a 16-byte quad per K step
+// for E8P, 8 index bytes per K step for 1-bit.
+template <int K, int SPG>
 struct RowChunk;
-template <>
-struct RowChunk<QS_CB_E8P> {
-  uint4 q[4];
+template <int SPG>
+struct RowChunk<QS_CB_E8P, SPG> {
+  uint4 q[SPG];
 };
-template <>
-struct RowChunk<QS_CB_E8_1BIT> {
-  uint2 q[4];
+template <int SPG>
+struct RowChunk<QS_CB_E8_1BIT, SPG> {
+  uint2 q[SPG];
 };
 
-template <int K>
-__device__ __forceinline__ void load_row_chunk(const uint8_t *stage, int64_t RT, int64_t kc, int64_t R,
-                                               bool valid, RowChunk<K> &rc) {
+template <int K, int G>
+__device__ __forceinline__ void load_row_chunk(const uint8_t *stage, int64_t RT, int64_t kc, int64_t R, int dg,
+                                               bool valid, RowChunk<K, 4 / G> &rc) {
   const int64_t rtg = R >> 4, rr = R & 15, half = rr >> 3, g = rr & 7;
   if constexpr (K == QS_CB_E8P) {
     const uint8_t *p = stage + (kc * RT + rtg) * 1024 + half * 512 + g * 64;
 #pragma unroll
-    for (int t = 0; t < 4; ++t) rc.q[t] = valid ? ldg_nc_v4(p + 16 * t) : make_uint4(0u, 0u, 0u, 0u);
+    for (int u = 0; u < 4 / G; ++u) rc.q[u] = valid ? ldg_nc_v4(p + 16 * (dg + G * u)) : make_uint4(0u, 0u, 0u, 0u);
   } else {
     const uint8_t *p = stage + (kc * RT + rtg) * 512 + g * 64 + half * 8;
 #pragma unroll
-    for (int t = 0; t < 4; ++t)
-      rc.q[t] = valid ? __ldg(reinterpret_cast<const uint2 *>(p + 16 * t)) : make_uint2(0u, 0u);
+    for (int u = 0; u < 4 / G; ++u)
+      rc.q[u] = valid ? __ldg(reinterpret_cast<const uint2 *>(p + 16 * (dg + G * u))) : make_uint2(0u, 0u);
   }
 }
 
-template <int K>
-__device__ __forceinline__ void decode_row(const RowChunk<K> &rc, int t, const uint2 *tbl_e8p,
+template <int K, int SPG>
+__device__ __forceinline__ void decode_row(const RowChunk<K, SPG> &rc, int t, const uint2 *tbl_e8p,
                                            const uint2 *tbl_1b, uint8_t *arow, int rsw) {
   if constexpr (K == QS_CB_E8P) decode_e8p_row(rc.q[t], tbl_e8p, arow, rsw);
   else decode_1bit_row(rc.q[t], tbl_1b, arow, rsw);
 }
 
 template <int K0, int K1, int NST>
-__global__ void __launch_bounds__(kThreads, 1) gemm_tc_kernel(const __grid_constant__ CUtensorMap tmap_x,
+__global__ void __launch_bounds__(Cfg<NST>::threads, 1) gemm_tc_kernel(const __grid_constant__ CUtensorMap tmap_x,
                                                                TcArgs a) {
   using C = Cfg<NST>;
-  constexpr int S = C::stages;
+  constexpr int S = C::stages, G = C::groups, SPG = 4 / G;
   extern __shared__ __align__(1024) uint8_t dsm[];
   pdl_launch_dependents();
   // 1024-byte aligned ring (the swizzle atom); tables and barriers after it.
@@ -230,25 +240,26 @@ __global__ void __launch_bounds__(kThreads, 1) gemm_tc_kernel(const __grid_const
       sm100::umma_commit(acc_full);
     }
   } else {
-    // ---- decode producers (128 threads, thread r <-> tile row r)
-    const int r = threadIdx.x - 64;
+    // ---- decode producers (group dg of 128 threads, thread r <-> tile row r)
+    const int dg = (warp - 2) >> 2;
+    const int r = (threadIdx.x - 64) & 127;
     const int64_t R = m0 + r;
     const bool valid = R < a.m_pad;
     const int rsw = r & 7;
-    RowChunk<K0> c0, n0c;
-    RowChunk<K1> c1, n1c;
-    load_row_chunk<K0>(a.stage[0], a.RT, 0, R, valid, c0);
-    if constexpr (NST == 2) load_row_chunk<K1>(a.stage[1], a.RT, 0, R, valid, c1);
+    RowChunk<K0, SPG> c0, n0c;
+    RowChunk<K1, SPG> c1, n1c;
+    load_row_chunk<K0, G>(a.stage[0], a.RT, 0, R, dg, valid, c0);
+    if constexpr (NST == 2) load_row_chunk<K1, G>(a.stage[1], a.RT, 0, R, dg, valid, c1);
     const int rowoff = (r >> 3) * 1024 + (r & 7) * 128;
     bool ok = true;
     for (int kc = 0; kc < K / 4 && ok; ++kc) {  // one 32-code chunk = 4 K steps
       if (kc + 1 < K / 4) {  // prefetch the next chunk's codes
-        load_row_chunk<K0>(a.stage[0], a.RT, kc + 1, R, valid, n0c);
-        if constexpr (NST == 2) load_row_chunk<K1>(a.stage[1], a.RT, kc + 1, R, valid, n1c);
+        load_row_chunk<K0, G>(a.stage[0], a.RT, kc + 1, R, dg, valid, n0c);
+        if constexpr (NST == 2) load_row_chunk<K1, G>(a.stage[1], a.RT, kc + 1, R, dg, valid, n1c);
       }
 #pragma unroll
-      for (int t = 0; t < 4; ++t) {
-        const int ks = kc * 4 + t, s = ks % S, use = ks / S;
+      for (int t = 0; t < SPG; ++t) {
+        const int ks = kc * 4 + dg + G * t, s = ks % S, use = ks / S;
         if (use > 0 && !sm100::mbar_wait_bounded(empty(s), (use - 1) & 1, kWaitLimitNs)) {
           set_error();
           ok = false;
@@ -266,11 +277,12 @@ __global__ void __launch_bounds__(kThreads, 1) gemm_tc_kernel(const __grid_const
     // ---- epilogue
     if (ok && sm100::mbar_wait_bounded(acc_full, 0, kWaitLimitNs)) {
       sm100::tc_fence_after_sync();
-      const int quarter = warp & 3;
+      const int quarter = warp & 3;  // TMEM lanes this warp may read
       const int64_t row = m0 + quarter * 32 + lane;
       const uint32_t lane_addr = tmem + (static_cast<uint32_t>(quarter * 32) << 16);
       const float ls = *a.layer_scale;
-      for (int c = 0; c < kBN; c += 16) {
+      constexpr int cols = kBN / G;
+      for (int c = dg * cols; c < (dg + 1) * cols; c += 16) {
         uint32_t v0[16], v1[16];
         sm100::tmem_ld_16(lane_addr + c, v0);
         if constexpr (NST == 2) sm100::tmem_ld_16(lane_addr + kBN + c, v1);
@@ -333,7 +345,7 @@ int run_gemm(const CUtensorMap &map, const TcArgs &a, cudaStream_t s) {
   auto kern = gemm_tc_kernel<K0, K1, NST>;
   QS_CUDA_TRY(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, C::smem_bytes));
   const dim3 grid(static_cast<unsigned>(ceil_div(a.m, kBM)), static_cast<unsigned>(ceil_div(a.batch, kBN)));
-  return launch_pdl("gemm_tc", kern, grid, dim3(kThreads), C::smem_bytes, s, map, a);
+  return launch_pdl("gemm_tc", kern, grid, dim3(C::threads), C::smem_bytes, s, map, a);
 }
 
 }  // namespace
