@@ -30,6 +30,10 @@ sys.path.insert(0, ROOT)
 
 L2_BYTES = 126 * 1024 * 1024
 
+# dram__bytes_read.sum + dram__bytes_write.sum per launch of the fused decode+matmul
+# kernel, from the ncu capture summarised in profiles/gemv_c2_b1.md
+NCU_TRAFFIC = {("c2_rvq3_4096to11008", 1): 16.98688e6}
+
 
 def parse():
     p = argparse.ArgumentParser()
@@ -364,11 +368,9 @@ def run_ours(args):
     else:
         gb = sum(gemv_bytes(m, n, kinds, B) for _, m, n in layers)
         achieved = gb * mm_steps * R * L / (ms_mm / 1e3) / 1e9
-        traffic = None
-        tfile = os.path.join(ROOT, "profiles", f"traffic_{args.config}_b{B}.json")
-        if os.path.exists(tfile):
-            with open(tfile) as f:
-                traffic = json.load(f).get("dram_bytes_per_launch")
+        # DRAM bytes per launch of the dominant kernel from an ncu capture of this
+        # workload (profiles/gemv_c2_b1.md); other workloads have none yet
+        traffic = NCU_TRAFFIC.get((args.config, B))
         roofline = {"bound": "hbm", "achieved": achieved, "peak": hbm_peak, "unit": "GB/s",
                     "frac": achieved / hbm_peak, "traffic": traffic,
                     "kernel": "qs::gemv_kernel (fused decode + mma.sync matmul)",
