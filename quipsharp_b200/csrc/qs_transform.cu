@@ -43,9 +43,14 @@ static size_t plan_smem(int N, int C, int elem_bytes) {
 constexpr int kXLatencyPointsFft = 2048;
 constexpr int kXLatencyPointsFwht = 4096;
 
+// Few rows: the rows alone cannot fill the SMs; plans minimise one row's latency.
+static bool few_rows(int64_t rows) { return rows * 2 <= xnum_sms(); }
+
 // CTAs per row wanted before the stages are known: the fewest whose share of
-// the two row buffers fits kXSmemCap; then, while the rows alone leave SMs
-// idle, doubled until each CTA's share is at most `latency_points` (<= 16).
+// the two row buffers fits kXSmemCap (a cluster across SMs costs a many-row
+// transform more in barriers and remote stores than it gains); then, while the
+// rows alone leave SMs idle, doubled (up to 16) while each CTA's share is above
+// `latency_points`.
 static int wanted_cluster(int N, int elem_bytes, int64_t rows, int latency_points) {
   int C = 1;
   while (plan_smem(N, C, elem_bytes) > kXSmemCap && C < kXMaxCluster) C *= 2;
@@ -60,7 +65,7 @@ static int wanted_cluster(int N, int elem_bytes, int64_t rows, int latency_point
 // so the SM runs several warps per scheduler while one row is in flight.
 constexpr int kXLatencyTasks = 256;
 static int max_radix_log(int N, int C, int64_t rows, int cap) {
-  if (rows * 2 > xnum_sms()) return cap;
+  if (!few_rows(rows)) return cap;
   int w = 1;
   while (w < cap && (N / C) >> (w + 1) >= kXLatencyTasks) ++w;
   return w;
@@ -85,9 +90,9 @@ static int finish_plan(XPlan &p, XLaunch &L, int elem_bytes, int64_t rows, int w
   int most = 128;
   for (int s = 0; s < p.nst; ++s) {
     XStage &S = p.st[s];
-    // odd radices: one output pair per task in cluster (compact) kernels,
-    // groups of up to six pairs in one-CTA kernels
-    if ((S.R & 1) && S.R > 1) S.G = C > 1 ? (S.R - 1) / 2 : xodd_groups(S.R);
+    // odd radices: one output pair per task (compact rolled code) for few
+    // rows across a cluster, else groups of up to six pairs (unrolled code)
+    if ((S.R & 1) && S.R > 1) S.G = C > 1 && few_rows(rows) ? (S.R - 1) / 2 : xodd_groups(S.R);
     S.nbC = S.nb / C;
     S.dnbC = make_fastdiv(static_cast<uint32_t>(S.nbC));
     most = std::max(most, S.nbC * S.G);

@@ -406,7 +406,7 @@ __device__ __forceinline__ void xodd_pair_compact(int g, const XStage &S, const 
 }
 
 // Odd-prime stage: task t = g * nbC + i (output group g of butterfly
-// j = rank + C * i; COMPACT: output pair g + 1, G = (P - 1) / 2 groups);
+// j = rank + C * i; compact plans: output pair g + 1, G = (P - 1) / 2 groups);
 // tasks of a warp share g except at group boundaries.
 template <int P, bool COMPACT, typename Src, typename Dst>
 __device__ __forceinline__ void xstage_odd(const XStage &S, const Src &src, const Dst &dst, const XTw &tw,
@@ -423,7 +423,10 @@ __device__ __forceinline__ void xstage_odd(const XStage &S, const Src &src, cons
       w1 = xtw(tw, k * S.twstep, inverse);
       wP = xtw(tw, k * S.twstep * P, inverse);
     }
-    if constexpr (COMPACT) xodd_pair_compact<P>(g, S, src, dst, j, k, w1, wP, tw_on, inverse);
+    // compact (one output pair per task, G = (P - 1) / 2) only in cluster
+    // kernels and only when the plan asks for it (few rows); G tells them apart
+    // for every prime with more than one output pair
+    if (COMPACT && S.G == (P - 1) / 2 && P > 3) xodd_pair_compact<P>(g, S, src, dst, j, k, w1, wP, tw_on, inverse);
     else xodd_dispatch<P, 0>(g, S, src, dst, j, k, w1, wP, tw_on, inverse);
   }
 }
