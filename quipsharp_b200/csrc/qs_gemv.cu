@@ -91,12 +91,14 @@ __device__ __forceinline__ void shift_words(uint32_t w3, uint32_t (&sw)[4]) {
   for (int p = 0; p < 4; ++p) sw[p] = 0x34003400u ^ (imul(y, 1u << (2 * p)) & 0x80008000u);
 }
 
-// One stage of one item: 8 codes for each of the lane's two rows (16 mma),
-// plus 2 mma for the E8P shifts against the per-code activation sums sf.
-template <int KIND>
+// One stage of one item: 8 codes for each of the lane's two rows (16 mma per
+// token group), plus 2 mma per token group for the E8P shifts against the
+// per-code activation sums sf.  Each decoded fragment feeds all NTG groups.
+template <int KIND, int NTG>
 __device__ __forceinline__ void stage_item(const uint8_t *tbl, uint32_t off_e8p, uint32_t off_1b, const uint4 &qa,
-                                           const uint4 &qb, const uint32_t (&bf)[32],
-                                           const uint32_t (&sf)[4], float (&acc)[4], float (&acc2)[4]) {
+                                           const uint4 &qb, const uint32_t (&bf)[NTG][32],
+                                           const uint32_t (&sf)[NTG][4], float (&acc)[NTG][4],
+                                           float (&acc2)[NTG][4]) {
   if constexpr (KIND == QS_CB_E8P) {
     const uint32_t floa = qa.z ^ imul(qa.z, 256u), flob = qb.z ^ imul(qb.z, 256u);
     const uint32_t fhia = (qa.w & 0x00FFFFFFu) ^ shf_l_wrap(qa.z, qa.w, 8);
@@ -106,14 +108,20 @@ __device__ __forceinline__ void stage_item(const uint8_t *tbl, uint32_t off_e8p,
       uint32_t Wa[4], Wb[4];
       e8p_words(tbl, off_e8p, c < 4 ? qa.x : qa.y, c & 3, imul(floa, 1u << c), imul(fhia, 1u << c), Wa);
       e8p_words(tbl, off_e8p, c < 4 ? qb.x : qb.y, c & 3, imul(flob, 1u << c), imul(fhib, 1u << c), Wb);
-      mma_16816(acc, Wa[0], Wb[0], Wa[1], Wb[1], bf[4 * c + 0], bf[4 * c + 1]);
-      mma_16816(acc2, Wa[2], Wb[2], Wa[3], Wb[3], bf[4 * c + 2], bf[4 * c + 3]);
+#pragma unroll
+      for (int tg = 0; tg < NTG; ++tg) {
+        mma_16816(acc[tg], Wa[0], Wb[0], Wa[1], Wb[1], bf[tg][4 * c + 0], bf[tg][4 * c + 1]);
+        mma_16816(acc2[tg], Wa[2], Wb[2], Wa[3], Wb[3], bf[tg][4 * c + 2], bf[tg][4 * c + 3]);
+      }
     }
     uint32_t swa[4], swb[4];
     shift_words(qa.w, swa);
     shift_words(qb.w, swb);
-    mma_16816(acc, swa[0], swb[0], swa[1], swb[1], sf[0], sf[1]);
-    mma_16816(acc2, swa[2], swb[2], swa[3], swb[3], sf[2], sf[3]);
+#pragma unroll
+    for (int tg = 0; tg < NTG; ++tg) {
+      mma_16816(acc[tg], swa[0], swb[0], swa[1], swb[1], sf[tg][0], sf[tg][1]);
+      mma_16816(acc2[tg], swa[2], swb[2], swa[3], swb[3], sf[tg][2], sf[tg][3]);
+    }
   } else {
     // 1-bit quad: qa = 16 bytes: row g codes 0..7 in (x, y), row g+8 in (z, w)
 #pragma unroll
@@ -121,8 +129,11 @@ __device__ __forceinline__ void stage_item(const uint8_t *tbl, uint32_t off_e8p,
       uint32_t Wa[4], Wb[4];
       onebit_words(tbl, off_1b, c < 4 ? qa.x : qa.y, c & 3, Wa);
       onebit_words(tbl, off_1b, c < 4 ? qa.z : qa.w, c & 3, Wb);
-      mma_16816(acc, Wa[0], Wb[0], Wa[1], Wb[1], bf[4 * c + 0], bf[4 * c + 1]);
-      mma_16816(acc2, Wa[2], Wb[2], Wa[3], Wb[3], bf[4 * c + 2], bf[4 * c + 3]);
+#pragma unroll
+      for (int tg = 0; tg < NTG; ++tg) {
+        mma_16816(acc[tg], Wa[0], Wb[0], Wa[1], Wb[1], bf[tg][4 * c + 0], bf[tg][4 * c + 1]);
+        mma_16816(acc2[tg], Wa[2], Wb[2], Wa[3], Wb[3], bf[tg][4 * c + 2], bf[tg][4 * c + 3]);
+      }
     }
   }
 }
@@ -179,8 +190,10 @@ __device__ __forceinline__ void load_activations(const GemvArgs &a, int64_t kc, 
   }
 }
 
-template <int K0, int K1, int NST>
-__global__ void __launch_bounds__(kGemvThreads, 2) gemv_kernel(GemvArgs a) {
+// NTG token groups of 8 per pass (1: batches <= 8, two CTAs per SM; 2: batches
+// 9..16 in one pass over the weights, one CTA per SM for the registers).
+template <int K0, int K1, int NST, int NTG>
+__global__ void __launch_bounds__(kGemvThreads, NTG == 1 ? 2 : 1) gemv_kernel(GemvArgs a) {
   extern __shared__ __align__(256) uint8_t gsm[];
   pdl_launch_dependents();
   // 256-byte aligned table rows: the row index is multiplied by 256 and the
@@ -202,44 +215,52 @@ __global__ void __launch_bounds__(kGemvThreads, 2) gemv_kernel(GemvArgs a) {
   const uint32_t off_1b = 128 + (lane & 15) * 8;   // 1-bit replicas: bytes [128, 256)
   const int g = lane >> 2, t = lane & 3;
   const float ls = *a.layer_scale;
-  float tokscale[2];  // layer scale x per-token x2 scale of this lane's two output tokens
+  float tokscale[NTG][2];  // layer scale x per-token x2 scale of this lane's output tokens
 #pragma unroll
-  for (int j = 0; j < 2; ++j) tokscale[j] = 2 * t + j < a.ntok ? ls * a.rowscale[a.tok0 + 2 * t + j] : 0.f;
+  for (int tg = 0; tg < NTG; ++tg)
+#pragma unroll
+    for (int j = 0; j < 2; ++j) {
+      const int tok = 8 * tg + 2 * t + j;
+      tokscale[tg][j] = tok < a.ntok ? ls * a.rowscale[a.tok0 + tok] : 0.f;
+    }
 
-  uint32_t bf[32], sf[4];
+  uint32_t bf[NTG][32], sf[NTG][4];
   int64_t kc = start / a.RT, rt = start % a.RT;
-  load_activations(a, kc, g, t, bf, sf);
+#pragma unroll
+  for (int tg = 0; tg < NTG; ++tg) load_activations(a, kc, 8 * tg + g, t, bf[tg], sf[tg]);
   for (int64_t it = start; it < end; ++it) {
     if (it + 1 < end) load_item<K0, K1, NST>(a, it + 1, lane, nq);
 
-    float acc0[4] = {0.f, 0.f, 0.f, 0.f}, acc0b[4] = {0.f, 0.f, 0.f, 0.f};
-    float acc1[4] = {0.f, 0.f, 0.f, 0.f}, acc1b[4] = {0.f, 0.f, 0.f, 0.f};
-    stage_item<K0>(tbl, off_e8p, off_1b, q[0], q[nquads<K0>() - 1], bf, sf, acc0, acc0b);
+    float acc0[NTG][4], acc0b[NTG][4], acc1[NTG][4], acc1b[NTG][4];
+#pragma unroll
+    for (int tg = 0; tg < NTG; ++tg)
+#pragma unroll
+      for (int i = 0; i < 4; ++i) acc0[tg][i] = acc0b[tg][i] = acc1[tg][i] = acc1b[tg][i] = 0.f;
+    stage_item<K0, NTG>(tbl, off_e8p, off_1b, q[0], q[nquads<K0>() - 1], bf, sf, acc0, acc0b);
     if constexpr (NST == 2) {
       constexpr int o = nquads<K0>();
-      stage_item<K1>(tbl, off_e8p, off_1b, q[o], q[o + nquads<K1>() - 1], bf, sf, acc1, acc1b);
-    }
-#pragma unroll
-    for (int i = 0; i < 4; ++i) {
-      acc0[i] += acc0b[i];
-      acc1[i] += acc1b[i];
+      stage_item<K1, NTG>(tbl, off_e8p, off_1b, q[o], q[o + nquads<K1>() - 1], bf, sf, acc1, acc1b);
     }
 
     // epilogue: c0 (row g, tok 2t), c1 (row g, tok 2t+1), c2/c3 rows g+8
     const int64_t row0 = rt * kRowsPerTile + g, row1 = row0 + 8;
 #pragma unroll
-    for (int j = 0; j < 2; ++j) {
-      const int tok = 2 * t + j;
-      if (tok < a.ntok) {
-        const int gt = a.tok0 + tok;
-        const float f = tokscale[j];
-        float v0 = a.sscale[0] * acc0[j], v1 = a.sscale[0] * acc0[2 + j];
-        if constexpr (NST == 2) {
-          v0 = fmaf(a.sscale[1], acc1[j], v0);
-          v1 = fmaf(a.sscale[1], acc1[2 + j], v1);
+    for (int tg = 0; tg < NTG; ++tg) {
+#pragma unroll
+      for (int j = 0; j < 2; ++j) {
+        const int tok = 8 * tg + 2 * t + j;
+        if (tok < a.ntok) {
+          const int gt = a.tok0 + tok;
+          const float f = tokscale[tg][j];
+          float v0 = a.sscale[0] * (acc0[tg][j] + acc0b[tg][j]);
+          float v1 = a.sscale[0] * (acc0[tg][2 + j] + acc0b[tg][2 + j]);
+          if constexpr (NST == 2) {
+            v0 = fmaf(a.sscale[1], acc1[tg][j] + acc1b[tg][j], v0);
+            v1 = fmaf(a.sscale[1], acc1[tg][2 + j] + acc1b[tg][2 + j], v1);
+          }
+          if (row0 < a.m) atomicAdd(a.y1 + gt * a.m + row0, v0 * f);
+          if (row1 < a.m) atomicAdd(a.y1 + gt * a.m + row1, v1 * f);
         }
-        if (row0 < a.m) atomicAdd(a.y1 + gt * a.m + row0, v0 * f);
-        if (row1 < a.m) atomicAdd(a.y1 + gt * a.m + row1, v1 * f);
       }
     }
 #pragma unroll
@@ -247,7 +268,10 @@ __global__ void __launch_bounds__(kGemvThreads, 2) gemv_kernel(GemvArgs a) {
     if (++rt == a.RT) {
       rt = 0;
       ++kc;
-      if (it + 1 < end) load_activations(a, kc, g, t, bf, sf);
+      if (it + 1 < end) {
+#pragma unroll
+        for (int tg = 0; tg < NTG; ++tg) load_activations(a, kc, 8 * tg + g, t, bf[tg], sf[tg]);
+      }
     }
   }
 }
@@ -265,15 +289,18 @@ static int num_sms() {
 
 template <int K0, int K1, int NST>
 static int run_gemv(GemvArgs &a, int64_t batch, cudaStream_t s) {
-  auto kern = gemv_kernel<K0, K1, NST>;
+  // batches 9..16: one pass of two token groups; else passes of 8 tokens
+  const bool two = batch > 8 && batch <= 16;
+  auto kern = two ? gemv_kernel<K0, K1, NST, 2> : gemv_kernel<K0, K1, NST, 1>;
   QS_CUDA_TRY(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, kTblBytes + 256));
+  const int per_pass = two ? 16 : 8;
   const int64_t warps_needed = a.items;
-  int grid = 2 * num_sms();
+  int grid = (two ? 1 : 2) * num_sms();
   if (warps_needed < static_cast<int64_t>(grid) * (kGemvThreads / 32))
     grid = static_cast<int>(ceil_div(warps_needed, kGemvThreads / 32));
-  for (int64_t tok0 = 0; tok0 < batch; tok0 += 8) {
+  for (int64_t tok0 = 0; tok0 < batch; tok0 += per_pass) {
     a.tok0 = static_cast<int>(tok0);
-    a.ntok = static_cast<int>(batch - tok0 < 8 ? batch - tok0 : 8);
+    a.ntok = static_cast<int>(batch - tok0 < per_pass ? batch - tok0 : per_pass);
     int st = launch_pdl("gemv", kern, dim3(grid), dim3(kGemvThreads), kTblBytes + 256, s, a);
     if (st) return st;
   }

@@ -91,6 +91,9 @@ def test_forward_config_shapes_vs_reference(golden_configs, cfg):
     (8192, 28672, (syn.E8P, syn.E8_1BIT), 1, torch.bfloat16),     # Llama-3-70B down (14336 in)
     (256, 512, (syn.E8P, syn.E8P), 5, torch.float32),             # 4-bit RVQ
     (40, 24, (syn.E8P,), 9, torch.float16),                       # ragged: m, n not tile multiples
+    (2048, 1024, (syn.E8P, syn.E8_1BIT), 12, torch.float16),      # 3-bit RVQ, 9..16 tokens in one pass
+    (512, 1024, (syn.E8_1BIT, syn.E8P), 11, torch.bfloat16),      # 1-bit first stage, one pass
+    (384, 512, (syn.E8P, syn.E8P), 16, torch.float32),            # 4-bit RVQ at the one-pass limit
 ])
 def test_forward_shapes_vs_oracle(m, n, kinds, B, dt):
     lay = syn.make_layer(m, n, kinds, seed=m + n + B, has_bias=True)
