@@ -90,10 +90,20 @@ static int finish_plan(XPlan &p, XLaunch &L, int elem_bytes, int64_t rows, int w
   int most = 128;
   for (int s = 0; s < p.nst; ++s) {
     XStage &S = p.st[s];
-    // odd radices: one output pair per task (compact rolled code) for few
-    // rows across a cluster, else groups of up to six pairs (unrolled code)
-    if ((S.R & 1) && S.R > 1) S.G = C > 1 && few_rows(rows) ? (S.R - 1) / 2 : xodd_groups(S.R);
     S.nbC = S.nb / C;
+    // odd radices: few rows across a cluster run compact rolled code with one
+    // output pair per task, or two when one pair per task would need more
+    // than one round of kXMaxThreads; otherwise unrolled groups of up to six
+    S.compact = 0;
+    if ((S.R & 1) && S.R > 1) {
+      const int H = (S.R - 1) / 2;
+      if (C > 1 && few_rows(rows) && H > 1) {
+        S.compact = S.nbC * H <= kXMaxThreads ? 1 : 2;
+        S.G = (H + S.compact - 1) / S.compact;
+      } else {
+        S.G = xodd_groups(S.R);
+      }
+    }
     S.dnbC = make_fastdiv(static_cast<uint32_t>(S.nbC));
     most = std::max(most, S.nbC * S.G);
   }
@@ -104,8 +114,8 @@ static int finish_plan(XPlan &p, XLaunch &L, int elem_bytes, int64_t rows, int w
 }
 
 // Complex FFT of N points: the prime >= 11 (at most one, once), 7 / 5 / 3, then
-// the power-of-two part in balanced stages (radices up to 16 for one CTA per
-// row, up to 8 across a cluster); a copy stage follows an odd last radix (the
+// the power-of-two part in balanced stages (radices up to 16; smaller for few
+// rows, see max_radix_log); a copy stage follows an odd last radix (the
 // last stage writes the sink).
 static int make_fft_plan(int64_t N64, int64_t rows, XPlan &p, XLaunch &L) {
   if (N64 < 1 || N64 > kXMaxN)
@@ -152,6 +162,7 @@ static int make_fft_plan(int64_t N64, int64_t rows, XPlan &p, XLaunch &L) {
     XStage &S = p.st[s];
     S.R = radix[s];
     S.G = 1;
+    S.compact = 0;
     S.Ns = Ns;
     S.nb = N / S.R;
     S.twstep = N / (Ns * S.R);
@@ -185,6 +196,7 @@ static int make_fwht_plan(int64_t n, int64_t rows, XPlan &p, XLaunch &L) {
     XStage &S = p.st[s];
     S.R = 1 << widths[s];
     S.G = 1;
+    S.compact = 0;
     S.Ns = 1;
     S.nb = p.N / S.R;
     S.twstep = 0;

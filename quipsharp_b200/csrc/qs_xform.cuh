@@ -74,6 +74,7 @@ struct XStage {
   int nb;      // butterflies: N / R
   int nbC;     // butterflies per CTA: nb / C
   int twstep;  // N / (Ns * R)
+  int compact;  // odd radices in cluster kernels: 1 / 2 output pairs per task, rolled code (0: unrolled groups)
   FastDiv dNs, dnbC;
 };
 
@@ -366,19 +367,27 @@ __device__ __forceinline__ void xodd_dispatch(int gi, const XStage &S, const Src
   }
 }
 
-// Output pair k = g + 1 of butterfly j, compact: the loop over the inputs is
-// rolled (by 3) and cos / sin come from the constant table (latency variant:
-// a cluster per row runs this code once, so its length and the per-thread
-// dependency chain, not the instruction count, set the time).
-template <int P, typename Src, typename Dst>
-__device__ __forceinline__ void xodd_pair_compact(int g, const XStage &S, const Src &src, const Dst &dst, int j,
-                                                  int k, float2 w1, float2 wP, bool tw_on, bool inverse) {
+// Output pairs k = g*PER + 1 .. g*PER + PER of butterfly j, compact: the
+// loop over the inputs is rolled (by 3) and cos / sin come from the constant
+// table (latency variant: a cluster per row runs this code once, so its
+// length and the per-thread dependency chain, not the instruction count, set
+// the time).
+template <int P, int PER, typename Src, typename Dst>
+__device__ __forceinline__ void xodd_pairs_compact(int g, const XStage &S, const Src &src, const Dst &dst, int j,
+                                                   int k, float2 w1, float2 wP, bool tw_on, bool inverse) {
   constexpr int H = (P - 1) / 2;
   constexpr int off = prime_offset(P);
-  const int kk = g + 1;
+  const int klo = g * PER + 1;
   const float2 x0 = src(j);
-  float2 A = x0, B = make_float2(0.f, 0.f), s0 = x0, tr = w1;
-  int idx = 0;
+  float2 A[PER], B[PER];
+  int idx[PER];
+#pragma unroll
+  for (int q = 0; q < PER; ++q) {
+    A[q] = x0;
+    B[q] = make_float2(0.f, 0.f);
+    idx[q] = 0;
+  }
+  float2 s0 = x0, tr = w1;
 #pragma unroll 3
   for (int r = 1; r <= H; ++r) {
     float2 xa = src(j + r * S.nb), xb = src(j + (P - r) * S.nb);
@@ -388,25 +397,34 @@ __device__ __forceinline__ void xodd_pair_compact(int g, const XStage &S, const 
       xb = xcmul(xb, xcmul(wP, xconj(tr)));
     }
     const float2 a = xcadd(xa, xb), b = xcsub(xa, xb);
-    s0 = xcadd(s0, a);
-    idx += kk;  // (r * k) mod P, kept incrementally
-    if (idx >= P) idx -= P;
-    const float c = kDftCos[off + idx];
-    const float sn = kDftSin[off + idx];
-    A.x = fmaf(a.x, c, A.x);
-    A.y = fmaf(a.y, c, A.y);
-    B.x = fmaf(b.x, sn, B.x);
-    B.y = fmaf(b.y, sn, B.y);
+    if (g == 0) s0 = xcadd(s0, a);
+#pragma unroll
+    for (int q = 0; q < PER; ++q) {
+      idx[q] += klo + q;  // (r * k) mod P, kept incrementally (k > H only in a partial last group)
+      if (idx[q] >= P) idx[q] -= P;
+      const float c = kDftCos[off + idx[q]];
+      const float sn = kDftSin[off + idx[q]];
+      A[q].x = fmaf(a.x, c, A[q].x);
+      A[q].y = fmaf(a.y, c, A[q].y);
+      B[q].x = fmaf(b.x, sn, B[q].x);
+      B[q].y = fmaf(b.y, sn, B[q].y);
+    }
   }
   const int base = (j - k) * P + k;
-  const float2 miB = make_float2(B.y, -B.x);  // -iB
-  dst(base + kk * S.Ns, inverse ? xcsub(A, miB) : xcadd(A, miB));
-  dst(base + (P - kk) * S.Ns, inverse ? xcadd(A, miB) : xcsub(A, miB));
+#pragma unroll
+  for (int q = 0; q < PER; ++q) {
+    const int kk = klo + q;
+    if (kk <= H) {
+      const float2 miB = make_float2(B[q].y, -B[q].x);  // -iB
+      dst(base + kk * S.Ns, inverse ? xcsub(A[q], miB) : xcadd(A[q], miB));
+      dst(base + (P - kk) * S.Ns, inverse ? xcadd(A[q], miB) : xcsub(A[q], miB));
+    }
+  }
   if (g == 0) dst(base, s0);
 }
 
 // Odd-prime stage: task t = g * nbC + i (output group g of butterfly
-// j = rank + C * i; compact plans: output pair g + 1, G = (P - 1) / 2 groups);
+// j = rank + C * i; compact plans: output pairs g*PER + 1 .. g*PER + PER);
 // tasks of a warp share g except at group boundaries.
 template <int P, bool COMPACT, typename Src, typename Dst>
 __device__ __forceinline__ void xstage_odd(const XStage &S, const Src &src, const Dst &dst, const XTw &tw,
@@ -423,10 +441,9 @@ __device__ __forceinline__ void xstage_odd(const XStage &S, const Src &src, cons
       w1 = xtw(tw, k * S.twstep, inverse);
       wP = xtw(tw, k * S.twstep * P, inverse);
     }
-    // compact (one output pair per task, G = (P - 1) / 2) only in cluster
-    // kernels and only when the plan asks for it (few rows); G tells them apart
-    // for every prime with more than one output pair
-    if (COMPACT && S.G == (P - 1) / 2 && P > 3) xodd_pair_compact<P>(g, S, src, dst, j, k, w1, wP, tw_on, inverse);
+    // compact code only in cluster kernels and only when the plan asks for it (few rows)
+    if (COMPACT && S.compact == 1) xodd_pairs_compact<P, 1>(g, S, src, dst, j, k, w1, wP, tw_on, inverse);
+    else if (COMPACT && S.compact == 2) xodd_pairs_compact<P, 2>(g, S, src, dst, j, k, w1, wP, tw_on, inverse);
     else xodd_dispatch<P, 0>(g, S, src, dst, j, k, w1, wP, tw_on, inverse);
   }
 }
