@@ -174,7 +174,10 @@ int qs_linear_fwd_noalloc(const void *x, int x_dtype, int64_t batch, int64_t n, 
  *    y1 is float32 (batch, m) with row stride ld_y1.  With shards = P > 1, y1
  *    is the rank-major result of an all-gather of P shards of (batch, m/P):
  *    element (b, c) sits at ((c / (m/P)) * batch + b) * (m/P) + c % (m/P)
- *    (ld_y1 is ignored), so no re-layout copy is needed after the gather. */
+ *    (ld_y1 is ignored), so no re-layout copy is needed after the gather.
+ *    y1 is consumed: for many rows of an RFFT layer (shards == 1, ld_y1 == m)
+ *    the transform runs in two passes and uses y1 as its scratch, so its
+ *    contents are unspecified afterwards. */
 int64_t qs_linear_input_bytes(int64_t batch, int64_t n);
 int qs_linear_input(const void *x, int x_dtype, int64_t batch, int64_t n, int transform,
                     const float *sv, const void *phase_v, void *x2_workspace,
@@ -183,7 +186,7 @@ int qs_linear_matmul(const void *x2_workspace, int64_t batch, int64_t n, int64_t
                      const void *packed, int stages, const int *kinds,
                      const float *stage_scales, const float *layer_scale, float *y1,
                      qs_stream_t stream);
-int qs_linear_output(const float *y1, int64_t ld_y1, int64_t shards, int64_t batch, int64_t m,
+int qs_linear_output(float *y1, int64_t ld_y1, int64_t shards, int64_t batch, int64_t m,
                      int transform, const float *su, const void *phase_u, const float *bias,
                      void *y, int y_dtype, qs_stream_t stream);
 

@@ -213,7 +213,7 @@ QS_API int qs_linear_matmul(const void *x2_workspace, int64_t batch, int64_t n, 
                        layer_scale, y1, (cudaStream_t)stream);
 }
 
-QS_API int qs_linear_output(const float *y1, int64_t ld_y1, int64_t shards, int64_t batch,
+QS_API int qs_linear_output(float *y1, int64_t ld_y1, int64_t shards, int64_t batch,
                             int64_t m, int transform, const float *su, const void *phase_u,
                             const float *bias, void *y, int y_dtype, qs_stream_t stream) {
   if (!valid_io_dtype(y_dtype)) return fail(QS_ERR_INVALID_ARG, "bad dtype %d", y_dtype);

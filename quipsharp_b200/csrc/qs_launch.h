@@ -1,6 +1,7 @@
 // Internal launchers shared between the translation units of the library.
 #pragma once
 
+#include <cuda_fp16.h>
 #include <cuda_runtime.h>
 #include <stdint.h>
 
@@ -24,11 +25,19 @@ int64_t linear_input_bytes(int64_t batch, int64_t n);
 int launch_linear_input(const void *x, int x_dtype, int64_t batch, int64_t n, int transform,
                         const float *sv, const void *phase_v, void *x2ws, float *y1,
                         int64_t m_local, cudaStream_t s);
-int launch_linear_output(const float *y1, int64_t ld_y1, int64_t shards, int64_t batch, int64_t m,
+int launch_linear_output(float *y1, int64_t ld_y1, int64_t shards, int64_t batch, int64_t m,
                          int transform, const float *su, const void *phase_u, const float *bias,
                          void *y, int y_dtype, cudaStream_t s);
 int check_fft_size(int64_t n_complex);
 int check_fwht_size(int64_t n);
+
+// qs_xform2.cu: two-pass RFFT of the linear input / output steps for many rows
+bool two_pass_rfft(int64_t n_complex, int64_t rows, int *P, int *lgN1);
+int64_t two_pass_input_scratch_bytes(int64_t batch, int64_t n);
+int launch_two_pass_input(const void *x, int dtype, int64_t batch, int64_t n, const float2 *phase, float scale,
+                          __half *x2h, float *rowscale, int n_pad, void *scratch, cudaStream_t s);
+int launch_two_pass_output(float *y1, int64_t batch, int64_t m, const float2 *phase, const float *bias, float scale,
+                           void *y, int dtype, cudaStream_t s);
 
 // qs_pack.cu
 int launch_pack(const int16_t *codes, int stages, const int *kinds, int64_t m, int64_t n,

@@ -262,8 +262,10 @@ int launch_rfft(int inverse, const void *x, int64_t ld_x, void *y, int64_t ld_y,
 // and keeps every row inside fp16 range whatever the activation magnitudes.
 static int64_t n_padded(int64_t n) { return padded_T(n) * 8; }
 
+// Layout: [x2h][rowscale][two-pass scratch (float32 rows + L1 partial sums),
+// only for batches and sizes that use the two-pass RFFT].
 int64_t linear_input_bytes(int64_t batch, int64_t n) {
-  return round_up(batch * n_padded(n) * 2, 256) + round_up(batch * 4, 256);
+  return round_up(batch * n_padded(n) * 2, 256) + round_up(batch * 4, 256) + two_pass_input_scratch_bytes(batch, n);
 }
 
 int launch_linear_input(const void *x, int x_dtype, int64_t batch, int64_t n, int transform, const float *sv,
@@ -282,9 +284,13 @@ int launch_linear_input(const void *x, int x_dtype, int64_t batch, int64_t n, in
     return p.C > 1 ? run_xinput_rht<true>(L, s, x, x_dtype, p, sv, sc, x2h, rowscale, np, y1, m_local)
                    : run_xinput_rht<false>(L, s, x, x_dtype, p, sv, sc, x2h, rowscale, np, y1, m_local);
   }
-  if ((st = make_fft_plan(n / 2, batch, p, L))) return st;
   const float2 *ph = static_cast<const float2 *>(phase_v);
   const float sc = inv_sqrt_f32(n / 2);
+  if (!y1 && two_pass_rfft(n / 2, batch, nullptr, nullptr)) {
+    void *scratch = static_cast<char *>(x2ws) + round_up(batch * n_pad * 2, 256) + round_up(batch * 4, 256);
+    return launch_two_pass_input(x, x_dtype, batch, n, ph, sc, x2h, rowscale, np, scratch, s);
+  }
+  if ((st = make_fft_plan(n / 2, batch, p, L))) return st;
   switch (p.big) {
 #define QS_CASE(B)                                                                                             \
   case B:                                                                                                      \
@@ -296,7 +302,7 @@ int launch_linear_input(const void *x, int x_dtype, int64_t batch, int64_t n, in
   }
 }
 
-int launch_linear_output(const float *y1, int64_t ld_y1, int64_t shards, int64_t batch, int64_t m, int transform,
+int launch_linear_output(float *y1, int64_t ld_y1, int64_t shards, int64_t batch, int64_t m, int transform,
                          const float *su, const void *phase_u, const float *bias, void *y, int y_dtype,
                          cudaStream_t s) {
   XPlan p;
@@ -309,9 +315,14 @@ int launch_linear_output(const float *y1, int64_t ld_y1, int64_t shards, int64_t
                    : run_xoutput_rht<false>(L, s, y1, ld_y1, shards, batch, p, su, bias, sc, y, y_dtype);
   }
   if (ld_y1 % 2) return fail(QS_ERR_ALIGNMENT, "RFFT y1 row stride must be even");
-  if ((st = make_fft_plan(m / 2, batch, p, L))) return st;
   const float2 *ph = static_cast<const float2 *>(phase_u);
   const float sc = inv_sqrt_f32(m / 2);
+  // the two-pass store loop reads phase / bias and writes y two complex values at a time
+  const bool aligned16 = (reinterpret_cast<uintptr_t>(ph) & 15) == 0 && (reinterpret_cast<uintptr_t>(bias) & 15) == 0 &&
+                         (reinterpret_cast<uintptr_t>(y) & 15) == 0;
+  if (shards == 1 && ld_y1 == m && aligned16 && two_pass_rfft(m / 2, batch, nullptr, nullptr))
+    return launch_two_pass_output(y1, batch, m, ph, bias, sc, y, y_dtype, s);
+  if ((st = make_fft_plan(m / 2, batch, p, L))) return st;
   switch (p.big) {
 #define QS_CASE(B)                                                                                                \
   case B:                                                                                                         \

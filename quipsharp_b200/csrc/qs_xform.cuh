@@ -258,35 +258,46 @@ __device__ __forceinline__ void xdft_pow2(float2 (&v)[R], bool inverse) {
 // ---- FFT stages ----------------------------------------------------------------
 // Butterfly j of this CTA: j = rank + C * i, i < nbC.
 
-// Power-of-two (or copy, R = 1) Stockham stage: butterfly j reads
-// src[j + r*nb], twiddles by W_{Ns*R}^{r*k} (k = j mod Ns), transforms, writes
+// Power-of-two (or copy, R = 1) Stockham butterfly j: reads src[j + r*nb],
+// twiddles by W_{Ns*R}^{r*k} (k = j mod Ns), transforms, writes
 // dst[(j - k)*R + k + r*Ns].
+// The same with the R input values already in registers (v[r] = src[j + r*nb]).
+template <int R, typename Dst>
+__device__ __forceinline__ void xbutterfly_pow2_vals(const XStage &S, float2 (&v)[R], const Dst &dst, const XTw &tw,
+                                                     bool inverse, int j) {
+  int k = 0;
+  if (S.Ns > 1) {
+    k = j - fdiv(j, S.dNs) * S.Ns;
+    if constexpr (R > 1) {
+      // powers w^r by a product tree (depth log2 R): w^r = w^(r/2) * w^(r - r/2)
+      float2 pw[R];
+      pw[1] = xtw(tw, k * S.twstep, inverse);
+#pragma unroll
+      for (int r = 2; r < R; ++r) pw[r] = xcmul(pw[r / 2], pw[r - r / 2]);
+#pragma unroll
+      for (int r = 1; r < R; ++r) v[r] = xcmul(v[r], pw[r]);
+    }
+  }
+  if constexpr (R > 1) xdft_pow2<R>(v, inverse);
+  const int base = (j - k) * R + k;
+#pragma unroll
+  for (int r = 0; r < R; ++r) dst(base + r * S.Ns, v[r]);
+}
+
+template <int R, typename Src, typename Dst>
+__device__ __forceinline__ void xbutterfly_pow2(const XStage &S, const Src &src, const Dst &dst, const XTw &tw,
+                                                bool inverse, int j) {
+  float2 v[R];
+#pragma unroll
+  for (int r = 0; r < R; ++r) v[r] = src(j + r * S.nb);
+  xbutterfly_pow2_vals<R>(S, v, dst, tw, inverse, j);
+}
+
+// Stage over this CTA's butterflies j = rank + C * i, i < nbC.
 template <int R, typename Src, typename Dst>
 __device__ __forceinline__ void xstage_pow2(const XStage &S, const Src &src, const Dst &dst, const XTw &tw,
                                             bool inverse, int rank, int C) {
-  for (int i = threadIdx.x; i < S.nbC; i += blockDim.x) {
-    const int j = rank + C * i;
-    float2 v[R];
-#pragma unroll
-    for (int r = 0; r < R; ++r) v[r] = src(j + r * S.nb);
-    int k = 0;
-    if (S.Ns > 1) {
-      k = j - fdiv(j, S.dNs) * S.Ns;
-      if constexpr (R > 1) {
-        // powers w^r by a product tree (depth log2 R): w^r = w^(r/2) * w^(r - r/2)
-        float2 pw[R];
-        pw[1] = xtw(tw, k * S.twstep, inverse);
-#pragma unroll
-        for (int r = 2; r < R; ++r) pw[r] = xcmul(pw[r / 2], pw[r - r / 2]);
-#pragma unroll
-        for (int r = 1; r < R; ++r) v[r] = xcmul(v[r], pw[r]);
-      }
-    }
-    if constexpr (R > 1) xdft_pow2<R>(v, inverse);
-    const int base = (j - k) * R + k;
-#pragma unroll
-    for (int r = 0; r < R; ++r) dst(base + r * S.Ns, v[r]);
-  }
+  for (int i = threadIdx.x; i < S.nbC; i += blockDim.x) xbutterfly_pow2<R>(S, src, dst, tw, inverse, rank + C * i);
 }
 
 __host__ __device__ constexpr int xodd_groups(int P) {

@@ -33,6 +33,29 @@ def test_prefill_matmul_vs_oracle(m, n, kinds, B, dt):
     assert rel_l2(y.float().cpu().numpy(), oracle_y(lay, x)) < TOL[dt]
 
 
+# Many rows of RFFT layers whose half-width N = P * 2^a (P an odd prime) is at
+# least 4096: the input / output transforms run in two passes (per-column P-point
+# DFTs, then per-block power-of-two FFTs with a warp (N1 <= 512) or the whole
+# CTA (N1 > 512) per block).
+@pytest.mark.parametrize("m,n,kinds,B,dt", [
+    (11008, 1024, (syn.E8P,), 100, torch.bfloat16),               # output 5504 = 43 * 128 (warp blocks)
+    (512, 11008, (syn.E8P, syn.E8_1BIT), 96, torch.float16),      # input 5504 (warp blocks), RVQ
+    (14336, 256, (syn.E8P,), 80, torch.float32),                  # output 7168 = 7 * 1024 (CTA blocks), fp32 out
+    (256, 14336, (syn.E8P,), 77, torch.bfloat16),                 # input 7168 (CTA blocks)
+])
+def test_prefill_two_pass_transforms_vs_oracle(m, n, kinds, B, dt):
+    lay = syn.make_layer(m, n, kinds, seed=m + 3 * n + B, transform_kind="rfft", has_bias=True)
+    x = syn.make_activations(B, n, dtype=dt, seed=B + 7)
+    y = make_module(lay)(x.to(DEV))
+    torch.cuda.synchronize()
+    N.check(N.lib().qs_device_status(N.stream_of(y)))
+    assert y.shape == (B, m) and y.dtype == dt
+    assert rel_l2(y.float().cpu().numpy(), oracle_y(lay, x)) < TOL[dt]
+    # the same rows through the few-row (one-pass) transforms agree
+    y_few = make_module(lay)(x[:8].to(DEV))
+    assert rel_l2(y[:8].float().cpu().numpy(), y_few.float().cpu().numpy()) < TOL[dt]
+
+
 def test_prefill_and_decode_paths_agree():
     """The same layer through the decode-regime kernel (16 tokens) and the
     prefill GEMM (17 tokens): the shared 16 rows agree."""
