@@ -31,11 +31,12 @@ int launch_linear_output(float *y1, int64_t ld_y1, int64_t shards, int64_t batch
 int check_fft_size(int64_t n_complex);
 int check_fwht_size(int64_t n);
 
-// qs_xform2.cu: two-pass RFFT of the linear input / output steps for many rows
+// qs_xform2.cu: two-pass RFFT of the linear input / output steps
 bool two_pass_rfft(int64_t n_complex, int64_t rows, int *P, int *lgN1);
 int64_t two_pass_input_scratch_bytes(int64_t batch, int64_t n);
 int launch_two_pass_input(const void *x, int dtype, int64_t batch, int64_t n, const float2 *phase, float scale,
-                          __half *x2h, float *rowscale, int n_pad, void *scratch, cudaStream_t s);
+                          __half *x2h, float *rowscale, int n_pad, void *scratch, float *y1, int64_t m_local,
+                          cudaStream_t s);
 int launch_two_pass_output(float *y1, int64_t batch, int64_t m, const float2 *phase, const float *bias, float scale,
                            void *y, int dtype, cudaStream_t s);
 

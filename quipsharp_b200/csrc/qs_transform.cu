@@ -286,9 +286,9 @@ int launch_linear_input(const void *x, int x_dtype, int64_t batch, int64_t n, in
   }
   const float2 *ph = static_cast<const float2 *>(phase_v);
   const float sc = inv_sqrt_f32(n / 2);
-  if (!y1 && two_pass_rfft(n / 2, batch, nullptr, nullptr)) {
+  if (two_pass_rfft(n / 2, batch, nullptr, nullptr) && (!y1 || few_rows(batch))) {
     void *scratch = static_cast<char *>(x2ws) + round_up(batch * n_pad * 2, 256) + round_up(batch * 4, 256);
-    return launch_two_pass_input(x, x_dtype, batch, n, ph, sc, x2h, rowscale, np, scratch, s);
+    return launch_two_pass_input(x, x_dtype, batch, n, ph, sc, x2h, rowscale, np, scratch, y1, m_local, s);
   }
   if ((st = make_fft_plan(n / 2, batch, p, L))) return st;
   switch (p.big) {

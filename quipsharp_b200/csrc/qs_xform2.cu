@@ -290,6 +290,222 @@ __global__ void __launch_bounds__(256) xblk_kernel(XPlan p1, XBlkArgs a) {
   }
 }
 
+// ---- few rows ("spread" mode) ---------------------------------------------------
+// When the rows alone cannot fill the GPU (decode), pass A splits each column's
+// output pairs over G = spread_groups(P) lanes of a warp (all lanes load the column, a warp
+// barrier, then each lane stores its pairs: in place is safe), and pass B
+// gives each block to its own warp (N1 <= 512) or CTA, across as many CTAs as
+// there are blocks, writing the output straight to global memory.
+// Lanes per column in spread mode: a power of two up to 4, at most the number
+// of output pairs (P - 1) / 2 (more lanes repeat the column loads and the
+// per-group code without shortening the chain enough).
+__host__ __device__ constexpr int spread_groups(int P) {
+  int G = 1;
+  while (G * 2 <= (P - 1) / 2 && G < 4) G *= 2;
+  return G;
+}
+constexpr int kSpreadGroupsMax = 4;
+// Largest prime of the few-row two-pass path: above it the column DFTs are long
+// enough that the one-pass cluster plan of qs_transform.cu is as fast.
+constexpr int kSpreadMaxPrime = 13;
+
+template <int P, bool OUT, int G, int g>
+__device__ __forceinline__ void xcol_group(const float2 (&v)[P], float2 *__restrict__ col, int lgN1, int j1, int N) {
+  constexpr int H = (P - 1) / 2;
+  constexpr int per = (H + G - 1) / G;
+  constexpr int klo = g * per + 1;
+  constexpr int off = prime_offset(P);
+  if constexpr (klo <= H) {
+    float sn, cs;
+    sincospif(2.0f * static_cast<float>(j1) / static_cast<float>(N), &sn, &cs);
+    const float2 w = make_float2(cs, OUT ? sn : -sn);
+    sincospif(2.0f * static_cast<float>(j1) / static_cast<float>(1 << lgN1), &sn, &cs);
+    const float2 wP = make_float2(cs, OUT ? sn : -sn);
+    sincospif(2.0f * static_cast<float>((j1 * klo) % N) / static_cast<float>(N), &sn, &cs);
+    float2 wk = make_float2(cs, OUT ? sn : -sn);  // w^klo
+#pragma unroll
+    for (int q = 0; q < per; ++q) {
+          const int k = klo + q;
+      if (k <= H) {
+        float2 A = v[0], B = make_float2(0.f, 0.f);
+#pragma unroll
+        for (int r = 1; r <= H; ++r) {
+          const float c = kDftCos[off + (r * (klo + q)) % P];
+          const float s = kDftSin[off + (r * (klo + q)) % P];
+          A.x = fmaf(v[r].x, c, A.x);
+          A.y = fmaf(v[r].y, c, A.y);
+          B.x = fmaf(v[P - r].x, s, B.x);
+          B.y = fmaf(v[P - r].y, s, B.y);
+        }
+        const float2 miB = make_float2(B.y, -B.x);
+        const float2 Xk = OUT ? xcsub(A, miB) : xcadd(A, miB);
+        const float2 Xm = OUT ? xcadd(A, miB) : xcsub(A, miB);
+        col[k << lgN1] = xcmul(Xk, wk);
+        col[(P - k) << lgN1] = xcmul(Xm, xcmul(wP, xconj(wk)));
+        wk = xcmul(wk, w);
+      }
+    }
+  }
+}
+
+template <int P, bool OUT, int G, int g = 0>
+__device__ __forceinline__ void xcol_group_dispatch(int gi, const float2 (&v)[P], float2 *__restrict__ col, int lgN1,
+                                                    int j1, int N) {
+  if constexpr (g < G) {
+    if (gi == g) xcol_group<P, OUT, G, g>(v, col, lgN1, j1, N);
+    else xcol_group_dispatch<P, OUT, G, g + 1>(gi, v, col, lgN1, j1, N);
+  }
+}
+
+template <int P, bool OUT>
+__global__ void __launch_bounds__(256) xcol_spread_kernel(const void *x, int dtype, const float2 *phase, float2 *y,
+                                                          float *partial, int N, int lgN1, int64_t tasks) {
+  constexpr int G = spread_groups(P);
+  pdl_launch_dependents();
+  pdl_wait();
+  const int64_t t = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x;
+  if (t >= tasks) return;  // tasks = rows * N1 * G, a multiple of 32: whole warps leave together
+  constexpr int H = (P - 1) / 2;
+  const int g = static_cast<int>(t & (G - 1));
+  const int64_t c = t / G;
+  const int64_t b = c >> lgN1;
+  const int j1 = static_cast<int>(c & ((int64_t(1) << lgN1) - 1));
+  const float2 *__restrict__ cin = y + b * N + j1;
+  float2 *__restrict__ col = y + b * N + j1;
+  float2 v[P];
+  float l1 = 0.f;
+#pragma unroll
+  for (int j2 = 0; j2 < P; ++j2) {
+    const int o = j2 << lgN1;
+    if constexpr (OUT) {
+      v[j2] = cin[o];
+    } else {
+      const int64_t e = b * N + j1 + o;
+      float2 z;
+      if (dtype == QS_F16) z = __half22float2(reinterpret_cast<const __half2 *>(x)[e]);
+      else if (dtype == QS_BF16) z = __bfloat1622float2(reinterpret_cast<const __nv_bfloat162 *>(x)[e]);
+      else z = reinterpret_cast<const float2 *>(x)[e];
+      v[j2] = xcmul(z, phase[j1 + o]);
+      if (g == 0) l1 += fabsf(v[j2].x) + fabsf(v[j2].y);
+    }
+  }
+  __syncwarp();  // every lane of the column has read it before any lane stores into it
+  float2 s0 = v[0];
+#pragma unroll
+  for (int r = 1; r <= H; ++r) {
+    const float2 a = xcadd(v[r], v[P - r]), d = xcsub(v[r], v[P - r]);
+    v[r] = a;
+    v[P - r] = d;
+    s0 = xcadd(s0, a);
+  }
+  if (g == 0) col[0] = s0;
+  xcol_group_dispatch<P, OUT, G>(g, v, col, lgN1, j1, N);
+  if constexpr (!OUT) {
+    for (int o = 16; o > 0; o >>= 1) l1 += __shfl_xor_sync(0xffffffffu, l1, o);
+    if ((threadIdx.x & 31) == 0) partial[t >> 5] = l1;
+  }
+}
+
+// Global sink of a spread block: element k + P*k1 of row b.
+template <bool OUT>
+struct XSpreadSink {
+  const float2 *phase;
+  const float *bias;
+  void *out;
+  int dtype;
+  __half *x2h;
+  int64_t n_pad;
+  int64_t b;
+  int N, k, P;
+  float scale;
+  __device__ __forceinline__ void operator()(int k1, float2 z) const {
+    const int e = k + P * k1;
+    z.x *= scale;
+    z.y *= scale;
+    if constexpr (OUT) {
+      z = xcmul(z, xconj(phase[e]));
+      if (bias) {
+        const float2 bb = reinterpret_cast<const float2 *>(bias)[e];
+        z.x += bb.x;
+        z.y += bb.y;
+      }
+      const int64_t o = b * N + e;
+      if (dtype == QS_F16) reinterpret_cast<__half2 *>(out)[o] = __floats2half2_rn(z.x, z.y);
+      else if (dtype == QS_BF16) reinterpret_cast<__nv_bfloat162 *>(out)[o] = __floats2bfloat162_rn(z.x, z.y);
+      else reinterpret_cast<float2 *>(out)[o] = z;
+    } else {
+      reinterpret_cast<__half2 *>(x2h + b * n_pad)[e] = __floats2half2_rn(z.x, z.y);
+    }
+  }
+};
+
+// Input step: the row's fp16 scale from its L1 partial sums (every warp of the row computes it).
+__device__ __forceinline__ void xrow_scale_from_l1(const float *partial, int nparts, int64_t b, float scale, int lane,
+                                                   float &sc, float &inv) {
+  float part = 0.f;
+  for (int i = lane; i < nparts; i += 32) part += partial[b * nparts + i];
+  for (int o = 16; o > 0; o >>= 1) part += __shfl_xor_sync(0xffffffffu, part, o);
+  float s2;
+  xpow2_scale(part * scale, s2, inv);
+  sc = scale * s2;
+}
+
+struct XSpreadArgs {
+  int64_t rows;
+  float *y1;        // input step of a decode-sized batch: y1 (rows, m_local) to zero, or null
+  int64_t m_local;
+};
+
+template <bool OUT, int R0>
+__global__ void __launch_bounds__(256) xblk_spread_kernel(XPlan p1, XBlkArgs a, XSpreadArgs sa) {
+  extern __shared__ float2 xsm3[];
+  __shared__ XTw tw;
+  constexpr int RW = R0 ? R0 : 1;
+  pdl_launch_dependents();
+  build_xtw(tw, a.N1);
+  pdl_wait();
+  if (!OUT && sa.y1) {  // zero y1 for the decode matmul: a slice per CTA
+    const int64_t total = sa.rows * sa.m_local;
+    const int64_t z0 = total * blockIdx.x / gridDim.x, z1 = total * (blockIdx.x + 1) / gridDim.x;
+    for (int64_t i = z0 + threadIdx.x; i < z1; i += blockDim.x) sa.y1[i] = 0.f;
+  }
+  __syncthreads();  // twiddle tables
+  const int N = a.N, P = a.P, N1 = a.N1;
+  const int bufE = xbuf_elems<float2>(N1);
+  const int lane = threadIdx.x & 31;
+  int64_t blk_id;
+  float2 *b0;
+  if constexpr (R0 != 0) {
+    const int warp = threadIdx.x >> 5;
+    blk_id = static_cast<int64_t>(blockIdx.x) * (blockDim.x >> 5) + warp;
+    if (blk_id >= sa.rows * P) return;  // no CTA barrier follows
+    b0 = xsm3 + static_cast<size_t>(2 * warp) * bufE;
+  } else {
+    blk_id = blockIdx.x;
+    b0 = xsm3;
+  }
+  const int64_t b = blk_id / P;
+  const int k = static_cast<int>(blk_id - b * P);
+  const float2 *blk = a.y + b * N + static_cast<int64_t>(k) * N1;
+  float sc = a.scale, inv = 1.f;
+  if constexpr (!OUT) xrow_scale_from_l1(a.partial, a.nparts, b, a.scale, lane, sc, inv);
+  XSpreadSink<OUT> sink{a.phase, a.bias, a.out, a.dtype, a.x2h, a.n_pad, b, N, k, P, sc};
+  if constexpr (R0 != 0) {
+    float2 cur[RW];
+#pragma unroll
+    for (int r = 0; r < RW; ++r) cur[r] = blk[lane + 32 * r];
+    xfft_block_warp<RW>(p1, cur, b0, b0 + bufE, tw, OUT, lane, sink);
+  } else {
+    xfft_row<0, false>(p1, b0, b0 + bufE, tw, OUT, 0, XBlockSrc{blk}, sink);
+  }
+  if constexpr (!OUT) {
+    if (k == 0) {
+      for (int i = 2 * N + lane; i < a.n_pad; i += 32) a.x2h[b * a.n_pad + i] = __float2half_rn(0.f);
+      if (lane == 0) a.rowscale[b] = inv;
+    }
+  }
+}
+
 // ---- host -----------------------------------------------------------------------
 static int xnum_sms2() {
   static int cached[64] = {0};
@@ -302,9 +518,12 @@ static int xnum_sms2() {
   return n;
 }
 
-// Rows at or above which the two-pass path is used (the rows alone fill the SMs).
+// Half widths that use the two-pass path: N = P * 2^a >= 4096, P an odd prime
+// <= 43, 2^a >= 64; few rows (spread mode) only for P <= kSpreadMaxPrime.
+static bool spread_mode(int64_t rows) { return rows * 2 <= xnum_sms2(); }
+
 bool two_pass_rfft(int64_t N, int64_t rows, int *P_out, int *lgN1_out) {
-  if (rows * 2 <= xnum_sms2() || N < 4096) return false;
+  if (N < 4096) return false;
   int P = 0;
   for (int q : {43, 41, 37, 31, 29, 23, 19, 17, 13, 11, 7, 5, 3}) {
     if (N % q == 0) {
@@ -313,6 +532,7 @@ bool two_pass_rfft(int64_t N, int64_t rows, int *P_out, int *lgN1_out) {
     }
   }
   if (!P || (N / P) % P == 0) return false;
+  if (spread_mode(rows) && P > kSpreadMaxPrime) return false;
   const int64_t N1 = N / P;
   if (N1 < 64 || (N1 & (N1 - 1))) return false;
   int lg = 0;
@@ -326,7 +546,7 @@ int64_t two_pass_input_scratch_bytes(int64_t batch, int64_t n) {
   int P, lg;
   if (n % 2 || !two_pass_rfft(n / 2, batch, &P, &lg)) return 0;
   const int64_t N = n / 2, N1 = int64_t(1) << lg;
-  return round_up(batch * N * 8, 256) + round_up(batch * (N1 / 32) * 4, 256);
+  return round_up(batch * N * 8, 256) + round_up(batch * (N1 * kSpreadGroupsMax / 32) * 4, 256);
 }
 
 // Plan of the N1-point block FFT.  Warp per block (N1 <= 512): first radix
@@ -384,6 +604,45 @@ static int launch_col(int P, const void *x, int dtype, const float2 *phase, floa
 }
 
 template <bool OUT>
+static int launch_col_spread(int P, const void *x, int dtype, const float2 *phase, float2 *y, float *partial, int N,
+                             int lgN1, int64_t tasks, cudaStream_t s) {
+  const dim3 grid(static_cast<unsigned>(ceil_div(tasks, 256)));
+  switch (P) {
+#define QS_COL(Q) \
+  case Q: return launch_pdl("two_pass_columns", xcol_spread_kernel<Q, OUT>, grid, dim3(256), 0, s, x, dtype, phase, y, partial, N, lgN1, tasks);
+    QS_COL(3) QS_COL(5) QS_COL(7) QS_COL(11) QS_COL(13) QS_COL(17) QS_COL(19) QS_COL(23) QS_COL(29) QS_COL(31)
+    QS_COL(37) QS_COL(41) QS_COL(43)
+#undef QS_COL
+    default: return fail(QS_ERR_UNSUPPORTED, "two-pass FFT: bad prime %d", P);
+  }
+}
+
+// Spread pass B: a warp per block (N1 <= 512) in CTAs of 8 warps, else a CTA per block.
+template <bool OUT>
+static int launch_blk_spread(const XBlkArgs &a0, const XSpreadArgs &sa, cudaStream_t s) {
+  XBlkArgs a = a0;
+  const bool warp = a.N1 <= 512;
+  a.warp_mode = warp;
+  XPlan p1;
+  block_plan(a.N1, warp, p1);
+  const int64_t nblocks = sa.rows * a.P;
+  const size_t smem = static_cast<size_t>(warp ? 16 : 2) * xbuf_elems<float2>(a.N1) * sizeof(float2);
+  auto kern = xblk_spread_kernel<OUT, 0>;
+  if (warp) {
+    switch (a.N1 >> 5) {
+      case 2: kern = xblk_spread_kernel<OUT, 2>; break;
+      case 4: kern = xblk_spread_kernel<OUT, 4>; break;
+      case 8: kern = xblk_spread_kernel<OUT, 8>; break;
+      case 16: kern = xblk_spread_kernel<OUT, 16>; break;
+      default: return fail(QS_ERR_UNSUPPORTED, "two-pass FFT: block of %d points", a.N1);
+    }
+  }
+  QS_CUDA_TRY(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
+  const int64_t grid = warp ? ceil_div(nblocks, 8) : nblocks;
+  return launch_pdl("two_pass_blocks", kern, dim3(static_cast<unsigned>(grid)), dim3(256), smem, s, p1, a, sa);
+}
+
+template <bool OUT>
 static int launch_blk(int64_t rows, const XBlkArgs &a0, cudaStream_t s) {
   XBlkArgs a = a0;
   const int threads = 256;
@@ -405,7 +664,10 @@ int launch_two_pass_output(float *y1, int64_t batch, int64_t m, const float2 *ph
   const int64_t N = m / 2;
   if (!two_pass_rfft(N, batch, &P, &lg)) return fail(QS_ERR_INVALID_ARG, "two-pass FFT not applicable");
   float2 *yc = reinterpret_cast<float2 *>(y1);
-  int st = launch_col<true>(P, nullptr, 0, nullptr, yc, nullptr, static_cast<int>(N), lg, batch << lg, s);
+  const bool spread = spread_mode(batch);
+  int st = spread ? launch_col_spread<true>(P, nullptr, 0, nullptr, yc, nullptr, static_cast<int>(N), lg,
+                                            (batch << lg) * spread_groups(P), s)
+                  : launch_col<true>(P, nullptr, 0, nullptr, yc, nullptr, static_cast<int>(N), lg, batch << lg, s);
   if (st) return st;
   XBlkArgs a{};
   a.y = yc;
@@ -417,17 +679,23 @@ int launch_two_pass_output(float *y1, int64_t batch, int64_t m, const float2 *ph
   a.scale = scale;
   a.out = y;
   a.dtype = dtype;
+  if (spread) return launch_blk_spread<true>(a, XSpreadArgs{batch, nullptr, 0}, s);
   return launch_blk<true>(batch, a, s);
 }
 
 int launch_two_pass_input(const void *x, int dtype, int64_t batch, int64_t n, const float2 *phase, float scale,
-                          __half *x2h, float *rowscale, int n_pad, void *scratch, cudaStream_t s) {
+                          __half *x2h, float *rowscale, int n_pad, void *scratch, float *y1, int64_t m_local,
+                          cudaStream_t s) {
   int P, lg;
   const int64_t N = n / 2;
   if (!two_pass_rfft(N, batch, &P, &lg)) return fail(QS_ERR_INVALID_ARG, "two-pass FFT not applicable");
   float2 *yc = static_cast<float2 *>(scratch);
   float *partial = reinterpret_cast<float *>(static_cast<char *>(scratch) + round_up(batch * N * 8, 256));
-  int st = launch_col<false>(P, x, dtype, phase, yc, partial, static_cast<int>(N), lg, batch << lg, s);
+  const bool spread = spread_mode(batch);
+  if (!spread && y1) return fail(QS_ERR_INVALID_ARG, "two-pass FFT: y1 zeroing only in spread mode");
+  int st = spread ? launch_col_spread<false>(P, x, dtype, phase, yc, partial, static_cast<int>(N), lg,
+                                             (batch << lg) * spread_groups(P), s)
+                  : launch_col<false>(P, x, dtype, phase, yc, partial, static_cast<int>(N), lg, batch << lg, s);
   if (st) return st;
   XBlkArgs a{};
   a.y = yc;
@@ -436,10 +704,11 @@ int launch_two_pass_input(const void *x, int dtype, int64_t batch, int64_t n, co
   a.N1 = 1 << lg;
   a.scale = scale;
   a.partial = partial;
-  a.nparts = (1 << lg) / 32;
+  a.nparts = (1 << lg) / 32 * (spread ? spread_groups(P) : 1);
   a.x2h = x2h;
   a.rowscale = rowscale;
   a.n_pad = n_pad;
+  if (spread) return launch_blk_spread<false>(a, XSpreadArgs{batch, y1, y1 ? m_local : 0}, s);
   return launch_blk<false>(batch, a, s);
 }
 
