@@ -53,7 +53,12 @@ struct Cfg {
   static_assert(groups <= stages && 4 % groups == 0, "decode groups vs ring stages");
   static constexpr int stage_bytes = NST * kATile + kBTile;
   static constexpr int ring_bytes = stages * stage_bytes;
-  static constexpr int tables_bytes = 2 * 256 * 8;
+  // codebook tables of the stages' kinds, each row replicated `reps` times so the
+  // lanes of a warp read their own copies (bank-conflict free for 16 replicas:
+  // a 128-byte row holds one 8-byte replica per bank pair)
+  static constexpr int reps = NST == 1 ? 16 : 8;
+  static constexpr int table_entries = 256 * reps;
+  static constexpr int tables_bytes = NST * table_entries * 8;
   static constexpr int bar_bytes = 256;
   static constexpr int smem_bytes = 1024 /*align slack*/ + ring_bytes + tables_bytes + bar_bytes;
   static constexpr uint32_t tmem_cols = NST * kBN;
@@ -73,14 +78,14 @@ __device__ __forceinline__ void set_error() { atomicExch(&g_tc_error, 1); }
 
 // E8P: 8 codes of one row (a packed quad) -> 8 x 16-byte chunks of fp16
 // weights (shift included), written to the row's swizzled positions.
-__device__ __forceinline__ void decode_e8p_row(const uint4 &q, const uint2 *tbl, uint8_t *arow, int rsw) {
+__device__ __forceinline__ void decode_e8p_row(const uint4 &q, const uint2 *tbl, int reps, uint8_t *arow, int rsw) {
   const uint32_t flo = q.z ^ (q.z << 8);
   const uint32_t fhi = (q.w & 0x00FFFFFFu) ^ shf_l_wrap(q.z, q.w, 8);
 #pragma unroll
   for (int c = 0; c < 8; ++c) {
     const uint32_t src = c < 4 ? q.x : q.y;
     const uint32_t idx = (src >> (8 * (c & 3))) & 0xFFu;
-    const uint2 T = tbl[idx];
+    const uint2 T = tbl[idx * reps];
     const uint32_t tl = T.x ^ ((flo << c) & 0x80808080u);
     const uint32_t th = T.y ^ ((fhi << c) & 0x80808080u);
     const uint32_t sw = 0x34003400u ^ (prmt(q.w << c, 0u, 0xB4B4u) & 0x80008000u);
@@ -94,11 +99,11 @@ __device__ __forceinline__ void decode_e8p_row(const uint4 &q, const uint2 *tbl,
 }
 
 // 1-bit: 8 index bytes of one row -> 8 chunks.
-__device__ __forceinline__ void decode_1bit_row(const uint2 &q, const uint2 *tbl, uint8_t *arow, int rsw) {
+__device__ __forceinline__ void decode_1bit_row(const uint2 &q, const uint2 *tbl, int reps, uint8_t *arow, int rsw) {
 #pragma unroll
   for (int c = 0; c < 8; ++c) {
     const uint32_t src = c < 4 ? q.x : q.y;
-    const uint2 T = tbl[(src >> (8 * (c & 3))) & 0xFFu];
+    const uint2 T = tbl[((src >> (8 * (c & 3))) & 0xFFu) * reps];
     uint4 w;
     w.x = prmt(T.x, 0u, 0x1404u);
     w.y = prmt(T.x, 0u, 0x3424u);
@@ -139,10 +144,11 @@ __device__ __forceinline__ void load_row_chunk(const uint8_t *stage, int64_t RT,
 }
 
 template <int K, int SPG>
-__device__ __forceinline__ void decode_row(const RowChunk<K, SPG> &rc, int t, const uint2 *tbl_e8p,
-                                           const uint2 *tbl_1b, uint8_t *arow, int rsw) {
-  if constexpr (K == QS_CB_E8P) decode_e8p_row(rc.q[t], tbl_e8p, arow, rsw);
-  else decode_1bit_row(rc.q[t], tbl_1b, arow, rsw);
+__device__ __forceinline__ void decode_row(const RowChunk<K, SPG> &rc, int t, const uint2 *tbl, int reps,
+                                           uint8_t *arow, int rsw) {
+  // tbl: this stage's table already offset to the thread's replica
+  if constexpr (K == QS_CB_E8P) decode_e8p_row(rc.q[t], tbl, reps, arow, rsw);
+  else decode_1bit_row(rc.q[t], tbl, reps, arow, rsw);
 }
 
 template <int K0, int K1, int NST>
@@ -155,8 +161,8 @@ __global__ void __launch_bounds__(Cfg<NST>::threads, 1) gemm_tc_kernel(const __g
   // 1024-byte aligned ring (the swizzle atom); tables and barriers after it.
   uint8_t *base = dsm + ((1024u - (smem_u32(dsm) & 1023u)) & 1023u);
   uint8_t *ring = base;
-  uint2 *tbl_e8p = reinterpret_cast<uint2 *>(base + C::ring_bytes);
-  uint2 *tbl_1b = tbl_e8p + 256;
+  uint2 *tbl0 = reinterpret_cast<uint2 *>(base + C::ring_bytes);  // stage 0's codebook
+  uint2 *tbl1 = tbl0 + C::table_entries;                            // stage 1's (RVQ)
   uint64_t *bars = reinterpret_cast<uint64_t *>(base + C::ring_bytes + C::tables_bytes);
   // bars: full_a[S], full_b[S], empty[S], acc_full, then the TMEM address holder
   const uint32_t bar0 = smem_u32(bars);
@@ -171,9 +177,10 @@ __global__ void __launch_bounds__(Cfg<NST>::threads, 1) gemm_tc_kernel(const __g
   const int n0 = blockIdx.y * kBN;
 
   // ---- setup (independent of the previous kernel)
-  for (int i = threadIdx.x; i < 256; i += blockDim.x) {
-    tbl_e8p[i] = kE8pHiBytes[i];
-    tbl_1b[i] = kE81BitHiBytes[i];
+  for (int i = threadIdx.x; i < C::table_entries; i += blockDim.x) {
+    const int row = i / C::reps;
+    tbl0[i] = K0 == QS_CB_E8P ? kE8pHiBytes[row] : kE81BitHiBytes[row];
+    if constexpr (NST == 2) tbl1[i] = K1 == QS_CB_E8P ? kE8pHiBytes[row] : kE81BitHiBytes[row];
   }
   if (threadIdx.x == 0) {
     for (int s = 0; s < S; ++s) {
@@ -251,6 +258,7 @@ __global__ void __launch_bounds__(Cfg<NST>::threads, 1) gemm_tc_kernel(const __g
     load_row_chunk<K0, G>(a.stage[0], a.RT, 0, R, dg, valid, c0);
     if constexpr (NST == 2) load_row_chunk<K1, G>(a.stage[1], a.RT, 0, R, dg, valid, c1);
     const int rowoff = (r >> 3) * 1024 + (r & 7) * 128;
+    const int rep = lane % C::reps;  // this thread's table replica
     bool ok = true;
     for (int kc = 0; kc < K / 4 && ok; ++kc) {  // one 32-code chunk = 4 K steps
       if (kc + 1 < K / 4) {  // prefetch the next chunk's codes
@@ -266,8 +274,8 @@ __global__ void __launch_bounds__(Cfg<NST>::threads, 1) gemm_tc_kernel(const __g
           break;
         }
         uint8_t *st = ring + s * C::stage_bytes;
-        decode_row<K0>(c0, t, tbl_e8p, tbl_1b, st + rowoff, rsw);
-        if constexpr (NST == 2) decode_row<K1>(c1, t, tbl_e8p, tbl_1b, st + kATile + rowoff, rsw);
+        decode_row<K0>(c0, t, tbl0 + rep, C::reps, st + rowoff, rsw);
+        if constexpr (NST == 2) decode_row<K1>(c1, t, tbl1 + rep, C::reps, st + kATile + rowoff, rsw);
         sm100::fence_proxy_async_smem();
         sm100::mbar_arrive(full_a(s));
       }
