@@ -253,17 +253,22 @@ __global__ void __launch_bounds__(Cfg<NST>::threads, 1) gemm_tc_kernel(const __g
     const int64_t R = m0 + r;
     const bool valid = R < a.m_pad;
     const int rsw = r & 7;
-    RowChunk<K0, SPG> c0, n0c;
-    RowChunk<K1, SPG> c1, n1c;
+    // codes two chunks ahead of the decode (a chunk is ~1 us of MMA work)
+    RowChunk<K0, SPG> c0, n0c, nn0c;
+    RowChunk<K1, SPG> c1, n1c, nn1c;
     load_row_chunk<K0, G>(a.stage[0], a.RT, 0, R, dg, valid, c0);
     if constexpr (NST == 2) load_row_chunk<K1, G>(a.stage[1], a.RT, 0, R, dg, valid, c1);
+    if (K / 4 > 1) {
+      load_row_chunk<K0, G>(a.stage[0], a.RT, 1, R, dg, valid, n0c);
+      if constexpr (NST == 2) load_row_chunk<K1, G>(a.stage[1], a.RT, 1, R, dg, valid, n1c);
+    }
     const int rowoff = (r >> 3) * 1024 + (r & 7) * 128;
     const int rep = lane % C::reps;  // this thread's table replica
     bool ok = true;
     for (int kc = 0; kc < K / 4 && ok; ++kc) {  // one 32-code chunk = 4 K steps
-      if (kc + 1 < K / 4) {  // prefetch the next chunk's codes
-        load_row_chunk<K0, G>(a.stage[0], a.RT, kc + 1, R, dg, valid, n0c);
-        if constexpr (NST == 2) load_row_chunk<K1, G>(a.stage[1], a.RT, kc + 1, R, dg, valid, n1c);
+      if (kc + 2 < K / 4) {
+        load_row_chunk<K0, G>(a.stage[0], a.RT, kc + 2, R, dg, valid, nn0c);
+        if constexpr (NST == 2) load_row_chunk<K1, G>(a.stage[1], a.RT, kc + 2, R, dg, valid, nn1c);
       }
 #pragma unroll
       for (int t = 0; t < SPG; ++t) {
@@ -280,7 +285,11 @@ __global__ void __launch_bounds__(Cfg<NST>::threads, 1) gemm_tc_kernel(const __g
         sm100::mbar_arrive(full_a(s));
       }
       c0 = n0c;
-      if constexpr (NST == 2) c1 = n1c;
+      n0c = nn0c;
+      if constexpr (NST == 2) {
+        c1 = n1c;
+        n1c = nn1c;
+      }
     }
     // ---- epilogue
     if (ok && sm100::mbar_wait_bounded(acc_full, 0, kWaitLimitNs)) {
