@@ -107,12 +107,6 @@ __device__ __forceinline__ uint32_t smem_u32(const void *p) {
   return static_cast<uint32_t>(__cvta_generic_to_shared(p));
 }
 
-__device__ __forceinline__ uint2 lds64(uint32_t addr) {
-  uint2 v;
-  asm volatile("ld.shared.v2.u32 {%0, %1}, [%2];" : "=r"(v.x), "=r"(v.y) : "r"(addr));
-  return v;
-}
-
 // Read-only streaming load (weights read once per launch).  Not volatile:
 // ordering follows data dependencies so loads can overlap with compute.
 __device__ __forceinline__ uint4 ldg_nc_v4(const void *p) {

@@ -6,31 +6,39 @@
 // Execution model
 //  * One row of N points is transformed by a group of C CTAs (C = 1, or a
 //    thread-block cluster of 2..16 CTAs exchanging data through distributed
-//    shared memory).  Few rows (decode) spread each row over a cluster so the
-//    transform's latency is divided over up to 16 SMs; many rows (prefill) run
-//    one CTA per row, or a small cluster when a row does not fit one SM's
-//    shared memory twice.
-//  * The row lives in two shared buffers (ping-pong), distributed over the
-//    group: element e sits in CTA e / E at offset e % E, E = N / C.
-//  * A stage is a set of independent tasks (butterflies, or parts of one); the
-//    group's CTAs split the task range.  A thread loads the values of a task
-//    from the source buffer, transforms them in registers, and stores them to
-//    the destination buffer; a barrier (CTA or cluster) separates stages.
-//  * The first stage reads the row from global memory (with the cast and the
-//    sign / phase multiply fused into the load) and, for the output steps, the
-//    last stage writes global memory (scale, sign / conjugate phase, bias and
-//    cast fused into the store), so HBM sees the row once in and once out.
+//    shared memory).  Few rows (decode) spread a long row over a cluster so
+//    its latency is divided over several SMs; many rows (prefill) run one CTA
+//    per row, or a small cluster when a row does not fit one SM's shared
+//    memory twice.  (Many rows of the RFFT's N = P * 2^a widths use the
+//    two-pass kernels of qs_xform2.cu instead.)
+//  * The row lives in two shared buffers (ping-pong), distributed cyclically:
+//    element e sits in CTA e mod C at local index e / C, so butterfly j, whose
+//    inputs are j + r * nb with C dividing nb, finds them all in CTA j mod C;
+//    stages read their own CTA's buffer and store to the owners' buffers.
+//  * A stage is a set of independent tasks (butterflies, or output groups of
+//    one); each CTA runs the tasks of its own butterflies.  A thread loads a
+//    task's values, transforms them in registers and stores them; a barrier
+//    (CTA or cluster) separates stages.
+//  * A power-of-two first stage reads the row from global memory (the cast and
+//    the sign / phase multiply fused into the load); an odd first stage reads
+//    a copy made by a coalesced load pass.  For the output steps the last
+//    stage writes global memory (scale, sign / conjugate phase, bias and cast
+//    fused into the store), so HBM sees the row once in and once out.
 //
 // FFT: mixed-radix Stockham, radices {16, 8, 4, 2} (in-register DIT), odd
-// primes 3..43.  Stage order: the prime >= 11 (at most one, first, read from
-// global), then 7 / 5 / 3, then the power-of-two stages.  The odd-prime DFT
-// uses the conjugate-pair form X_k, X_{P-k} = A_k -+ i B_k; its (P-1)/2 output
-// pairs are split into G groups that run as separate tasks (warp-uniform), each
-// with compile-time cos / sin operands.  Twiddles W_N^e come from two small
+// primes 3..43.  Stage order: the prime >= 11 (at most one, first), then
+// 7 / 5 / 3, then the power-of-two stages.  The odd-prime DFT uses the
+// conjugate-pair form X_k, X_{P-k} = A_k -+ i B_k; its (P-1)/2 output pairs are
+// split into G groups that run as separate tasks (warp-uniform): unrolled with
+// compile-time cos / sin operands, or (few rows in a cluster) compact rolled
+// code with one or two pairs per task.  Twiddles W_N^e come from two small
 // shared tables (W_N^e = C[e >> 7] * F[e & 127]); the powers a butterfly needs
-// are formed by repeated complex multiplication.
+// are formed by a product tree.
 //
-// FWHT: passes of W <= 5 index bits (groups of 2^W values in registers).
+// FWHT: passes of up to 5 index bits (groups of 2^W values in registers) in
+// a rotating form: a pass transforms the top W bits of the index and writes
+// them at the bottom, so after passes covering all bits every element is back
+// in place.
 #pragma once
 
 #include "qs_common.cuh"
@@ -105,12 +113,6 @@ __host__ __device__ constexpr int xbuf_elems(int E) {
 }
 
 // ---- cluster primitives --------------------------------------------------------
-__device__ __forceinline__ uint32_t cluster_rank() {
-  uint32_t r;
-  asm volatile("mov.u32 %0, %%cluster_ctarank;" : "=r"(r));
-  return r;
-}
-
 __device__ __forceinline__ void cluster_sync() {
   asm volatile("barrier.cluster.arrive.release.aligned;\n\tbarrier.cluster.wait.acquire.aligned;" ::: "memory");
 }
