@@ -178,6 +178,9 @@ int qs_linear_fwd_noalloc(const void *x, int x_dtype, int64_t batch, int64_t n, 
  *    y1 is consumed: for many rows of an RFFT layer (shards == 1, ld_y1 == m)
  *    the transform runs in two passes and uses y1 as its scratch, so its
  *    contents are unspecified afterwards. */
+/* Bytes of the x2 workspace of qs_linear_input / qs_linear_matmul: the fp16
+ * operand, the per-row scales and, for RFFT widths that transform in two passes
+ * (n/2 = P * 2^a >= 4096), a float32 scratch row per token. */
 int64_t qs_linear_input_bytes(int64_t batch, int64_t n);
 int qs_linear_input(const void *x, int x_dtype, int64_t batch, int64_t n, int transform,
                     const float *sv, const void *phase_v, void *x2_workspace,
