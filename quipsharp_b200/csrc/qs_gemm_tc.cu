@@ -327,6 +327,212 @@ __global__ void __launch_bounds__(Cfg<NST>::threads, 1) gemm_tc_kernel(const __g
   }
 }
 
+// ---- persistent variant (one-stage codebooks) -----------------------------------
+// One CTA per SM loops over output tiles (tile t = blockIdx.x + i * gridDim.x,
+// weight-row tile fastest).  TMEM holds two 256-column accumulators: the MMA
+// issuer fills accumulator i & 1 for the CTA's i-th tile while four dedicated
+// epilogue warps drain the other one, so a tile's epilogue and the next tile's
+// pipeline fill overlap its successor's mainloop.  The ring's K-step sequence
+// runs on across tiles (global step gs = tile_index * K + ks), and the decode
+// groups prefetch weight codes two 32-code chunks ahead across tile boundaries.
+// Barriers: full_a / full_b / empty per ring stage as above; acc_full[b]
+// (tcgen05.commit after a tile's last MMA) and acc_empty[b] (128 epilogue
+// arrivals) per accumulator.  Each waiter's own previous wait on a barrier
+// proves the phase two back complete, so every parity wait is exact.
+// The dependent kernel is released only when a CTA reaches its last tile, so
+// its CTAs cannot take SMs while this grid still has work queued.
+struct PCfg {
+  static constexpr int stages = 4;
+  static constexpr int groups = 4;
+  static constexpr int decode_warps = 4 * groups;
+  static constexpr int epi_warp0 = 2 + decode_warps;  // warps 18..21: TMEM lane quarters 2, 3, 0, 1
+  static constexpr int threads = 32 * (epi_warp0 + 4);
+  static constexpr uint32_t tmem_cols = 2 * Cfg<1>::tmem_cols;  // two accumulators
+  static_assert(threads > Cfg<1>::threads, "persistent kernel adds epilogue warps");
+};
+
+template <int K0>
+__global__ void __launch_bounds__(PCfg::threads, 1) gemm_tc_persistent_kernel(
+    const __grid_constant__ CUtensorMap tmap_x, TcArgs a, int tiles_m, int tiles_total) {
+  using C = Cfg<1>;  // ring and table geometry
+  constexpr int S = PCfg::stages, G = PCfg::groups;
+  static_assert(S == C::stages && G == C::groups, "persistent ring geometry");
+  extern __shared__ __align__(1024) uint8_t dsm[];
+  uint8_t *base = dsm + ((1024u - (smem_u32(dsm) & 1023u)) & 1023u);
+  uint8_t *ring = base;
+  uint2 *tbl0 = reinterpret_cast<uint2 *>(base + C::ring_bytes);
+  uint64_t *bars = reinterpret_cast<uint64_t *>(base + C::ring_bytes + C::tables_bytes);
+  // bars: full_a[S], full_b[S], empty[S], acc_full[2], acc_empty[2], then the TMEM address holder
+  const uint32_t bar0 = smem_u32(bars);
+  auto full_a = [&](int s) { return bar0 + 8u * s; };
+  auto full_b = [&](int s) { return bar0 + 8u * (S + s); };
+  auto empty = [&](int s) { return bar0 + 8u * (2 * S + s); };
+  auto acc_full = [&](int b) { return bar0 + 8u * (3 * S + b); };
+  auto acc_empty = [&](int b) { return bar0 + 8u * (3 * S + 2 + b); };
+  uint32_t *tmem_holder = reinterpret_cast<uint32_t *>(bars + 3 * S + 4);
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+
+  for (int i = threadIdx.x; i < C::table_entries; i += blockDim.x)
+    tbl0[i] = K0 == QS_CB_E8P ? kE8pHiBytes[i / C::reps] : kE81BitHiBytes[i / C::reps];
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < S; ++s) {
+      sm100::mbar_init(full_a(s), 128);
+      sm100::mbar_init(full_b(s), 1);
+      sm100::mbar_init(empty(s), 1);
+    }
+    for (int b = 0; b < 2; ++b) {
+      sm100::mbar_init(acc_full(b), 1);
+      sm100::mbar_init(acc_empty(b), 128);
+    }
+    sm100::fence_barrier_init();
+    sm100::prefetch_tmap(&tmap_x);
+  }
+  if (warp == 1) sm100::tmem_alloc(smem_u32(tmem_holder), PCfg::tmem_cols);
+  sm100::tc_fence_before_sync();
+  __syncthreads();
+  sm100::tc_fence_after_sync();
+  const uint32_t tmem = *tmem_holder;
+  pdl_wait();  // x2h / rowscale come from the input-transform kernel
+
+  const int K = a.ksteps;
+  const int my_tiles = tiles_total > static_cast<int>(blockIdx.x)
+                           ? (tiles_total - 1 - static_cast<int>(blockIdx.x)) / static_cast<int>(gridDim.x) + 1
+                           : 0;
+  if (my_tiles == 0 && threadIdx.x == 0) pdl_launch_dependents();
+  auto tile_of = [&](int i) { return static_cast<int>(blockIdx.x) + i * static_cast<int>(gridDim.x); };
+
+  if (warp == 0) {
+    // ---- TMA producer
+    if (lane == 0) {
+      int64_t gs = 0, issued = 0;
+      bool ok = true;
+      for (int i = 0; i < my_tiles && ok; ++i) {
+        const int n0 = (tile_of(i) / tiles_m) * kBN;
+        for (int ks = 0; ks < K; ++ks, ++gs) {
+          const int s = static_cast<int>(gs % S);
+          const int64_t use = gs / S;
+          if (use > 0 && !sm100::mbar_wait_bounded(empty(s), static_cast<uint32_t>((use - 1) & 1), kWaitLimitNs)) {
+            set_error();
+            ok = false;
+            break;
+          }
+          sm100::mbar_arrive_expect_tx(full_b(s), kBTile);
+          sm100::tma_load_2d(smem_u32(ring + s * C::stage_bytes + kATile), &tmap_x, ks * kBK, n0, full_b(s));
+          issued = gs + 1;
+        }
+      }
+      for (int64_t g = issued > S ? issued - S : 0; g < issued; ++g)
+        if (!sm100::mbar_wait_bounded(full_b(static_cast<int>(g % S)), static_cast<uint32_t>((g / S) & 1), kWaitLimitNs))
+          set_error();
+    }
+  } else if (warp == 1) {
+    // ---- MMA issuer
+    if (lane == 0) {
+      constexpr uint32_t idesc = sm100::idesc_f16_f32(kBM, kBN);
+      int64_t gs = 0;
+      bool ok = true;
+      for (int i = 0; i < my_tiles && ok; ++i) {
+        const int b = i & 1, u = i >> 1;
+        if (u > 0 && !sm100::mbar_wait_bounded(acc_empty(b), static_cast<uint32_t>((u - 1) & 1), kWaitLimitNs)) {
+          set_error();
+          break;
+        }
+        sm100::tc_fence_after_sync();
+        for (int ks = 0; ks < K; ++ks, ++gs) {
+          const int s = static_cast<int>(gs % S);
+          const uint32_t par = static_cast<uint32_t>((gs / S) & 1);
+          ok = sm100::mbar_wait_bounded(full_a(s), par, kWaitLimitNs) &&
+               sm100::mbar_wait_bounded(full_b(s), par, kWaitLimitNs);
+          if (!ok) {
+            set_error();
+            break;
+          }
+          sm100::tc_fence_after_sync();
+          uint8_t *st = ring + s * C::stage_bytes;
+          const uint64_t adesc = sm100::sw128_kmajor_desc(smem_u32(st));
+          const uint64_t bdesc = sm100::sw128_kmajor_desc(smem_u32(st + kATile));
+#pragma unroll
+          for (int k = 0; k < kBK / 16; ++k)
+            sm100::umma_f16(tmem + b * kBN, adesc + 2 * k, bdesc + 2 * k, idesc, (ks | k) != 0);
+          sm100::umma_commit(empty(s));
+        }
+        sm100::umma_commit(acc_full(b));
+      }
+    }
+  } else if (warp < PCfg::epi_warp0) {
+    // ---- decode producers (group dg of 128 threads, thread r <-> tile row r)
+    const int dg = (warp - 2) >> 2;
+    const int r = (threadIdx.x - 64) & 127;
+    const int rsw = r & 7;
+    const int rowoff = (r >> 3) * 1024 + (r & 7) * 128;
+    const int rep = lane % C::reps;
+    const int KC = K / 4;
+    const int nchunks = my_tiles * KC;
+    auto chunk_load = [&](int q, RowChunk<K0, 1> &rc) {
+      const int mt = tile_of(q / KC) % tiles_m;
+      const int64_t R = static_cast<int64_t>(mt) * kBM + r;
+      load_row_chunk<K0, G>(a.stage[0], a.RT, q % KC, R, dg, R < a.m_pad, rc);
+    };
+    RowChunk<K0, 1> c0, n0c, nn0c;
+    if (nchunks > 0) chunk_load(0, c0);
+    if (nchunks > 1) chunk_load(1, n0c);
+    bool ok = true;
+    for (int q = 0; q < nchunks && ok; ++q) {
+      if (q + 2 < nchunks) chunk_load(q + 2, nn0c);
+      const int64_t gs = static_cast<int64_t>(q) * 4 + dg;  // this group's K step of the chunk
+      const int s = static_cast<int>(gs % S);
+      const int64_t use = gs / S;
+      if (use > 0 && !sm100::mbar_wait_bounded(empty(s), static_cast<uint32_t>((use - 1) & 1), kWaitLimitNs)) {
+        set_error();
+        ok = false;
+        break;
+      }
+      decode_row<K0>(c0, 0, tbl0 + rep, C::reps, ring + s * C::stage_bytes + rowoff, rsw);
+      sm100::fence_proxy_async_smem();
+      sm100::mbar_arrive(full_a(s));
+      c0 = n0c;
+      n0c = nn0c;
+    }
+  } else {
+    // ---- epilogue warps: TMEM lane quarter warp & 3, all 256 token columns
+    const int quarter = warp & 3;
+    const float ls = *a.layer_scale;
+    for (int i = 0; i < my_tiles; ++i) {
+      const int b = i & 1, u = i >> 1;
+      if (!sm100::mbar_wait_bounded(acc_full(b), static_cast<uint32_t>(u & 1), kWaitLimitNs)) {
+        set_error();
+        break;
+      }
+      if (i == my_tiles - 1 && threadIdx.x == 32 * PCfg::epi_warp0) pdl_launch_dependents();
+      sm100::tc_fence_after_sync();
+      const int t = tile_of(i);
+      const int64_t row = static_cast<int64_t>(t % tiles_m) * kBM + quarter * 32 + lane;
+      const int n0 = (t / tiles_m) * kBN;
+      const uint32_t lane_addr = tmem + b * kBN + (static_cast<uint32_t>(quarter * 32) << 16);
+      for (int c = 0; c < kBN; c += 16) {
+        uint32_t v[16];
+        sm100::tmem_ld_16(lane_addr + c, v);
+        sm100::tmem_ld_wait();
+#pragma unroll
+        for (int j = 0; j < 16; ++j) {
+          const int64_t tok = n0 + c + j;
+          if (tok < a.batch && row < a.m)
+            a.y1[tok * a.m + row] = a.sscale[0] * __uint_as_float(v[j]) * ls * a.rowscale[tok];
+        }
+      }
+      sm100::tc_fence_before_sync();
+      sm100::mbar_arrive(acc_empty(b));
+    }
+  }
+  // ---- teardown
+  sm100::tc_fence_before_sync();
+  __syncthreads();
+  if (warp == 1) {
+    sm100::tc_fence_after_sync();
+    sm100::tmem_dealloc(tmem, PCfg::tmem_cols);
+  }
+}
+
 // ---- tensor map for the fp16 activation tiles ----------------------------
 using EncodeTiledFn = CUresult (*)(CUtensorMap *, CUtensorMapDataType, cuuint32_t, void *, const cuuint64_t *,
                                    const cuuint64_t *, const cuuint32_t *, const cuuint32_t *, CUtensorMapInterleave,
@@ -354,6 +560,29 @@ int encode_x_map(CUtensorMap *map, const void *x2h, int64_t n_pad, int64_t batch
                   CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
   if (r != CUDA_SUCCESS) return fail(QS_ERR_CUDA, "cuTensorMapEncodeTiled failed (%d)", static_cast<int>(r));
   return QS_OK;
+}
+
+static int tc_num_sms() {
+  static int cached[64] = {0};
+  int dev = 0;
+  cudaGetDevice(&dev);
+  if (dev < 64 && cached[dev]) return cached[dev];
+  int n = 148;
+  cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, dev);
+  if (dev < 64) cached[dev] = n;
+  return n;
+}
+
+template <int K0>
+int run_gemm_persistent(const CUtensorMap &map, const TcArgs &a, cudaStream_t s) {
+  using C = Cfg<1>;
+  auto kern = gemm_tc_persistent_kernel<K0>;
+  QS_CUDA_TRY(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, C::smem_bytes));
+  const int tiles_m = static_cast<int>(ceil_div(a.m, kBM));
+  const int tiles_total = tiles_m * static_cast<int>(ceil_div(a.batch, kBN));
+  const int grid = tiles_total < tc_num_sms() ? tiles_total : tc_num_sms();
+  return launch_pdl("gemm_tc", kern, dim3(grid), dim3(PCfg::threads), C::smem_bytes, s, map, a, tiles_m,
+                    tiles_total);
 }
 
 template <int K0, int K1, int NST>
@@ -391,7 +620,7 @@ int launch_matmul_tc(const void *x2ws, int64_t batch, int64_t n, int64_t m, cons
   if (st) return st;
   const int k0 = kinds[0], k1 = stages == 2 ? kinds[1] : 0;
   if (stages == 1)
-    return k0 == QS_CB_E8P ? run_gemm<QS_CB_E8P, 0, 1>(map, a, s) : run_gemm<QS_CB_E8_1BIT, 0, 1>(map, a, s);
+    return k0 == QS_CB_E8P ? run_gemm_persistent<QS_CB_E8P>(map, a, s) : run_gemm_persistent<QS_CB_E8_1BIT>(map, a, s);
   if (k0 == QS_CB_E8P && k1 == QS_CB_E8_1BIT) return run_gemm<QS_CB_E8P, QS_CB_E8_1BIT, 2>(map, a, s);
   if (k0 == QS_CB_E8P && k1 == QS_CB_E8P) return run_gemm<QS_CB_E8P, QS_CB_E8P, 2>(map, a, s);
   if (k0 == QS_CB_E8_1BIT && k1 == QS_CB_E8P) return run_gemm<QS_CB_E8_1BIT, QS_CB_E8P, 2>(map, a, s);

@@ -686,6 +686,7 @@ __device__ __forceinline__ int64_t xy1_offset(int64_t row, int64_t col, int64_t 
 struct XRowArgs {
   int64_t row_base;
   int C;
+  int early;  // release the dependent kernel at the start (few rows) or only at exit (many rows)
 };
 
 __device__ __forceinline__ int64_t xrow(const XRowArgs &a, bool cl) {
@@ -738,7 +739,7 @@ __global__ void __launch_bounds__(kXMaxThreads, 1) xinput_rfft_kernel(
   const int C = plan.C;
   const int64_t row = xrow(ra, CL);
   float2 *const b0 = xsm, *const b1 = xsm + xbuf_elems<float2>(plan.E);
-  pdl_launch_dependents();
+  if (ra.early) pdl_launch_dependents();
   build_xtw(tw, plan.N);
   pdl_wait();  // x may be the previous kernel's output; y1 may still be read by it
   if (y1) xzero_row(y1, row, m_local, m_local * rank / C, m_local * (rank + 1) / C);
@@ -792,7 +793,7 @@ __global__ void __launch_bounds__(kXMaxThreads, 1) xoutput_rfft_kernel(
   float2 *b0 = xsm, *b1 = xsm + xbuf_elems<float2>(plan.E);
   const int N = plan.N;
   const int64_t mp = 2 * static_cast<int64_t>(N) / shards;
-  pdl_launch_dependents();
+  if (ra.early) pdl_launch_dependents();
   build_xtw(tw, N);
   pdl_wait();  // y1 comes from the matmul (or the all-gather)
   auto gsrc = [&](int e) {
@@ -855,7 +856,7 @@ __global__ void __launch_bounds__(kXMaxThreads, 1) xinput_rht_kernel(
   const int64_t row = xrow(ra, CL);
   const int n = plan.N;
   float *const b0 = fsm_x, *const b1 = fsm_x + xbuf_elems<float>(plan.E);
-  pdl_launch_dependents();
+  if (ra.early) pdl_launch_dependents();
   pdl_wait();
   if (y1) xzero_row(y1, row, m_local, m_local * rank / C, m_local * (rank + 1) / C);
   auto gsrc = [&](int i) { return load_as_float(x, row * n + i, dtype) * sv[i]; };
@@ -892,7 +893,7 @@ __global__ void __launch_bounds__(kXMaxThreads, 1) xoutput_rht_kernel(
   const int m = plan.N;
   const int64_t mp = m / shards;
   float *b0 = fsm_x, *b1 = fsm_x + xbuf_elems<float>(plan.E);
-  pdl_launch_dependents();
+  if (ra.early) pdl_launch_dependents();
   pdl_wait();
   auto gsrc = [&](int i) { return y1[xy1_offset(row, i, ld_y1, shards, mp, batch)]; };
   auto sink = [&](int i, float v) {
@@ -932,6 +933,17 @@ int run_xoutput_rht(const XLaunch &L, cudaStream_t s, const float *y1, int64_t l
                     int64_t batch, const XPlan &p, const float *su, const float *bias, float scale, void *y,
                     int dtype);
 
+inline int xlaunch_sms() {
+  static int cached[64] = {0};
+  int dev = 0;
+  cudaGetDevice(&dev);
+  if (dev < 64 && cached[dev]) return cached[dev];
+  int n = 148;
+  cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, dev);
+  if (dev < 64) cached[dev] = n;
+  return n;
+}
+
 template <typename... KArgs, typename... Args>
 cudaError_t xlaunch_ex(const cudaLaunchConfig_t &cfg, void (*kern)(KArgs...), Args... args) {
   return cudaLaunchKernelEx(&cfg, kern, static_cast<KArgs>(args)...);
@@ -965,7 +977,10 @@ int xlaunch(const char *what, void (*kern)(KArgs...), const XLaunch &L, int C, c
     }
     cfg.attrs = attr;
     cfg.numAttrs = na;
-    XRowArgs ra{r0, C};
+    // Few rows leave most SMs free: the dependent kernel may start its
+    // prologue at once.  Many rows: its CTAs would take SMs this grid still
+    // needs, so it is released only at exit.
+    XRowArgs ra{r0, C, L.rows * 2 <= xlaunch_sms() ? 1 : 0};
     const cudaError_t e = xlaunch_ex(cfg, kern, args..., ra);
     if (e != cudaSuccess) return fail(QS_ERR_CUDA, "%s launch failed: %s", what, cudaGetErrorString(e));
   }

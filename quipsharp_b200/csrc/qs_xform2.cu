@@ -30,7 +30,8 @@ namespace qs {
 template <int P, bool OUT>
 __global__ void __launch_bounds__(256, OUT ? 1 : 2) xcol_kernel(const void *x, int dtype, const float2 *phase, float2 *y,
                                                    float *partial, int N, int lgN1, int64_t cols) {
-  pdl_launch_dependents();
+  // many rows: the dependent kernel is released only at exit (its CTAs would
+  // otherwise take SMs this grid still needs)
   pdl_wait();  // OUT: y1 comes from the matmul; IN: x may be the previous kernel's output
   const int64_t t = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x;
   if (t >= cols) return;  // cols is a multiple of 32 (N1 >= 64): whole warps leave together
@@ -185,7 +186,7 @@ __global__ void __launch_bounds__(256) xblk_kernel(XPlan p1, XBlkArgs a) {
   extern __shared__ __align__(16) unsigned char xsm2[];
   __shared__ XTw tw;
   __shared__ float red[8];
-  pdl_launch_dependents();
+  // many rows: the dependent kernel is released only at exit
   build_xtw(tw, a.N1);
   pdl_wait();  // the pass-A result
   const int64_t b = blockIdx.x;
