@@ -165,7 +165,7 @@ int qs_linear_fwd_noalloc(const void *x, int x_dtype, int64_t batch, int64_t n, 
  * each rank runs qs_linear_input + qs_linear_matmul on its rows of the
  * weight, the y1 shards are all-gathered, then every rank runs
  * qs_linear_output on the full y1).
- * Batches above 16 tokens run the prefill matmul (fused decode + tcgen05
+ * Batches above 32 tokens run the prefill matmul (fused decode + tcgen05
  * tensor-core GEMM); smaller ones the decode-regime kernel.
  *  - qs_linear_input: x -> x2 (fp16 tiles + per-row scale in workspace) and
  *    zeroes y1 (batch, m_local) float32.

@@ -191,7 +191,8 @@ __device__ __forceinline__ void load_activations(const GemvArgs &a, int64_t kc, 
 }
 
 // NTG token groups of 8 per pass (1: batches <= 8, two CTAs per SM; 2: batches
-// 9..16 in one pass over the weights, one CTA per SM for the registers).
+// 9 and more in passes of 16 tokens over the weights, one CTA per SM for the
+// registers; the tcgen05 GEMM takes over at kTcMinBatch).
 template <int K0, int K1, int NST, int NTG>
 __global__ void __launch_bounds__(kGemvThreads, NTG == 1 ? 2 : 1) gemv_kernel(GemvArgs a) {
   extern __shared__ __align__(256) uint8_t gsm[];
@@ -289,8 +290,8 @@ static int num_sms() {
 
 template <int K0, int K1, int NST>
 static int run_gemv(GemvArgs &a, int64_t batch, cudaStream_t s) {
-  // batches 9..16: one pass of two token groups; else passes of 8 tokens
-  const bool two = batch > 8 && batch <= 16;
+  // batches above 8: passes of 16 tokens (two token groups); else one pass of 8
+  const bool two = batch > 8;
   auto kern = two ? gemv_kernel<K0, K1, NST, 2> : gemv_kernel<K0, K1, NST, 1>;
   QS_CUDA_TRY(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, kTblBytes + 256));
   const int per_pass = two ? 16 : 8;

@@ -54,6 +54,9 @@ int launch_matmul_tc(const void *x2ws, int64_t batch, int64_t n, int64_t m, cons
                      const int *kinds, const float *stage_scales, const float *layer_scale, float *y1,
                      cudaStream_t s);
 int device_status(cudaStream_t s);
-constexpr int64_t kTcMinBatch = 17;  // batches of at least this many tokens use the tcgen05 GEMM
+// Batches of at least this many tokens use the tcgen05 GEMM.  Below it the
+// mma.sync kernel's passes of 16 tokens are faster: a 128 x 256 GEMM tile with
+// few tokens is decode-bound and leaves SMs without a row tile.
+constexpr int64_t kTcMinBatch = 33;
 
 }  // namespace qs

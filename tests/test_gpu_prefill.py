@@ -1,5 +1,5 @@
 """GPU parity of the prefill matmul (fused decode + tcgen05 GEMM, batches of
-17 tokens and more) through the public module, against the CPU oracle.
+33 tokens and more) through the public module, against the CPU oracle.
 
 Same tolerance as the decode-regime tests (relative L2 against the float32
 oracle: 1e-3 fp32 out, 2e-3 fp16 out, 1e-2 bf16 out): the weights are exact in
@@ -20,7 +20,7 @@ DEV = "cuda"
     (384, 512, (syn.E8P,), 300, torch.bfloat16),                   # RFFT both sides, ragged token tile
     (256, 1024, (syn.E8P,), 2048, torch.bfloat16),                 # RHT, 8 token tiles
     (200, 256, (syn.E8P, syn.E8_1BIT), 100, torch.float16),        # 3-bit RVQ, ragged row tile
-    (128, 256, (syn.E8P, syn.E8P), 17, torch.float32),             # 4-bit RVQ at the threshold batch
+    (128, 256, (syn.E8P, syn.E8P), 33, torch.float32),             # 4-bit RVQ at the threshold batch
     (1792, 3584, (syn.E8P,), 64, torch.bfloat16),                  # Qwen2.5-7B hidden width
 ])
 def test_prefill_matmul_vs_oracle(m, n, kinds, B, dt):
@@ -57,11 +57,11 @@ def test_prefill_two_pass_transforms_vs_oracle(m, n, kinds, B, dt):
 
 
 def test_prefill_and_decode_paths_agree():
-    """The same layer through the decode-regime kernel (16 tokens) and the
-    prefill GEMM (17 tokens): the shared 16 rows agree."""
+    """The same layer through the decode-regime kernel (32 tokens: two passes
+    of 16) and the prefill GEMM (33 tokens): the shared 32 rows agree."""
     lay = syn.make_layer(512, 1024, (syn.E8P, syn.E8_1BIT), seed=42)
     mod = make_module(lay)
-    x = syn.make_activations(17, 1024, dtype=torch.float16, seed=5).to(DEV)
-    y_tc = mod(x)[:16].float()
-    y_mma = mod(x[:16]).float()
+    x = syn.make_activations(33, 1024, dtype=torch.float16, seed=5).to(DEV)
+    y_tc = mod(x)[:32].float()
+    y_mma = mod(x[:32]).float()
     assert rel_l2(y_tc.cpu().numpy(), y_mma.cpu().numpy()) < 2e-3
