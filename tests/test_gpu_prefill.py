@@ -42,6 +42,8 @@ def test_prefill_matmul_vs_oracle(m, n, kinds, B, dt):
     (512, 11008, (syn.E8P, syn.E8_1BIT), 96, torch.float16),      # input 5504 (warp blocks), RVQ
     (14336, 256, (syn.E8P,), 80, torch.float32),                  # output 7168 = 7 * 1024 (CTA blocks), fp32 out
     (256, 14336, (syn.E8P,), 77, torch.bfloat16),                 # input 7168 (CTA blocks)
+    (14336, 256, (syn.E8P,), 40, torch.float16),                  # GEMM batch, few rows: spread two-pass output
+    (256, 14336, (syn.E8P, syn.E8_1BIT), 48, torch.bfloat16),     # GEMM batch, few rows: spread two-pass input
 ])
 def test_prefill_two_pass_transforms_vs_oracle(m, n, kinds, B, dt):
     lay = syn.make_layer(m, n, kinds, seed=m + 3 * n + B, transform_kind="rfft", has_bias=True)
