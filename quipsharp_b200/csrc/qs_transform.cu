@@ -29,6 +29,27 @@ static int xnum_sms() {
   return n;
 }
 
+// The dry-pass hint flag (see xbusy_flag in qs_xform.cuh): one int per device,
+// its address looked up once per device.
+__device__ int g_qs_xbusy;
+
+int *xbusy_flag() {
+  static int *cached[64] = {nullptr};
+  static bool tried[64] = {false};
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64) return nullptr;
+  if (!tried[dev]) {
+    void *p = nullptr;
+    if (cudaGetSymbolAddress(&p, g_qs_xbusy) != cudaSuccess) {
+      p = nullptr;
+      cudaGetLastError();
+    }
+    cached[dev] = static_cast<int *>(p);
+    tried[dev] = true;
+  }
+  return cached[dev];
+}
+
 static float inv_sqrt_f32(int64_t n) { return static_cast<float>(1.0 / std::sqrt(static_cast<double>(n))); }
 
 static size_t plan_smem(int N, int C, int elem_bytes) {
@@ -277,6 +298,7 @@ int launch_linear_input(const void *x, int x_dtype, int64_t batch, int64_t n, in
   const int np = static_cast<int>(n_pad);
   XPlan p;
   XLaunch L;
+  L.warm = 1;
   int st;
   if (transform == QS_RHT) {
     if ((st = make_fwht_plan(n, batch, p, L))) return st;

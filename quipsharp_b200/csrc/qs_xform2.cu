@@ -455,6 +455,7 @@ struct XSpreadArgs {
   int64_t rows;
   float *y1;        // input step of a decode-sized batch: y1 (rows, m_local) to zero, or null
   int64_t m_local;
+  int *busy;        // output step: the dry-pass hint flag (xbusy_flag), set while it runs
 };
 
 template <bool OUT, int R0>
@@ -462,6 +463,8 @@ __global__ void __launch_bounds__(256) xblk_spread_kernel(XPlan p1, XBlkArgs a, 
   extern __shared__ float2 xsm3[];
   __shared__ XTw tw;
   constexpr int RW = R0 ? R0 : 1;
+  const bool flag = OUT && blockIdx.x == 0 && threadIdx.x == 0;
+  if (flag) xbusy_set(sa.busy, 1);  // dry-pass hint for the next input step (xbusy_flag)
   pdl_launch_dependents();
   build_xtw(tw, a.N1);
   pdl_wait();
@@ -505,6 +508,7 @@ __global__ void __launch_bounds__(256) xblk_spread_kernel(XPlan p1, XBlkArgs a, 
       if (lane == 0) a.rowscale[b] = inv;
     }
   }
+  if (flag) xbusy_set(sa.busy, 0);
 }
 
 // ---- host -----------------------------------------------------------------------
@@ -680,7 +684,7 @@ int launch_two_pass_output(float *y1, int64_t batch, int64_t m, const float2 *ph
   a.scale = scale;
   a.out = y;
   a.dtype = dtype;
-  if (spread) return launch_blk_spread<true>(a, XSpreadArgs{batch, nullptr, 0}, s);
+  if (spread) return launch_blk_spread<true>(a, XSpreadArgs{batch, nullptr, 0, xbusy_flag()}, s);
   return launch_blk<true>(batch, a, s);
 }
 
@@ -709,7 +713,7 @@ int launch_two_pass_input(const void *x, int dtype, int64_t batch, int64_t n, co
   a.x2h = x2h;
   a.rowscale = rowscale;
   a.n_pad = n_pad;
-  if (spread) return launch_blk_spread<false>(a, XSpreadArgs{batch, y1, y1 ? m_local : 0}, s);
+  if (spread) return launch_blk_spread<false>(a, XSpreadArgs{batch, y1, y1 ? m_local : 0, nullptr}, s);
   return launch_blk<false>(batch, a, s);
 }
 
