@@ -3,15 +3,21 @@
 //
 // Weights stream from HBM once in the packed layout of qs_pack.cu and are
 // decoded in registers into fp16 mma.sync A fragments; the tokens form the
-// N=8 side of m16n8k16 (swap-AB GEMV).  Decode of one E8P code (8 weights):
-//   * one 8-byte shared-memory load of the fp16 high bytes of the table row
-//     (the table is replicated 16x so the 16 lanes of a half-warp hit distinct
-//     banks),
-//   * the eight sign flips are XORed into the byte sign bits: the packed code
-//     stores prefix parities g_i, so flips = g ^ (g << 8) for all codes of a
-//     16-byte quad at once, and the inferred 8th flip comes out of the same XOR,
-//   * four byte permutes build the f16x2 words, and the +-1/4 shift is one
-//     f16x2 add.  All decoded values are exact in fp16.
+// N=8 side of m16n8k16 (swap-AB GEMV).  Decode of one code (8 weights):
+//   * one 16-byte shared-memory load of the table row, already laid out as the
+//     four f16x2 words of the coordinate pairs (0,2), (1,3), (4,6), (5,7) (all
+//     table values have a zero low byte; the table is replicated 8x so the 8
+//     lanes of a quarter-warp hit distinct banks),
+//   * E8P: the eight sign flips are XORed into the words' sign bits.  The packed
+//     code stores prefix parities g_i, so flips = g ^ (g << 8) for all codes of a
+//     16-byte quad at once, with the flips of coordinates 0..3 (4..7) of code c
+//     on the byte sign bits of one word after a shift by c; that word (pairs
+//     (1,3)) or the same shifted by 8 more (pairs (0,2)) has exactly the two
+//     flips of a pair on bits 15 and 31, so each word takes one AND-XOR; the
+//     +-1/4 shift is added by the tensor core (see shift_words).  1-bit: the
+//     words are used as loaded.  All decoded values are exact in fp16.
+//   * The activations are loaded in the same pair order (one byte permute per
+//     word, once per code chunk), so A and B agree on k.
 // RVQ stages accumulate separately (exact weights) and are combined with their
 // float32 stage scales in the epilogue.  Each warp walks a contiguous range of
 // (code-chunk, row-tile) items; partial sums of a row tile are added to the
@@ -22,7 +28,7 @@
 namespace qs {
 
 constexpr int kGemvThreads = 256;
-constexpr int kTblBytes = 256 * 256;  // 256 rows x (16 E8P replicas + 16 1-bit replicas) x 8 B
+constexpr int kTblBytes = 256 * 256;  // 256 rows x (8 E8P replicas + 8 1-bit replicas) x 16 B
 
 struct GemvArgs {
   const __half *x2h;       // (batch, n_pad)
@@ -35,51 +41,55 @@ struct GemvArgs {
   int tok0, ntok;
 };
 
-// Fill the replicated table: thread i < 256 owns table row i, reads its E8P
-// and 1-bit entries once and writes the 16 replicas of each.
+// f16x2 words of the coordinate pairs (0,2), (1,3), (4,6), (5,7) from the fp16
+// high bytes of coordinates 0..3 (hb.x) and 4..7 (hb.y).
+__device__ __forceinline__ uint4 pair_words(uint2 hb) {
+  return make_uint4((hb.x << 8) & 0xFF00FF00u, hb.x & 0xFF00FF00u, (hb.y << 8) & 0xFF00FF00u, hb.y & 0xFF00FF00u);
+}
+
+// Fill the replicated table: thread i < 256 owns table row i (256 bytes: 8
+// replicas of its E8P entry, then 8 of its 1-bit entry, 16 bytes each).
 __device__ __forceinline__ void load_table(uint8_t *tbl) {
   for (int row = threadIdx.x; row < 256; row += blockDim.x) {
-    const uint2 e = kE8pHiBytes[row], o = kE81BitHiBytes[row];
-    uint2 *dst = reinterpret_cast<uint2 *>(tbl + row * 256);
+    const uint4 e = pair_words(kE8pHiBytes[row]), o = pair_words(kE81BitHiBytes[row]);
+    uint4 *dst = reinterpret_cast<uint4 *>(tbl + row * 256);
 #pragma unroll
-    for (int r = 0; r < 16; ++r) {
-      dst[(r + row) & 15] = e;          // rotate the write order to spread banks
-      dst[16 + ((r + row) & 15)] = o;
+    for (int r = 0; r < 8; ++r) {
+      dst[(r + row) & 7] = e;  // rotate the write order to spread banks
+      dst[8 + ((r + row) & 7)] = o;
     }
   }
 }
 
-// Decoded f16x2 words of one code: W[0] = coords (0,1), ..., W[3] = (6,7).
-// tbl_lane: table base + this lane's replica offset; idxsrc byte csel holds
-// the row index.  E8P: the eight sign flips (flo/fhi, already shifted to the
-// byte sign bits) are XORed into the fp16 high bytes; the +-1/4 shift is added
-// by the tensor core (see shift_words), so W holds sign*|t| exactly.
-// tbl: the shared table; lane_off: this lane's replica offset within a row.
-// A plain shared-memory load (not asm) so the compiler can hoist it ahead of
-// the previous code's permutes while keeping it after the table fill barrier.
-__device__ __forceinline__ uint2 table_row(const uint8_t *tbl, uint32_t lane_off, uint32_t idxsrc, int csel) {
+// Table row of the code whose index is byte csel of idxsrc.  lane_off: this
+// lane's replica offset within a row.  A plain shared-memory load (not asm) so
+// the compiler can hoist it ahead of the previous code's work while keeping it
+// after the table fill barrier.
+__device__ __forceinline__ uint4 table_row(const uint8_t *tbl, uint32_t lane_off, uint32_t idxsrc, int csel) {
   const uint32_t idx = prmt(idxsrc, 0u, 0x4440u | static_cast<uint32_t>(csel));
-  return *reinterpret_cast<const uint2 *>(tbl + imad(idx, 256u, lane_off));
+  return *reinterpret_cast<const uint4 *>(tbl + imad(idx, 256u, lane_off));
 }
 
+// Decoded f16x2 words of one E8P code: W = pairs (0,2), (1,3), (4,6), (5,7)
+// holding sign*|t| exactly.  flo / fhi: flips of coordinates 0..3 / 4..7 on the
+// byte sign bits (code already selected by the shift); flo8 / fhi8: the same
+// shifted by 8.
 __device__ __forceinline__ void e8p_words(const uint8_t *tbl, uint32_t lane_off, uint32_t idxsrc, int csel,
-                                          uint32_t flo, uint32_t fhi, uint32_t (&W)[4]) {
-  const uint2 T = table_row(tbl, lane_off, idxsrc, csel);
-  const uint32_t tl = T.x ^ (flo & 0x80808080u);
-  const uint32_t th = T.y ^ (fhi & 0x80808080u);
-  W[0] = prmt(tl, 0u, 0x1404u);
-  W[1] = prmt(tl, 0u, 0x3424u);
-  W[2] = prmt(th, 0u, 0x1404u);
-  W[3] = prmt(th, 0u, 0x3424u);
+                                          uint32_t flo, uint32_t flo8, uint32_t fhi, uint32_t fhi8, uint32_t (&W)[4]) {
+  const uint4 T = table_row(tbl, lane_off, idxsrc, csel);
+  W[0] = T.x ^ (flo8 & 0x80008000u);
+  W[1] = T.y ^ (flo & 0x80008000u);
+  W[2] = T.z ^ (fhi8 & 0x80008000u);
+  W[3] = T.w ^ (fhi & 0x80008000u);
 }
 
 __device__ __forceinline__ void onebit_words(const uint8_t *tbl, uint32_t lane_off, uint32_t idxsrc, int csel,
                                              uint32_t (&W)[4]) {
-  const uint2 T = table_row(tbl, lane_off, idxsrc, csel);
-  W[0] = prmt(T.x, 0u, 0x1404u);
-  W[1] = prmt(T.x, 0u, 0x3424u);
-  W[2] = prmt(T.y, 0u, 0x1404u);
-  W[3] = prmt(T.y, 0u, 0x3424u);
+  const uint4 T = table_row(tbl, lane_off, idxsrc, csel);
+  W[0] = T.x;
+  W[1] = T.y;
+  W[2] = T.z;
+  W[3] = T.w;
 }
 
 // The +-1/4 shifts of the 8 codes of a quad as four f16x2 words of +-0.25:
@@ -106,8 +116,10 @@ __device__ __forceinline__ void stage_item(const uint8_t *tbl, uint32_t off_e8p,
 #pragma unroll
     for (int c = 0; c < 8; ++c) {
       uint32_t Wa[4], Wb[4];
-      e8p_words(tbl, off_e8p, c < 4 ? qa.x : qa.y, c & 3, imul(floa, 1u << c), imul(fhia, 1u << c), Wa);
-      e8p_words(tbl, off_e8p, c < 4 ? qb.x : qb.y, c & 3, imul(flob, 1u << c), imul(fhib, 1u << c), Wb);
+      e8p_words(tbl, off_e8p, c < 4 ? qa.x : qa.y, c & 3, imul(floa, 1u << c), imul(floa, 256u << c),
+                imul(fhia, 1u << c), imul(fhia, 256u << c), Wa);
+      e8p_words(tbl, off_e8p, c < 4 ? qb.x : qb.y, c & 3, imul(flob, 1u << c), imul(flob, 256u << c),
+                imul(fhib, 1u << c), imul(fhib, 256u << c), Wb);
 #pragma unroll
       for (int tg = 0; tg < NTG; ++tg) {
         mma_16816(acc[tg], Wa[0], Wb[0], Wa[1], Wb[1], bf[tg][4 * c + 0], bf[tg][4 * c + 1]);
@@ -157,8 +169,10 @@ __device__ __forceinline__ void load_item(const GemvArgs &a, int64_t it, int lan
 }
 
 // Activation fragments of one code chunk for token g (or zeros): bf holds
-// the 64 fp16 inputs of codes 8t..8t+7 (B operands of the 16 mma), sf the
-// per-code sums as (code 2p+1, code 2p) f16x2 pairs (B operands of the shift mma).
+// the 64 fp16 inputs of codes 8t..8t+7 (B operands of the 16 mma) as the
+// coordinate pairs (0,2), (1,3), (4,6), (5,7) of each code (the order of the
+// decoded weight words), sf the per-code sums as (code 2p+1, code 2p) f16x2
+// pairs (B operands of the shift mma).
 __device__ __forceinline__ void load_activations(const GemvArgs &a, int64_t kc, int g, int t,
                                                  uint32_t (&bf)[32], uint32_t (&sf)[4]) {
   if (g < a.ntok) {
@@ -167,10 +181,10 @@ __device__ __forceinline__ void load_activations(const GemvArgs &a, int64_t kc, 
 #pragma unroll
     for (int c = 0; c < 8; ++c) {
       const uint4 v = __ldg(src + c);
-      bf[4 * c + 0] = v.x;
-      bf[4 * c + 1] = v.y;
-      bf[4 * c + 2] = v.z;
-      bf[4 * c + 3] = v.w;
+      bf[4 * c + 0] = prmt(v.x, v.y, 0x5410u);  // (x0, x2)
+      bf[4 * c + 1] = prmt(v.x, v.y, 0x7632u);  // (x1, x3)
+      bf[4 * c + 2] = prmt(v.z, v.w, 0x5410u);  // (x4, x6)
+      bf[4 * c + 3] = prmt(v.z, v.w, 0x7632u);  // (x5, x7)
       const float2 f0 = __half22float2(*reinterpret_cast<const __half2 *>(&v.x));
       const float2 f1 = __half22float2(*reinterpret_cast<const __half2 *>(&v.y));
       const float2 f2 = __half22float2(*reinterpret_cast<const __half2 *>(&v.z));
@@ -212,8 +226,8 @@ __global__ void __launch_bounds__(kGemvThreads, NTG == 1 ? 2 : 1) gemv_kernel(Ge
   if (start >= end) return;
   pdl_wait();  // x2h, rowscale and the zeroed y1 come from the input-transform kernel
 
-  const uint32_t off_e8p = (lane & 15) * 8;        // E8P replicas: bytes [0, 128) of a row
-  const uint32_t off_1b = 128 + (lane & 15) * 8;   // 1-bit replicas: bytes [128, 256)
+  const uint32_t off_e8p = (lane & 7) * 16;        // E8P replicas: bytes [0, 128) of a row
+  const uint32_t off_1b = 128 + (lane & 7) * 16;   // 1-bit replicas: bytes [128, 256)
   const int g = lane >> 2, t = lane & 3;
   const float ls = *a.layer_scale;
   float tokscale[NTG][2];  // layer scale x per-token x2 scale of this lane's output tokens
