@@ -155,14 +155,17 @@ __device__ __forceinline__ void stage_item(const uint8_t *tbl, uint32_t off_e8p,
 template <int K>
 constexpr int nquads() { return K == QS_CB_E8P ? 2 : 1; }
 
+// 32-bit index arithmetic throughout (items < 2^31 / 1024, batch * m < 2^31:
+// checked by the launcher), which keeps the per-item integer work small.
 template <int K0, int K1, int NST>
-__device__ __forceinline__ void load_item(const GemvArgs &a, int64_t it, int lane, uint4 (&q)[4]) {
-  const uint8_t *p0 = a.stage[0] + it * item_bytes(K0) + lane * 16;
+__device__ __forceinline__ void load_item(const GemvArgs &a, uint32_t it, int lane, uint4 (&q)[4]) {
+  constexpr uint32_t b0 = K0 == QS_CB_E8P ? 1024u : 512u, b1 = K1 == QS_CB_E8P ? 1024u : 512u;
+  const uint8_t *p0 = a.stage[0] + (it * b0 + static_cast<uint32_t>(lane) * 16u);
   q[0] = ldg_nc_v4(p0);
   if constexpr (K0 == QS_CB_E8P) q[1] = ldg_nc_v4(p0 + 512);
   if constexpr (NST == 2) {
     constexpr int o = nquads<K0>();
-    const uint8_t *p1 = a.stage[1] + it * item_bytes(K1) + lane * 16;
+    const uint8_t *p1 = a.stage[1] + (it * b1 + static_cast<uint32_t>(lane) * 16u);
     q[o] = ldg_nc_v4(p1);
     if constexpr (K1 == QS_CB_E8P) q[o + 1] = ldg_nc_v4(p1 + 512);
   }
@@ -173,10 +176,11 @@ __device__ __forceinline__ void load_item(const GemvArgs &a, int64_t it, int lan
 // coordinate pairs (0,2), (1,3), (4,6), (5,7) of each code (the order of the
 // decoded weight words), sf the per-code sums as (code 2p+1, code 2p) f16x2
 // pairs (B operands of the shift mma).
-__device__ __forceinline__ void load_activations(const GemvArgs &a, int64_t kc, int g, int t,
+__device__ __forceinline__ void load_activations(const GemvArgs &a, uint32_t kc, int g, int t,
                                                  uint32_t (&bf)[32], uint32_t (&sf)[4]) {
   if (g < a.ntok) {
-    const uint4 *src = reinterpret_cast<const uint4 *>(a.x2h + (a.tok0 + g) * a.n_pad + kc * 256 + t * 64);
+    const uint4 *src = reinterpret_cast<const uint4 *>(
+        a.x2h + (static_cast<uint32_t>(a.tok0 + g) * static_cast<uint32_t>(a.n_pad) + kc * 256u + t * 64u));
     float sum[8];
 #pragma unroll
     for (int c = 0; c < 8; ++c) {
@@ -217,7 +221,9 @@ __global__ void __launch_bounds__(kGemvThreads, NTG == 1 ? 2 : 1) gemv_kernel(Ge
   const int lane = threadIdx.x & 31;
   const int64_t warp = blockIdx.x * (kGemvThreads / 32) + (threadIdx.x >> 5);
   const int64_t nwarps = static_cast<int64_t>(gridDim.x) * (kGemvThreads / 32);
-  const int64_t start = warp * a.items / nwarps, end = (warp + 1) * a.items / nwarps;
+  const uint32_t start = static_cast<uint32_t>(warp * a.items / nwarps);
+  const uint32_t end = static_cast<uint32_t>((warp + 1) * a.items / nwarps);
+  const uint32_t m = static_cast<uint32_t>(a.m), RT = static_cast<uint32_t>(a.RT);
   // prologue, independent of the previous kernel: first weights in flight, table fill
   uint4 q[4], nq[4];
   if (start < end) load_item<K0, K1, NST>(a, start, lane, q);
@@ -240,10 +246,10 @@ __global__ void __launch_bounds__(kGemvThreads, NTG == 1 ? 2 : 1) gemv_kernel(Ge
     }
 
   uint32_t bf[NTG][32], sf[NTG][4];
-  int64_t kc = start / a.RT, rt = start % a.RT;
+  uint32_t kc = start / RT, rt = start % RT;
 #pragma unroll
   for (int tg = 0; tg < NTG; ++tg) load_activations(a, kc, 8 * tg + g, t, bf[tg], sf[tg]);
-  for (int64_t it = start; it < end; ++it) {
+  for (uint32_t it = start; it < end; ++it) {
     if (it + 1 < end) load_item<K0, K1, NST>(a, it + 1, lane, nq);
 
     float acc0[NTG][4], acc0b[NTG][4], acc1[NTG][4], acc1b[NTG][4];
@@ -258,14 +264,14 @@ __global__ void __launch_bounds__(kGemvThreads, NTG == 1 ? 2 : 1) gemv_kernel(Ge
     }
 
     // epilogue: c0 (row g, tok 2t), c1 (row g, tok 2t+1), c2/c3 rows g+8
-    const int64_t row0 = rt * kRowsPerTile + g, row1 = row0 + 8;
+    const uint32_t row0 = rt * kRowsPerTile + g, row1 = row0 + 8;
 #pragma unroll
     for (int tg = 0; tg < NTG; ++tg) {
 #pragma unroll
       for (int j = 0; j < 2; ++j) {
         const int tok = 8 * tg + 2 * t + j;
         if (tok < a.ntok) {
-          const int gt = a.tok0 + tok;
+          const uint32_t gt = static_cast<uint32_t>(a.tok0 + tok);
           const float f = tokscale[tg][j];
           float v0 = a.sscale[0] * (acc0[tg][j] + acc0b[tg][j]);
           float v1 = a.sscale[0] * (acc0[tg][2 + j] + acc0b[tg][2 + j]);
@@ -273,14 +279,14 @@ __global__ void __launch_bounds__(kGemvThreads, NTG == 1 ? 2 : 1) gemv_kernel(Ge
             v0 = fmaf(a.sscale[1], acc1[tg][j] + acc1b[tg][j], v0);
             v1 = fmaf(a.sscale[1], acc1[tg][2 + j] + acc1b[tg][2 + j], v1);
           }
-          if (row0 < a.m) atomicAdd(a.y1 + gt * a.m + row0, v0 * f);
-          if (row1 < a.m) atomicAdd(a.y1 + gt * a.m + row1, v1 * f);
+          if (row0 < m) atomicAdd(a.y1 + (gt * m + row0), v0 * f);
+          if (row1 < m) atomicAdd(a.y1 + (gt * m + row1), v1 * f);
         }
       }
     }
 #pragma unroll
     for (int i = 0; i < 4; ++i) q[i] = nq[i];
-    if (++rt == a.RT) {
+    if (++rt == RT) {
       rt = 0;
       ++kc;
       if (it + 1 < end) {
@@ -327,6 +333,11 @@ int launch_matmul(const void *x2ws, int64_t batch, int64_t n, int64_t m, const v
                   const float *layer_scale, float *y1, cudaStream_t s) {
   if (batch >= kTcMinBatch)
     return launch_matmul_tc(x2ws, batch, n, m, packed, stages, kinds, stage_scales, layer_scale, y1, s);
+  // the decode kernel indexes with 32 bits
+  if (batch * m >= (int64_t(1) << 31) || (padded_m(m) / kRowsPerTile) * (padded_T(n) / kCodesPerChunk) * 1024 >=
+      (int64_t(1) << 31) || batch * padded_T(n) * 8 >= (int64_t(1) << 31))
+    return fail(QS_ERR_UNSUPPORTED, "decode matmul of %lld x %lld at batch %lld exceeds 32-bit indexing",
+                (long long)m, (long long)n, (long long)batch);
   GemvArgs a{};
   a.n_pad = padded_T(n) * 8;
   a.x2h = static_cast<const __half *>(x2ws);
