@@ -104,6 +104,7 @@ __device__ __forceinline__ void shift_words(uint32_t w3, uint32_t (&sw)[4]) {
 // One stage of one item: 8 codes for each of the lane's two rows (16 mma per
 // token group), plus 2 mma per token group for the E8P shifts against the
 // per-code activation sums sf.  Each decoded fragment feeds all NTG groups.
+// acc / acc2 are outputs (the first mma starts them from zero).
 template <int KIND, int NTG>
 __device__ __forceinline__ void stage_item(const uint8_t *tbl, uint32_t off_e8p, uint32_t off_1b, const uint4 &qa,
                                            const uint4 &qb, const uint32_t (&bf)[NTG][32],
@@ -122,8 +123,13 @@ __device__ __forceinline__ void stage_item(const uint8_t *tbl, uint32_t off_e8p,
                 imul(fhib, 1u << c), imul(fhib, 256u << c), Wb);
 #pragma unroll
       for (int tg = 0; tg < NTG; ++tg) {
-        mma_16816(acc[tg], Wa[0], Wb[0], Wa[1], Wb[1], bf[tg][4 * c + 0], bf[tg][4 * c + 1]);
-        mma_16816(acc2[tg], Wa[2], Wb[2], Wa[3], Wb[3], bf[tg][4 * c + 2], bf[tg][4 * c + 3]);
+        if (c == 0) {  // the first products start the accumulators
+          mma_16816_zc(acc[tg], Wa[0], Wb[0], Wa[1], Wb[1], bf[tg][4 * c + 0], bf[tg][4 * c + 1]);
+          mma_16816_zc(acc2[tg], Wa[2], Wb[2], Wa[3], Wb[3], bf[tg][4 * c + 2], bf[tg][4 * c + 3]);
+        } else {
+          mma_16816(acc[tg], Wa[0], Wb[0], Wa[1], Wb[1], bf[tg][4 * c + 0], bf[tg][4 * c + 1]);
+          mma_16816(acc2[tg], Wa[2], Wb[2], Wa[3], Wb[3], bf[tg][4 * c + 2], bf[tg][4 * c + 3]);
+        }
       }
     }
     uint32_t swa[4], swb[4];
@@ -143,8 +149,13 @@ __device__ __forceinline__ void stage_item(const uint8_t *tbl, uint32_t off_e8p,
       onebit_words(tbl, off_1b, c < 4 ? qa.z : qa.w, c & 3, Wb);
 #pragma unroll
       for (int tg = 0; tg < NTG; ++tg) {
-        mma_16816(acc[tg], Wa[0], Wb[0], Wa[1], Wb[1], bf[tg][4 * c + 0], bf[tg][4 * c + 1]);
-        mma_16816(acc2[tg], Wa[2], Wb[2], Wa[3], Wb[3], bf[tg][4 * c + 2], bf[tg][4 * c + 3]);
+        if (c == 0) {  // the first products start the accumulators
+          mma_16816_zc(acc[tg], Wa[0], Wb[0], Wa[1], Wb[1], bf[tg][4 * c + 0], bf[tg][4 * c + 1]);
+          mma_16816_zc(acc2[tg], Wa[2], Wb[2], Wa[3], Wb[3], bf[tg][4 * c + 2], bf[tg][4 * c + 3]);
+        } else {
+          mma_16816(acc[tg], Wa[0], Wb[0], Wa[1], Wb[1], bf[tg][4 * c + 0], bf[tg][4 * c + 1]);
+          mma_16816(acc2[tg], Wa[2], Wb[2], Wa[3], Wb[3], bf[tg][4 * c + 2], bf[tg][4 * c + 3]);
+        }
       }
     }
   }
@@ -249,20 +260,15 @@ __global__ void __launch_bounds__(kGemvThreads, NTG == 1 ? 2 : 1) gemv_kernel(Ge
   uint32_t kc = start / RT, rt = start % RT;
 #pragma unroll
   for (int tg = 0; tg < NTG; ++tg) load_activations(a, kc, 8 * tg + g, t, bf[tg], sf[tg]);
-  for (uint32_t it = start; it < end; ++it) {
-    if (it + 1 < end) load_item<K0, K1, NST>(a, it + 1, lane, nq);
-
+  // One item: decode + mma of both stages from the quads in qq, atomics into y1,
+  // then advance the row tile (and the activations at a code-chunk boundary).
+  auto process = [&](uint32_t it, const uint4 (&qq)[4]) {
     float acc0[NTG][4], acc0b[NTG][4], acc1[NTG][4], acc1b[NTG][4];
-#pragma unroll
-    for (int tg = 0; tg < NTG; ++tg)
-#pragma unroll
-      for (int i = 0; i < 4; ++i) acc0[tg][i] = acc0b[tg][i] = acc1[tg][i] = acc1b[tg][i] = 0.f;
-    stage_item<K0, NTG>(tbl, off_e8p, off_1b, q[0], q[nquads<K0>() - 1], bf, sf, acc0, acc0b);
+    stage_item<K0, NTG>(tbl, off_e8p, off_1b, qq[0], qq[nquads<K0>() - 1], bf, sf, acc0, acc0b);
     if constexpr (NST == 2) {
       constexpr int o = nquads<K0>();
-      stage_item<K1, NTG>(tbl, off_e8p, off_1b, q[o], q[o + nquads<K1>() - 1], bf, sf, acc1, acc1b);
+      stage_item<K1, NTG>(tbl, off_e8p, off_1b, qq[o], qq[o + nquads<K1>() - 1], bf, sf, acc1, acc1b);
     }
-
     // epilogue: c0 (row g, tok 2t), c1 (row g, tok 2t+1), c2/c3 rows g+8
     const uint32_t row0 = rt * kRowsPerTile + g, row1 = row0 + 8;
 #pragma unroll
@@ -284,8 +290,6 @@ __global__ void __launch_bounds__(kGemvThreads, NTG == 1 ? 2 : 1) gemv_kernel(Ge
         }
       }
     }
-#pragma unroll
-    for (int i = 0; i < 4; ++i) q[i] = nq[i];
     if (++rt == RT) {
       rt = 0;
       ++kc;
@@ -294,6 +298,14 @@ __global__ void __launch_bounds__(kGemvThreads, NTG == 1 ? 2 : 1) gemv_kernel(Ge
         for (int tg = 0; tg < NTG; ++tg) load_activations(a, kc, 8 * tg + g, t, bf[tg], sf[tg]);
       }
     }
+  };
+  // two items per trip with ping-pong quad registers (no copies between items)
+  for (uint32_t it = start; it < end; it += 2) {
+    if (it + 1 < end) load_item<K0, K1, NST>(a, it + 1, lane, nq);
+    process(it, q);
+    if (it + 1 >= end) break;
+    if (it + 2 < end) load_item<K0, K1, NST>(a, it + 2, lane, q);
+    process(it + 1, nq);
   }
 }
 
