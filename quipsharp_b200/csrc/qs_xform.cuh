@@ -9,8 +9,8 @@
 //    shared memory).  Few rows (decode) spread a long row over a cluster so
 //    its latency is divided over several SMs; many rows (prefill) run one CTA
 //    per row, or a small cluster when a row does not fit one SM's shared
-//    memory twice.  (Many rows of the RFFT's N = P * 2^a widths use the
-//    two-pass kernels of qs_xform2.cu instead.)
+//    memory twice.  (The RFFT's N = P * 2^a >= 4096 widths use the two-pass
+//    kernels of qs_xform2.cu instead, for few rows and many.)
 //  * The row lives in two shared buffers (ping-pong), distributed cyclically:
 //    element e sits in CTA e mod C at local index e / C, so butterfly j, whose
 //    inputs are j + r * nb with C dividing nb, finds them all in CTA j mod C;

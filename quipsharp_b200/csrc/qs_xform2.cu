@@ -306,8 +306,8 @@ __host__ __device__ constexpr int spread_groups(int P) {
   return G;
 }
 constexpr int kSpreadGroupsMax = 4;
-// Largest prime of the few-row two-pass path: above it the column DFTs are long
-// enough that the one-pass cluster plan of qs_transform.cu is as fast.
+// Largest prime whose spread pass A splits a column over lanes (xcol_spread_kernel);
+// larger primes take a warp per column (xcol_warp_kernel).
 constexpr int kSpreadMaxPrime = 13;
 
 template <int P, bool OUT, int G, int g>
@@ -404,6 +404,107 @@ __global__ void __launch_bounds__(256) xcol_spread_kernel(const void *x, int dty
   if constexpr (!OUT) {
     for (int o = 16; o > 0; o >>= 1) l1 += __shfl_xor_sync(0xffffffffu, l1, o);
     if ((threadIdx.x & 31) == 0) partial[t >> 5] = l1;
+  }
+}
+
+// Spread pass A for the primes above kSpreadMaxPrime: a warp per column
+// (columns j1 of the rows' N1 x P layout, inputs j1 + j2 * N1), lane k computing
+// output pair k (lane 0 the DC term).  Lane l loads inputs l and l + 32, the
+// conjugate-pair sums a_r = x_r + x_{P-r}, b_r = x_r - x_{P-r} (one shuffle) are
+// staged per warp in shared memory and read back as broadcasts, and lane k
+// holds its H cos / sin coefficients in registers, formed by rotation before
+// the dependent-launch wait.  Outputs get the four-step twiddles and land in
+// place (every lane loads the column before any lane stores).  The input step
+// also writes the column's L1 norm to partial[column].
+constexpr int kColWarpsMax = 4;
+
+template <int P, bool OUT>
+__global__ void __launch_bounds__(32 * kColWarpsMax) xcol_warp_kernel(const void *x, int dtype, const float2 *phase,
+                                                                     float2 *y, float *partial, int N, int lgN1,
+                                                                     int64_t cols) {
+  constexpr int H = (P - 1) / 2;
+  __shared__ float4 stage_all[kColWarpsMax][H + 1];
+  pdl_launch_dependents();
+  const int lane = threadIdx.x & 31, w = threadIdx.x >> 5;
+  float cr[H], sr[H];
+  {
+    float sk, ck;
+    sincospif(2.0f * static_cast<float>(lane <= H ? lane : 0) / static_cast<float>(P), &sk, &ck);
+    float2 z = make_float2(ck, sk);
+#pragma unroll
+    for (int r = 0; r < H; ++r) {
+      cr[r] = z.x;
+      sr[r] = z.y;
+      z = xcmul(z, make_float2(ck, sk));
+    }
+  }
+  pdl_wait();  // OUT: y1 comes from the matmul; IN: x may be the previous kernel's output
+  const int64_t c = static_cast<int64_t>(blockIdx.x) * (blockDim.x >> 5) + w;
+  if (c >= cols) return;  // whole warps leave together
+  const int64_t b = c >> lgN1;
+  const int j1 = static_cast<int>(c & ((int64_t(1) << lgN1) - 1));
+  float2 *__restrict__ col = y + b * N + j1;
+  auto load = [&](int j2) -> float2 {
+    const int o = j2 << lgN1;
+    if constexpr (OUT) {
+      return col[o];
+    } else {
+      const int64_t e = b * N + j1 + o;
+      float2 z;
+      if (dtype == QS_F16) z = __half22float2(reinterpret_cast<const __half2 *>(x)[e]);
+      else if (dtype == QS_BF16) z = __bfloat1622float2(reinterpret_cast<const __nv_bfloat162 *>(x)[e]);
+      else z = reinterpret_cast<const float2 *>(x)[e];
+      return xcmul(z, phase[j1 + o]);
+    }
+  };
+  const float2 v0 = lane < P ? load(lane) : make_float2(0.f, 0.f);
+  const float2 v1 = lane + 32 < P ? load(lane + 32) : make_float2(0.f, 0.f);
+  if constexpr (!OUT) {
+    float l1 = fabsf(v0.x) + fabsf(v0.y) + fabsf(v1.x) + fabsf(v1.y);
+    for (int o = 16; o > 0; o >>= 1) l1 += __shfl_xor_sync(0xffffffffu, l1, o);
+    if (lane == 0) partial[c] = l1;
+  }
+  const int src = (P - lane) & 31;  // lane holding x_{P - lane}, in its second register when P - lane >= 32
+  const float2 u0 = make_float2(__shfl_sync(0xffffffffu, v0.x, src), __shfl_sync(0xffffffffu, v0.y, src));
+  const float2 u1 = make_float2(__shfl_sync(0xffffffffu, v1.x, src), __shfl_sync(0xffffffffu, v1.y, src));
+  const float2 xm = (lane >= 1 && P - lane >= 32) ? u1 : u0;
+  float4 *st = stage_all[w];
+  if (lane == 0) st[0] = make_float4(v0.x, v0.y, 0.f, 0.f);
+  else if (lane <= H) st[lane] = make_float4(v0.x + xm.x, v0.y + xm.y, v0.x - xm.x, v0.y - xm.y);
+  __syncwarp();  // the column is in registers / shared memory: stores into it may start
+  const float4 x0 = st[0];
+  float2 A = make_float2(x0.x, x0.y), A2 = make_float2(0.f, 0.f), B = A2, B2 = A2;
+#pragma unroll
+  for (int r = 0; r < H; ++r) {
+    const float4 ab = st[1 + r];
+    if (r & 1) {
+      A2.x = fmaf(ab.x, cr[r], A2.x);
+      A2.y = fmaf(ab.y, cr[r], A2.y);
+      B2.x = fmaf(ab.z, sr[r], B2.x);
+      B2.y = fmaf(ab.w, sr[r], B2.y);
+    } else {
+      A.x = fmaf(ab.x, cr[r], A.x);
+      A.y = fmaf(ab.y, cr[r], A.y);
+      B.x = fmaf(ab.z, sr[r], B.x);
+      B.y = fmaf(ab.w, sr[r], B.y);
+    }
+  }
+  A = xcadd(A, A2);
+  B = xcadd(B, B2);
+  if (lane == 0) {
+    col[0] = A;  // k = 0: every coefficient is 1, twiddle 1
+  } else if (lane <= H) {
+    const int k = lane;
+    float sn, cs;
+    sincospif(2.0f * static_cast<float>((j1 * k) % N) / static_cast<float>(N), &sn, &cs);
+    const float2 wk = make_float2(cs, OUT ? sn : -sn);  // W_N^(j1 k) (conjugate for the inverse)
+    sincospif(2.0f * static_cast<float>(j1) / static_cast<float>(1 << lgN1), &sn, &cs);
+    const float2 wP = make_float2(cs, OUT ? sn : -sn);  // W_N^(j1 P) = W_N1^j1
+    const float2 miB = make_float2(B.y, -B.x);          // -iB
+    const float2 Xk = OUT ? xcsub(A, miB) : xcadd(A, miB);
+    const float2 Xm = OUT ? xcadd(A, miB) : xcsub(A, miB);
+    col[k << lgN1] = xcmul(Xk, wk);
+    col[(P - k) << lgN1] = xcmul(Xm, xcmul(wP, xconj(wk)));
   }
 }
 
@@ -524,7 +625,7 @@ static int xnum_sms2() {
 }
 
 // Half widths that use the two-pass path: N = P * 2^a >= 4096, P an odd prime
-// <= 43, 2^a >= 64; few rows (spread mode) only for P <= kSpreadMaxPrime.
+// <= 43, 2^a >= 64.
 static bool spread_mode(int64_t rows) { return rows * 2 <= xnum_sms2(); }
 
 bool two_pass_rfft(int64_t N, int64_t rows, int *P_out, int *lgN1_out) {
@@ -537,7 +638,6 @@ bool two_pass_rfft(int64_t N, int64_t rows, int *P_out, int *lgN1_out) {
     }
   }
   if (!P || (N / P) % P == 0) return false;
-  if (spread_mode(rows) && P > kSpreadMaxPrime) return false;
   const int64_t N1 = N / P;
   if (N1 < 64 || (N1 & (N1 - 1))) return false;
   int lg = 0;
@@ -551,7 +651,8 @@ int64_t two_pass_input_scratch_bytes(int64_t batch, int64_t n) {
   int P, lg;
   if (n % 2 || !two_pass_rfft(n / 2, batch, &P, &lg)) return 0;
   const int64_t N = n / 2, N1 = int64_t(1) << lg;
-  return round_up(batch * N * 8, 256) + round_up(batch * (N1 * kSpreadGroupsMax / 32) * 4, 256);
+  // L1 partial sums: N1 / 32 * G per row (lane-split columns), N1 per row (a warp per column)
+  return round_up(batch * N * 8, 256) + round_up(batch * N1 * 4, 256);
 }
 
 // Plan of the N1-point block FFT.  Warp per block (N1 <= 512): first radix
@@ -615,8 +716,22 @@ static int launch_col_spread(int P, const void *x, int dtype, const float2 *phas
   switch (P) {
 #define QS_COL(Q) \
   case Q: return launch_pdl("two_pass_columns", xcol_spread_kernel<Q, OUT>, grid, dim3(256), 0, s, x, dtype, phase, y, partial, N, lgN1, tasks);
-    QS_COL(3) QS_COL(5) QS_COL(7) QS_COL(11) QS_COL(13) QS_COL(17) QS_COL(19) QS_COL(23) QS_COL(29) QS_COL(31)
-    QS_COL(37) QS_COL(41) QS_COL(43)
+    QS_COL(3) QS_COL(5) QS_COL(7) QS_COL(11) QS_COL(13)
+#undef QS_COL
+    default: return fail(QS_ERR_UNSUPPORTED, "two-pass FFT: bad prime %d", P);
+  }
+}
+
+template <bool OUT>
+static int launch_col_warp(int P, const void *x, int dtype, const float2 *phase, float2 *y, float *partial, int N,
+                           int lgN1, int64_t cols, cudaStream_t s) {
+  // one warp per CTA while the columns alone leave SMs idle (latency), else kColWarpsMax
+  const int wpc = cols <= xnum_sms2() ? 1 : kColWarpsMax;
+  const dim3 grid(static_cast<unsigned>(ceil_div(cols, wpc)));
+  switch (P) {
+#define QS_COL(Q) \
+  case Q: return launch_pdl("two_pass_columns", xcol_warp_kernel<Q, OUT>, grid, dim3(32 * wpc), 0, s, x, dtype, phase, y, partial, N, lgN1, cols);
+    QS_COL(17) QS_COL(19) QS_COL(23) QS_COL(29) QS_COL(31) QS_COL(37) QS_COL(41) QS_COL(43)
 #undef QS_COL
     default: return fail(QS_ERR_UNSUPPORTED, "two-pass FFT: bad prime %d", P);
   }
@@ -670,9 +785,11 @@ int launch_two_pass_output(float *y1, int64_t batch, int64_t m, const float2 *ph
   if (!two_pass_rfft(N, batch, &P, &lg)) return fail(QS_ERR_INVALID_ARG, "two-pass FFT not applicable");
   float2 *yc = reinterpret_cast<float2 *>(y1);
   const bool spread = spread_mode(batch);
-  int st = spread ? launch_col_spread<true>(P, nullptr, 0, nullptr, yc, nullptr, static_cast<int>(N), lg,
-                                            (batch << lg) * spread_groups(P), s)
-                  : launch_col<true>(P, nullptr, 0, nullptr, yc, nullptr, static_cast<int>(N), lg, batch << lg, s);
+  int st = !spread ? launch_col<true>(P, nullptr, 0, nullptr, yc, nullptr, static_cast<int>(N), lg, batch << lg, s)
+           : P > kSpreadMaxPrime
+               ? launch_col_warp<true>(P, nullptr, 0, nullptr, yc, nullptr, static_cast<int>(N), lg, batch << lg, s)
+               : launch_col_spread<true>(P, nullptr, 0, nullptr, yc, nullptr, static_cast<int>(N), lg,
+                                         (batch << lg) * spread_groups(P), s);
   if (st) return st;
   XBlkArgs a{};
   a.y = yc;
@@ -698,9 +815,11 @@ int launch_two_pass_input(const void *x, int dtype, int64_t batch, int64_t n, co
   float *partial = reinterpret_cast<float *>(static_cast<char *>(scratch) + round_up(batch * N * 8, 256));
   const bool spread = spread_mode(batch);
   if (!spread && y1) return fail(QS_ERR_INVALID_ARG, "two-pass FFT: y1 zeroing only in spread mode");
-  int st = spread ? launch_col_spread<false>(P, x, dtype, phase, yc, partial, static_cast<int>(N), lg,
-                                             (batch << lg) * spread_groups(P), s)
-                  : launch_col<false>(P, x, dtype, phase, yc, partial, static_cast<int>(N), lg, batch << lg, s);
+  const bool colwarp = spread && P > kSpreadMaxPrime;
+  int st = !spread ? launch_col<false>(P, x, dtype, phase, yc, partial, static_cast<int>(N), lg, batch << lg, s)
+           : colwarp ? launch_col_warp<false>(P, x, dtype, phase, yc, partial, static_cast<int>(N), lg, batch << lg, s)
+                     : launch_col_spread<false>(P, x, dtype, phase, yc, partial, static_cast<int>(N), lg,
+                                                (batch << lg) * spread_groups(P), s);
   if (st) return st;
   XBlkArgs a{};
   a.y = yc;
@@ -709,7 +828,7 @@ int launch_two_pass_input(const void *x, int dtype, int64_t batch, int64_t n, co
   a.N1 = 1 << lg;
   a.scale = scale;
   a.partial = partial;
-  a.nparts = (1 << lg) / 32 * (spread ? spread_groups(P) : 1);
+  a.nparts = colwarp ? (1 << lg) : (1 << lg) / 32 * (spread ? spread_groups(P) : 1);
   a.x2h = x2h;
   a.rowscale = rowscale;
   a.n_pad = n_pad;

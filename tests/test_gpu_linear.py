@@ -94,6 +94,9 @@ def test_forward_config_shapes_vs_reference(golden_configs, cfg):
     (2048, 1024, (syn.E8P, syn.E8_1BIT), 12, torch.float16),      # 3-bit RVQ, 9..16 tokens in one pass
     (512, 1024, (syn.E8_1BIT, syn.E8P), 11, torch.bfloat16),      # 1-bit first stage, one pass
     (384, 512, (syn.E8P, syn.E8P), 16, torch.float32),            # 4-bit RVQ at the one-pass limit
+    (11008, 1024, (syn.E8P,), 1, torch.float32),                  # output 5504 = 43 x 128: warp-per-column pass A
+    (4096, 11008, (syn.E8P, syn.E8_1BIT), 4, torch.float16),      # input 5504: warp-per-column pass A + L1 scale
+    (3584, 18944, (syn.E8P,), 2, torch.bfloat16),                 # input 9472 = 37 x 256
 ])
 def test_forward_shapes_vs_oracle(m, n, kinds, B, dt):
     lay = syn.make_layer(m, n, kinds, seed=m + n + B, has_bias=True)
