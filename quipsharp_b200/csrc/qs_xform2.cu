@@ -363,6 +363,7 @@ __global__ void __launch_bounds__(256) xcol_spread_kernel(const void *x, int dty
                                                           float *partial, int N, int lgN1, int64_t tasks) {
   constexpr int G = spread_groups(P);
   pdl_launch_dependents();
+  if constexpr (!OUT) xprefetch_l2(phase, 8 * static_cast<int64_t>(N), blockIdx.x, gridDim.x);
   pdl_wait();
   const int64_t t = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x;
   if (t >= tasks) return;  // tasks = rows * N1 * G, a multiple of 32: whole warps leave together
@@ -438,6 +439,7 @@ __global__ void __launch_bounds__(32 * kColWarpsMax) xcol_warp_kernel(const void
       z = xcmul(z, make_float2(ck, sk));
     }
   }
+  if constexpr (!OUT) xprefetch_l2(phase, 8 * static_cast<int64_t>(N), blockIdx.x, gridDim.x);
   pdl_wait();  // OUT: y1 comes from the matmul; IN: x may be the previous kernel's output
   const int64_t c = static_cast<int64_t>(blockIdx.x) * (blockDim.x >> 5) + w;
   if (c >= cols) return;  // whole warps leave together
@@ -567,6 +569,10 @@ __global__ void __launch_bounds__(256) xblk_spread_kernel(XPlan p1, XBlkArgs a, 
   const bool flag = OUT && blockIdx.x == 0 && threadIdx.x == 0;
   if (flag) xbusy_set(sa.busy, 1);  // dry-pass hint for the next input step (xbusy_flag)
   pdl_launch_dependents();
+  if constexpr (OUT) {  // layer constants of the sink, into L2 while pass A still runs
+    xprefetch_l2(a.phase, 8 * static_cast<int64_t>(a.N), blockIdx.x, gridDim.x);
+    xprefetch_l2(a.bias, 8 * static_cast<int64_t>(a.N), blockIdx.x, gridDim.x);
+  }
   build_xtw(tw, a.N1);
   pdl_wait();
   if (!OUT && sa.y1) {  // zero y1 for the decode matmul: a slice per CTA
