@@ -1,4 +1,5 @@
-"""`QuantizedLinear` on B200 (mirrors quipsharp/checkpoint.py:80-156).
+"""`QuantizedLinear` on B200 (mirrors quipsharp/checkpoint.py:80-156) and the
+compact checkpoint format (checkpoint.py:159-275).
 
 Same constructor, buffers and state_dict keys as the reference module, so a
 reference checkpoint's state dict loads unchanged: `codes` int16 (m, n/8) or
@@ -6,8 +7,21 @@ reference checkpoint's state dict loads unchanged: `codes` int16 (m, n/8) or
 (RFFT, complex64), optional float32 `bias`.  `forward` runs the fused CUDA path:
 the int16 codes are re-laid into the kernel's weight stream once and cached
 (rebuilt automatically when the `codes` buffer is replaced or modified in place).
+
+Checkpoints: a directory with the model's state dict (`quantized_state.pt`) and a
+JSON manifest (`quip_config.json`: model_id, bits, block_size, seed and one entry per
+quantized module), written and read exactly as the reference does, so checkpoints
+saved by either side load in the other.  The reference rebuilds a 3/4-bit RVQ
+codebook at load time by re-fitting its stage scales (a quantization sweep, offline
+work this package does not carry); here the stage scales come from the caller's
+codebook or from an optional `stage_scales` manifest entry that
+`save_quantized_checkpoint` writes (the reference's loader ignores it).  A 2-bit
+codebook needs no scales.
 """
 from __future__ import annotations
+
+import json
+from pathlib import Path
 
 import torch
 from torch import nn, Tensor
@@ -114,3 +128,123 @@ def replace_with_quantized_linear_(parent: nn.Module, attr: str, layer: Quantize
     qlin.codebook = codebook
     setattr(parent, attr, qlin)
     return qlin
+
+
+def codebook_for(bits: str, stage_scales=None):
+    """The codebook a `bits` checkpoint decodes with (checkpoint.py:60-77 builds the
+    same objects): 2-bit: E8P; 3-bit: RVQ [E8P, E8-1bit]; 4-bit: RVQ [E8P, E8P], with
+    the two RVQ stage scales given (they are fitted offline)."""
+    from .codebooks import E8PCodebook, E8OneBitCodebook
+    from .rvq import RVQStage
+    if bits == "2bit":
+        return E8PCodebook()
+    if bits not in ("3bit", "4bit"):
+        raise ValueError(f"unknown bits {bits!r}")
+    if stage_scales is None or len(stage_scales) != 2:
+        raise ValueError(f"a {bits} codebook needs its two RVQ stage scales: pass codebook= (e.g. the "
+                         "quantizer's) or save the checkpoint with stage_scales")
+    second = E8OneBitCodebook() if bits == "3bit" else E8PCodebook()
+    return RVQCodebookAdapter([RVQStage(E8PCodebook(), float(stage_scales[0])),
+                               RVQStage(second, float(stage_scales[1]))])
+
+
+def save_quantized_checkpoint(model: nn.Module, model_id: str, save_path, bits: str, block_size: int,
+                              seed: int, quantized_modules: list, tokenizer=None, stage_scales=None) -> None:
+    """checkpoint.py:159-185: the state dict and the manifest.  `quantized_modules`:
+    one {"name", "in_features", "out_features", "transform_kind"[, "has_bias"]} per
+    QuantizedLinear.  `stage_scales` (RVQ only) is recorded so this package's loader
+    can rebuild the codebook without refitting."""
+    save_path = Path(save_path)
+    save_path.mkdir(parents=True, exist_ok=True)
+    torch.save(model.state_dict(), save_path / STATE_NAME)
+    manifest = {"model_id": model_id, "bits": bits, "block_size": block_size, "seed": seed,
+                "quantized_modules": quantized_modules}
+    if stage_scales is not None:
+        manifest["stage_scales"] = [float(v) for v in stage_scales]
+    (save_path / MANIFEST_NAME).write_text(json.dumps(manifest, indent=2))
+    if tokenizer is not None:
+        tokenizer.save_pretrained(save_path)
+
+
+def is_quantized_checkpoint(path) -> bool:
+    """checkpoint.py:188-189."""
+    return (Path(path) / MANIFEST_NAME).exists()
+
+
+def _meta_skeleton(model_id: str) -> nn.Module:
+    """The architecture of `model_id` on the meta device (no weights), as
+    lazy_weights.py:149-179 builds it; needs the model's config locally (a
+    directory or the Hugging Face cache: there is no download here)."""
+    try:
+        from transformers import AutoConfig, AutoModelForCausalLM
+        full = AutoConfig.from_pretrained(model_id)
+        dtype = getattr(full, "dtype", None) or getattr(full, "torch_dtype", None) or torch.bfloat16
+        with torch.device("meta"):
+            return AutoModelForCausalLM.from_config(full.get_text_config(), dtype=dtype)
+    except Exception as e:  # no transformers, no local config, unknown architecture
+        raise RuntimeError(f"cannot build the architecture of {model_id!r} ({e}); pass model= "
+                           "(a skeleton whose quantized submodules will be replaced)") from e
+
+
+def load_quantized_checkpoint(save_path, device="cuda", gpu_devices=None, gpu_budget_bytes=None,
+                              cpu_budget_bytes=0, *, model: nn.Module | None = None, codebook=None):
+    """checkpoint.py:192-275: rebuild the architecture (or take `model`, a skeleton
+    on any device, meta included), swap in QuantizedLinear modules of the manifest's
+    shapes, load the state dict with assign=True, place it, give every quantized
+    module its codebook and return the model in eval mode.
+
+    Placement: everything on `device` (or gpu_devices[0]) when it fits; a checkpoint
+    above `gpu_budget_bytes` is spread over `gpu_devices` by decoder layer through
+    accelerate, as the reference does, and needs accelerate installed.
+    Codebook: `codebook` if given, else built from the manifest's bits (and its
+    stage_scales for RVQ, see codebook_for)."""
+    save_path = Path(save_path)
+    manifest = json.loads((save_path / MANIFEST_NAME).read_text())
+    state = torch.load(save_path / STATE_NAME, map_location="cpu")
+    if model is None:
+        model = _meta_skeleton(manifest["model_id"])
+    stages = num_rvq_stages(manifest["bits"])
+    for info in manifest["quantized_modules"]:
+        parent_name, _, attr = info["name"].rpartition(".")
+        parent = model.get_submodule(parent_name) if parent_name else model
+        setattr(parent, attr, QuantizedLinear(info["in_features"], info["out_features"], manifest["block_size"],
+                                              info["transform_kind"], num_stages=stages,
+                                              has_bias=info.get("has_bias", False)))
+    model.load_state_dict(state, strict=True, assign=True)
+
+    total_bytes = sum(t.numel() * t.element_size() for t in state.values())
+    if gpu_devices is None or gpu_budget_bytes is None or total_bytes <= gpu_budget_bytes:
+        target = gpu_devices[0] if gpu_devices else device
+        model.to(target)
+    else:
+        try:
+            from accelerate import dispatch_model
+        except ImportError as e:
+            raise NotImplementedError("the checkpoint exceeds gpu_budget_bytes and spreading it over several "
+                                      "devices needs accelerate") from e
+        layer_bytes: dict = {}
+        for key, t in state.items():
+            if key.startswith("model.layers."):
+                i = int(key.split(".")[2])
+                layer_bytes[i] = layer_bytes.get(i, 0) + t.numel() * t.element_size()
+        devices = list(gpu_devices) + (["cpu"] if cpu_budget_bytes else [])
+        budgets = [gpu_budget_bytes] * len(gpu_devices) + ([cpu_budget_bytes] if cpu_budget_bytes else [])
+        device_map, di, used = {}, 0, 0
+        for i in sorted(layer_bytes):
+            while di < len(devices) - 1 and used + layer_bytes[i] > budgets[di]:
+                di, used = di + 1, 0
+            device_map[f"model.layers.{i}"] = devices[di]
+            used += layer_bytes[i]
+        for name, _ in model.model.named_children():
+            if name != "layers":
+                device_map[f"model.{name}"] = gpu_devices[0]
+        if hasattr(model, "lm_head"):
+            device_map["lm_head"] = gpu_devices[0]
+        model = dispatch_model(model, device_map=device_map, main_device=gpu_devices[0])
+
+    shared = codebook if codebook is not None else codebook_for(manifest["bits"], manifest.get("stage_scales"))
+    for info in manifest["quantized_modules"]:
+        # the kernels carry their own tables: one codebook object serves every device
+        model.get_submodule(info["name"]).codebook = shared
+    model.eval()
+    return model

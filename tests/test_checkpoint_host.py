@@ -1,0 +1,85 @@
+"""Checkpoint format (quipsharp/checkpoint.py:159-275) on the host: checkpoints
+written by the REFERENCE's save_quantized_checkpoint (fixtures made by
+tests/golden/make_ckpt_fixture.py) load into this package's modules with every
+buffer intact, and this package's own save / load round-trips, including the
+optional RVQ stage scales that let the loader rebuild a 3-bit codebook."""
+import json
+import os
+import sys
+
+import pytest
+import torch
+
+from quipsharp_b200 import checkpoint as C
+from quipsharp_b200.codebooks import E8PCodebook, E8OneBitCodebook
+
+GOLDEN = os.path.join(os.path.dirname(os.path.abspath(__file__)), "golden")
+sys.path.insert(0, GOLDEN)
+from make_ckpt_fixture import toy_decoder, LAYERS  # noqa: E402
+
+
+def _check_against_state(model, ckpt_dir):
+    state = torch.load(os.path.join(ckpt_dir, C.STATE_NAME), map_location="cpu")
+    got = model.state_dict()
+    assert set(got) == set(state)
+    for k, v in state.items():
+        assert got[k].dtype == v.dtype and got[k].shape == v.shape, k
+        assert torch.equal(got[k].cpu(), v), k
+    for name, n, m, has_bias in LAYERS:
+        q = model.get_submodule(name)
+        assert isinstance(q, C.QuantizedLinear)
+        assert (q.in_features, q.out_features) == (n, m) and (q.bias is not None) == has_bias
+
+
+def test_reference_2bit_checkpoint_loads():
+    d = os.path.join(GOLDEN, "ckpt_ref_2bit")
+    assert C.is_quantized_checkpoint(d)
+    model = C.load_quantized_checkpoint(d, device="cpu", model=toy_decoder())
+    _check_against_state(model, d)
+    assert not model.training
+    for name, *_ in LAYERS:
+        assert isinstance(model.get_submodule(name).codebook, E8PCodebook)
+
+
+def test_reference_3bit_checkpoint_needs_stage_scales():
+    d = os.path.join(GOLDEN, "ckpt_ref_3bit")
+    with pytest.raises(ValueError):
+        C.load_quantized_checkpoint(d, device="cpu", model=toy_decoder())
+    scales = json.load(open(os.path.join(d, "stage_scales.json")))
+    model = C.load_quantized_checkpoint(d, device="cpu", model=toy_decoder(),
+                                        codebook=C.codebook_for("3bit", scales))
+    _check_against_state(model, d)
+    cb = model.get_submodule(LAYERS[0][0]).codebook
+    assert [type(s.codebook) for s in cb.stages] == [E8PCodebook, E8OneBitCodebook]
+    assert [s.scale for s in cb.stages] == [float(v) for v in scales]
+    assert model.get_submodule(LAYERS[1][0]).codes.shape == (2, 384, 32)
+
+
+def test_round_trip_records_stage_scales_and_loads_onto_meta(tmp_path):
+    src = os.path.join(GOLDEN, "ckpt_ref_3bit")
+    scales = json.load(open(os.path.join(src, "stage_scales.json")))
+    model = C.load_quantized_checkpoint(src, device="cpu", model=toy_decoder(),
+                                        codebook=C.codebook_for("3bit", scales))
+    manifest = json.load(open(os.path.join(src, C.MANIFEST_NAME)))
+    out = tmp_path / "ckpt"
+    C.save_quantized_checkpoint(model, manifest["model_id"], out, "3bit", 8, manifest["seed"],
+                                manifest["quantized_modules"], stage_scales=scales)
+    written = json.load(open(out / C.MANIFEST_NAME))
+    # the reference's keys unchanged, plus the stage scales
+    assert {k: written[k] for k in manifest} == manifest and written["stage_scales"] == scales
+    with torch.device("meta"):
+        skeleton = toy_decoder()
+    back = C.load_quantized_checkpoint(out, device="cpu", model=skeleton)
+    _check_against_state(back, out)
+    assert [s.scale for s in back.get_submodule(LAYERS[2][0]).codebook.stages] == scales
+
+
+def test_unknown_architecture_asks_for_a_skeleton():
+    with pytest.raises(RuntimeError, match="model="):
+        C.load_quantized_checkpoint(os.path.join(GOLDEN, "ckpt_ref_2bit"), device="cpu")
+
+
+def test_codebook_for_rejects_bad_bits():
+    with pytest.raises(ValueError):
+        C.codebook_for("5bit")
+    assert isinstance(C.codebook_for("2bit"), E8PCodebook)
