@@ -187,7 +187,8 @@ def _meta_skeleton(model_id: str) -> nn.Module:
 
 
 def load_quantized_checkpoint(save_path, device="cuda", gpu_devices=None, gpu_budget_bytes=None,
-                              cpu_budget_bytes=0, *, model: nn.Module | None = None, codebook=None):
+                              cpu_budget_bytes=0, *, model: nn.Module | None = None, codebook=None,
+                              prepack: bool = True):
     """checkpoint.py:192-275: rebuild the architecture (or take `model`, a skeleton
     on any device, meta included), swap in QuantizedLinear modules of the manifest's
     shapes, load the state dict with assign=True, place it, give every quantized
@@ -197,7 +198,9 @@ def load_quantized_checkpoint(save_path, device="cuda", gpu_devices=None, gpu_bu
     above `gpu_budget_bytes` is spread over `gpu_devices` by decoder layer through
     accelerate, as the reference does, and needs accelerate installed.
     Codebook: `codebook` if given, else built from the manifest's bits (and its
-    stage_scales for RVQ, see codebook_for)."""
+    stage_scales for RVQ, see codebook_for).  prepack: modules placed on a GPU re-lay
+    their codes into the kernels' weight stream (stage 2 of a 3-bit layer at one byte
+    per code) now rather than at their first forward."""
     save_path = Path(save_path)
     manifest = json.loads((save_path / MANIFEST_NAME).read_text())
     state = torch.load(save_path / STATE_NAME, map_location="cpu")
@@ -245,6 +248,9 @@ def load_quantized_checkpoint(save_path, device="cuda", gpu_devices=None, gpu_bu
     shared = codebook if codebook is not None else codebook_for(manifest["bits"], manifest.get("stage_scales"))
     for info in manifest["quantized_modules"]:
         # the kernels carry their own tables: one codebook object serves every device
-        model.get_submodule(info["name"]).codebook = shared
+        q = model.get_submodule(info["name"])
+        q.codebook = shared
+        if prepack and q.codes.is_cuda:
+            q.kernel()
     model.eval()
     return model

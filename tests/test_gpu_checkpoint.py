@@ -30,6 +30,7 @@ def test_loaded_checkpoint_forward_vs_oracle(bits, dt):
                                         codebook=C.codebook_for(bits, scales))
     for i, (name, n, m, _) in enumerate(LAYERS):
         q = model.get_submodule(name)
+        assert q._kernel is not None  # packed at load time
         x = syn.make_activations(3, n, dtype=dt, seed=20 + i)
         y = q(x.cuda())
         torch.cuda.synchronize()
