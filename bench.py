@@ -142,6 +142,37 @@ def gemv_bytes(m, n, kinds, batch):
     return m * n * bits // 8 + batch * n * 2 + batch * m * 4
 
 
+def _two_pass_width(N):
+    """The library's two-pass RFFT width rule (qs_xform2.cu two_pass_rfft): N = P * 2^a
+    >= 4096 with one odd prime P <= 43 (not squared) and 2^a >= 64."""
+    if N < 4096:
+        return False
+    P = 0
+    for q in (43, 41, 37, 31, 29, 23, 19, 17, 13, 11, 7, 5, 3):
+        if N % q == 0:
+            if P:
+                return False
+            P = q
+    if not P or (N // P) % P == 0:
+        return False
+    N1 = N // P
+    return N1 >= 64 and N1 & (N1 - 1) == 0
+
+
+def kernels_per_forward(m, n, batch, sms):
+    """This library's kernel launches for one forward of an (n -> m) layer: input
+    transform (two kernels for a two-pass RFFT width: many rows always, few rows in
+    decode), matmul (batches 9-32: one launch per 16 tokens), output transform (two
+    kernels for a two-pass width)."""
+    pow2 = lambda v: v & (v - 1) == 0
+    matmul = 1 if batch >= 33 or batch <= 8 else math.ceil(batch / 16)
+    if pow2(m) and pow2(n):  # RHT both sides
+        return 1 + matmul + 1
+    inp = 2 if _two_pass_width(n // 2) and (batch >= 33 or 2 * batch <= sms) else 1
+    out = 2 if _two_pass_width(m // 2) else 1
+    return inp + matmul + out
+
+
 def cpu_oracle_forward(m, n, kinds, batch, dtype):
     """A callable running the numpy port of the reference forward (oracle/)
     on one synthetic layer of the workload's shape, on this host's cores."""
@@ -447,8 +478,9 @@ def run_ours(args):
                     "path": "QuantizedLinear.forward (public module) over the layer set x passes per step, replayed "
                             "as a CUDA graph; pinned host input copied in and the last layer's output copied out "
                             "each step"},
-            "gpu_launches": args.steps * R * L * sum(2 + (1 if prefill else (1 if B <= 8 else math.ceil(B / 16)))
-                                                     for _ in layers),
+            "gpu_launches": args.steps * R * L * sum(
+                kernels_per_forward(m, n, B, torch.cuda.get_device_properties(dev).multi_processor_count)
+                for _, m, n in layers),
             "clocks": {"sm_mhz": c["sm_mhz"], "sm_max_mhz": c["sm_max_mhz"], "reasons": c["reasons"]},
         }
         print(json.dumps(line), flush=True)
