@@ -1031,21 +1031,15 @@ __global__ void __launch_bounds__(kXMaxThreads, 1) xinput_rfft_kernel(
   const int N = plan.N;
   const uint32_t *xh = reinterpret_cast<const uint32_t *>(static_cast<const char *>(x) + row * 4 * N);
   const float2 *xf = reinterpret_cast<const float2 *>(static_cast<const char *>(x) + row * 8 * N);
-  // Warm start (few rows, one CTA per row, launched while an output step of
-  // this library still runs): the row transform first runs over zeros (x is
-  // not read, phase is), through the same code as the real pass, so the real
-  // pass finds its instructions and phase_v in this SM's caches.  Its results
-  // are discarded.
-  bool dry = false;
   __shared__ int s_dry;
   if (threadIdx.x == 0) s_dry = ra.warm && ra.busy && *reinterpret_cast<volatile int *>(ra.busy);
   auto gsrc_h = [&](int e) {
-    const uint32_t w = dry ? 0u : xh[e];
+    const uint32_t w = xh[e];
     const float2 z = dtype == QS_F16 ? __half22float2(*reinterpret_cast<const __half2 *>(&w))
                                      : __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162 *>(&w));
     return xcmul(z, phase[e]);
   };
-  auto gsrc_f = [&](int e) { return xcmul(dry ? make_float2(0.f, 0.f) : xf[e], phase[e]); };
+  auto gsrc_f = [&](int e) { return xcmul(xf[e], phase[e]); };
   float amax = 0.f;
   const int rb = xresult_buf(plan);
   float2 *const rbuf = rb ? b1 : b0;
@@ -1057,20 +1051,38 @@ __global__ void __launch_bounds__(kXMaxThreads, 1) xinput_rfft_kernel(
     res(e, z);
   };
   __syncthreads();  // twiddle tables (the first stage may use them), s_dry
-  dry = !CL && s_dry;
-#pragma unroll 1
-  for (int pass = dry ? 0 : 1; pass < 2; ++pass) {
-    if (pass == 1) {
-      if (dry) {
-        xsync<CL>();  // the dry pass's stores land before the real pass rewrites the buffers
-        dry = false;
-        amax = 0.f;
-      }
-      pdl_wait();  // x may be the previous kernel's output; y1 may still be read by it
-      if (y1) xzero_row(y1, row, m_local, m_local * rank / C, m_local * (rank + 1) / C);
-    }
+  if (CL || !s_dry) {  // the plain path (many rows, clusters, no time to spare)
+    pdl_wait();  // x may be the previous kernel's output; y1 may still be read by it
+    if (y1) xzero_row(y1, row, m_local, m_local * rank / C, m_local * (rank + 1) / C);
     if (dtype == QS_F32) xfft_row<BIG, CL>(plan, b0, b1, tw, false, rank, gsrc_f, sink);
     else xfft_row<BIG, CL>(plan, b0, b1, tw, false, rank, gsrc_h, sink);
+  } else if constexpr (!CL) {
+    // Warm start (few rows, one CTA per row, launched while an output step of
+    // this library still runs): the row transform first runs over zeros (x is
+    // not read, phase is), through the same code as the real pass, so the real
+    // pass finds its instructions and phase_v in this SM's caches.  Its results
+    // are discarded.  A separate copy of the plain path, so the plain path
+    // carries none of this.
+    bool dry = true;
+    auto wsrc_h = [&](int e) {
+      const uint32_t w = dry ? 0u : xh[e];
+      const float2 z = dtype == QS_F16 ? __half22float2(*reinterpret_cast<const __half2 *>(&w))
+                                       : __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162 *>(&w));
+      return xcmul(z, phase[e]);
+    };
+    auto wsrc_f = [&](int e) { return xcmul(dry ? make_float2(0.f, 0.f) : xf[e], phase[e]); };
+#pragma unroll 1
+    for (int pass = 0; pass < 2; ++pass) {
+      if (pass == 1) {
+        __syncthreads();  // the dry pass's stores land before the real pass rewrites the buffers
+        dry = false;
+        amax = 0.f;
+        pdl_wait();
+        if (y1) xzero_row(y1, row, m_local, 0, m_local);
+      }
+      if (dtype == QS_F32) xfft_row<BIG, false>(plan, b0, b1, tw, false, 0, wsrc_f, sink);
+      else xfft_row<BIG, false>(plan, b0, b1, tw, false, 0, wsrc_h, sink);
+    }
   }
   const float row_max = xgroup_absmax<CL>(amax, red, slots, rank, C);
   float sc, inv;
@@ -1174,8 +1186,7 @@ __global__ void __launch_bounds__(kXMaxThreads, 1) xinput_rht_kernel(
   __shared__ int s_dry;  // warm start: see xinput_rfft_kernel
   if (threadIdx.x == 0) s_dry = ra.warm && ra.busy && *reinterpret_cast<volatile int *>(ra.busy);
   __syncthreads();
-  bool dry = !CL && s_dry;
-  auto gsrc = [&](int i) { return (dry ? 0.f : load_as_float(x, row * n + i, dtype)) * sv[i]; };
+  auto gsrc = [&](int i) { return load_as_float(x, row * n + i, dtype) * sv[i]; };
   float amax = 0.f;
   const int rb = xresult_buf(plan);
   float *const rbuf = rb ? b1 : b0;
@@ -1185,18 +1196,24 @@ __global__ void __launch_bounds__(kXMaxThreads, 1) xinput_rht_kernel(
     amax = fmaxf(amax, fabsf(v));
     res(i, v);
   };
+  if (CL || !s_dry) {
+    pdl_wait();
+    if (y1) xzero_row(y1, row, m_local, m_local * rank / C, m_local * (rank + 1) / C);
+    xfwht_row<CL>(plan, b0, b1, rank, gsrc, sink);
+  } else if constexpr (!CL) {
+    bool dry = true;
+    auto wsrc = [&](int i) { return (dry ? 0.f : load_as_float(x, row * n + i, dtype)) * sv[i]; };
 #pragma unroll 1
-  for (int pass = dry ? 0 : 1; pass < 2; ++pass) {
-    if (pass == 1) {
-      if (dry) {
-        xsync<CL>();
+    for (int pass = 0; pass < 2; ++pass) {
+      if (pass == 1) {
+        __syncthreads();
         dry = false;
         amax = 0.f;
+        pdl_wait();
+        if (y1) xzero_row(y1, row, m_local, 0, m_local);
       }
-      pdl_wait();
-      if (y1) xzero_row(y1, row, m_local, m_local * rank / C, m_local * (rank + 1) / C);
+      xfwht_row<false>(plan, b0, b1, 0, wsrc, sink);
     }
-    xfwht_row<CL>(plan, b0, b1, rank, gsrc, sink);
   }
   const float row_max = xgroup_absmax<CL>(amax, red, slots, rank, C);
   float sc, inv;
