@@ -66,7 +66,9 @@ def measured_peaks():
 
 
 class ClockSampler:
-    """nvidia-smi clocks / throttle reasons sampled every 200 ms while running."""
+    """nvidia-smi clocks / throttle reasons sampled every 200 ms while running.  Entry
+    waits for the first reading and exit for one more, so even a timed region shorter
+    than the sampling period is bracketed by readings."""
 
     FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
               "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
@@ -85,6 +87,9 @@ class ClockSampler:
                 text=True)
             self.t = threading.Thread(target=self._read, daemon=True)
             self.t.start()
+            t0 = time.time()
+            while not self.lines and time.time() - t0 < 5.0 and self.proc.poll() is None:
+                time.sleep(0.02)
         except Exception:
             self.proc = None
         return self
@@ -95,6 +100,9 @@ class ClockSampler:
 
     def __exit__(self, *exc):
         if self.proc is not None:
+            n0, t0 = len(self.lines), time.time()
+            while len(self.lines) <= n0 and time.time() - t0 < 1.0 and self.proc.poll() is None:
+                time.sleep(0.02)
             self.proc.terminate()
             try:
                 self.proc.wait(timeout=5)
