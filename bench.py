@@ -45,6 +45,9 @@ def parse():
     p.add_argument("--batch", type=int, default=1)
     p.add_argument("--stack", type=int, default=8192, help="layers per step")
     p.add_argument("--cpu-sample-s", type=float, default=15.0)
+    p.add_argument("--tp", action="store_true",
+                   help="tensor-parallel mode (not the default contract): the config's layer set "
+                        "column-sharded over the ranks, strong scaling")
     return p.parse_args()
 
 
@@ -498,10 +501,100 @@ def run_ours(args):
         dist.destroy_process_group()
 
 
+def run_tp(args):
+    """Tensor-parallel mode: every layer of the config's set column-sharded over the
+    ranks (TPQuantizedLinear: local fused matmul, NCCL all-gather of the float32 y1
+    shards, full-width output transform on every rank).  Strong scaling: one batch
+    through the whole set per step, timed eagerly with CUDA events (max over ranks);
+    at one rank the unsharded module runs, as the baseline."""
+    import datetime
+    import torch
+    import torch.distributed as dist
+    from quipsharp_b200 import synthetic as syn
+    from quipsharp_b200.checkpoint import QuantizedLinear
+    from quipsharp_b200.codebooks import E8PCodebook, E8OneBitCodebook
+    from quipsharp_b200.quantize import RVQCodebookAdapter
+    from quipsharp_b200.rvq import RVQStage
+    from quipsharp_b200.tensor_parallel import TPQuantizedLinear
+
+    world, rank, local = dist_env()
+    if world > 1:
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120))
+    torch.cuda.set_device(local)
+    dev = torch.device("cuda", local)
+    layers, kinds, dtype = config_spec(args.config)
+    B = args.batch
+    cb = lambda k: E8PCodebook() if k == "e8p" else E8OneBitCodebook()
+    mods = []
+    for li, (name, m, n) in enumerate(layers):
+        base = syn.make_layer(m, n, kinds, seed=1 + li, layer_scale=1.0 / math.sqrt(1.2 * n))
+        full = QuantizedLinear(n, m, 8, base.transform_kind, num_stages=len(kinds)).to(dev)
+        with torch.no_grad():
+            full.codes.copy_(base.codes.to(dev))
+            full.scale.fill_(base.layer_scale)
+            if base.transform_kind == "rht":
+                full.su.copy_(base.su)
+                full.sv.copy_(base.sv)
+            else:
+                full.phase_u.copy_(base.phase_u)
+                full.phase_v.copy_(base.phase_v)
+        full.codebook = cb(kinds[0]) if len(kinds) == 1 else RVQCodebookAdapter(
+            [RVQStage(cb(k), sc) for k, sc in zip(kinds, base.stage_scales)])
+        if world > 1:
+            mods.append((n, m, TPQuantizedLinear(full)))
+            del full
+        else:
+            full.kernel()
+            mods.append((n, m, full))
+    x0 = syn.make_activations(B, layers[0][2], dtype=dtype, seed=2).to(dev)
+
+    def step():
+        latest = {x0.shape[1]: x0}
+        for n, m, mod in mods:
+            latest[m] = mod(latest[n])
+
+    def timed(k):
+        if world > 1:
+            dist.barrier()
+        torch.cuda.synchronize()
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record()
+        for _ in range(k):
+            step()
+        e1.record()
+        torch.cuda.synchronize()
+        ms = torch.tensor([e0.elapsed_time(e1)], device=dev)
+        if world > 1:
+            dist.all_reduce(ms, op=dist.ReduceOp.MAX)
+        return float(ms.item())
+
+    with torch.no_grad():
+        timed(max(args.warmup, 3))
+        with ClockSampler(local) as clk:
+            ms = timed(args.steps)
+    if rank == 0:
+        c = clk.summary()
+        print(json.dumps({
+            "metric": f"quantized-linear tokens/s ({args.config}, batch {B}, tensor-parallel)",
+            "value": B * args.steps / (ms / 1000.0), "unit": "tokens/s", "n_gpus": world,
+            "steps": args.steps, "warmup": max(args.warmup, 3), "ms_per_step": ms / args.steps,
+            "higher_is_better": True, "scaling": "strong", "vs_baseline": None,
+            "dtype": str(dtype).replace("torch.", "").replace("bfloat16", "bf16").replace("float16", "f16"),
+            "data": "synthetic", "config": {"workload": args.config, "batch": B, "tp": world,
+                                            "layers": [list(l) for l in layers], "timing": "eager, max over ranks"},
+            "clocks": {"sm_mhz": c["sm_mhz"], "sm_max_mhz": c["sm_max_mhz"], "reasons": c["reasons"]},
+        }), flush=True)
+    if world > 1:
+        dist.barrier()
+        dist.destroy_process_group()
+
+
 def main():
     args = parse()
     if args.impl == "reference":
         run_reference(args)
+    elif args.tp:
+        run_tp(args)
     else:
         run_ours(args)
 
