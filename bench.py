@@ -505,8 +505,9 @@ def run_tp(args):
     """Tensor-parallel mode: every layer of the config's set column-sharded over the
     ranks (TPQuantizedLinear: local fused matmul, NCCL all-gather of the float32 y1
     shards, full-width output transform on every rank).  Strong scaling: one batch
-    through the whole set per step, timed eagerly with CUDA events (max over ranks);
-    at one rank the unsharded module runs, as the baseline."""
+    through the whole set per step, replayed as a CUDA graph (collectives included)
+    and timed with CUDA events (max over ranks); at one rank the unsharded module
+    runs, as the baseline."""
     import datetime
     import torch
     import torch.distributed as dist
@@ -553,15 +554,22 @@ def run_tp(args):
         for n, m, mod in mods:
             latest[m] = mod(latest[n])
 
+    stream = torch.cuda.Stream(dev)
+    graph = None
+
     def timed(k):
         if world > 1:
             dist.barrier()
         torch.cuda.synchronize()
         e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-        e0.record()
-        for _ in range(k):
-            step()
-        e1.record()
+        with torch.cuda.stream(stream):
+            e0.record(stream)
+            for _ in range(k):
+                if graph is not None:
+                    graph.replay()
+                else:
+                    step()
+            e1.record(stream)
         torch.cuda.synchronize()
         ms = torch.tensor([e0.elapsed_time(e1)], device=dev)
         if world > 1:
@@ -569,9 +577,18 @@ def run_tp(args):
         return float(ms.item())
 
     with torch.no_grad():
+        timed(max(args.warmup, 3))  # eager warm-up (packing, NCCL communicator set-up)
+        # one step (kernels and the NCCL all-gathers) captured as a CUDA graph and replayed
+        graph = torch.cuda.CUDAGraph()
+        with torch.cuda.stream(stream):
+            torch.cuda.synchronize()
+            with torch.cuda.graph(graph, stream=stream):
+                step()
+        torch.cuda.synchronize()
         timed(max(args.warmup, 3))
         with ClockSampler(local) as clk:
             ms = timed(args.steps)
+    graph = None  # release the graph (it holds NCCL work) before the process group goes
     if rank == 0:
         c = clk.summary()
         print(json.dumps({
@@ -581,7 +598,7 @@ def run_tp(args):
             "higher_is_better": True, "scaling": "strong", "vs_baseline": None,
             "dtype": str(dtype).replace("torch.", "").replace("bfloat16", "bf16").replace("float16", "f16"),
             "data": "synthetic", "config": {"workload": args.config, "batch": B, "tp": world,
-                                            "layers": [list(l) for l in layers], "timing": "eager, max over ranks"},
+                                            "layers": [list(l) for l in layers], "timing": "CUDA graph replay, max over ranks"},
             "clocks": {"sm_mhz": c["sm_mhz"], "sm_max_mhz": c["sm_max_mhz"], "reasons": c["reasons"]},
         }), flush=True)
     if world > 1:
