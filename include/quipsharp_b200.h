@@ -66,6 +66,16 @@ const char *qs_last_error(void);
  * hanging the GPU.  No counterpart in the reference (pure Python). */
 int qs_device_status(qs_stream_t stream);
 
+/* Limit, in nanoseconds, of the bounded waits between the warps of the
+ * pipelined kernels (default 4 s; 0 restores the default), applied to launches
+ * made after the call, process-wide.  A wait that runs out ends its kernel
+ * early with the qs_device_status flag set; the kernel still waits for its own
+ * copies and tensor-core work in flight (fixed 4 s limit) before it exits.
+ * Lower it to detect a stalled pipeline sooner.  No counterpart in the
+ * reference (pure Python). */
+int qs_set_wait_limit_ns(uint64_t ns);
+uint64_t qs_wait_limit_ns(void);
+
 /* Host-only.  Writes the 256x8 float32 table of `kind` (row-major) to host
  * memory: E8P = build_abs_table() (quipsharp/codebooks/e8p.py:84-89),
  * E8_1BIT = build_table() (quipsharp/codebooks/e8_1bit.py:67-71). */
@@ -107,7 +117,7 @@ int qs_fwht(const void *x, int64_t ld_x, void *y, int64_t ld_y, int dtype, int64
 
 /* to_transformed_space (inverse = 0, quipsharp/rfft.py:37-47) and
  * from_transformed_space (inverse = 1, quipsharp/rfft.py:50-60) over rows of
- * length n (even, n/2 <= 16384, prime factors of n/2 at most 43):
+ * length n (even, n/2 <= 32768, prime factors of n/2 at most 43):
  * forward: y = view_as_real(FFT_ortho(view_as_complex(x) * phase));
  * inverse: y = view_as_real(IFFT_ortho(view_as_complex(x)) * conj(phase)).
  * phase is complex64 (interleaved float2) of length n/2 on the device. */

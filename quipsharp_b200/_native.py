@@ -42,6 +42,8 @@ _SIGS = {
     "qs_version": (ctypes.c_char_p, []),
     "qs_last_error": (ctypes.c_char_p, []),
     "qs_device_status": (_I, [_P]),
+    "qs_set_wait_limit_ns": (_I, [ctypes.c_uint64]),
+    "qs_wait_limit_ns": (ctypes.c_uint64, []),
     "qs_codebook_table": (_I, [_I, _P]),
     "qs_decode": (_I, [_I, _P, _I, _L, _P, _P]),
     "qs_rvq_decode": (_I, [_I, _P, _P, _I, _P, _L, _P, _P]),

@@ -186,6 +186,77 @@ def _meta_skeleton(model_id: str) -> nn.Module:
                            "(a skeleton whose quantized submodules will be replaced)") from e
 
 
+def split_layers(layer_bytes: list[int], budgets: list[int]) -> list[int]:
+    """Device index of each decoder layer: contiguous runs whose sizes are
+    proportional to the device budgets.  Layer i goes to the device whose share
+    of the cumulative byte range holds the layer's midpoint; a device that would
+    exceed its budget raises (the checkpoint does not fit)."""
+    total = float(sum(layer_bytes))
+    cap = float(sum(budgets))
+    if total > cap:
+        raise ValueError(f"decoder layers need {int(total)} bytes, budgets allow {int(cap)}")
+    edges, acc = [], 0.0
+    for b in budgets:  # cumulative share boundaries of each device in [0, total]
+        acc += b
+        edges.append(total * acc / cap)
+    out, before, load = [], 0.0, [0] * len(budgets)
+    for size in layer_bytes:
+        mid = before + size / 2.0
+        d = next(i for i, e in enumerate(edges) if mid <= e or i == len(edges) - 1)
+        out.append(d)
+        load[d] += size
+        before += size
+    for d, (l, b) in enumerate(zip(load, budgets)):
+        if l > b:
+            raise ValueError(f"device {d} would hold {l} bytes of decoder layers, over its budget {b}")
+    return out
+
+
+def _move(obj, dev):
+    if torch.is_tensor(obj):
+        return obj.to(dev)
+    if isinstance(obj, (tuple, list)):
+        return type(obj)(_move(o, dev) for o in obj)
+    if isinstance(obj, dict):
+        return {k: _move(v, dev) for k, v in obj.items()}
+    return obj
+
+
+def _follow_inputs(module: nn.Module, dev) -> None:
+    """Move every tensor argument of module's forward onto `dev` first."""
+    module.register_forward_pre_hook(lambda _m, args, kwargs: (_move(args, dev), _move(kwargs, dev)),
+                                     with_kwargs=True)
+
+
+def place_decoder_layers(model: nn.Module, state: dict, devices: list, budgets: list[int]) -> None:
+    """Spread a decoder-only model over `devices` by decoder layer (split_layers
+    on the state dict's per-layer bytes).  The embeddings stay with the first
+    layer, the final norm and head go with the last; every placed module moves
+    its inputs to its own device, so the forward runs unchanged."""
+    body = getattr(model, "model", None)
+    layers = getattr(body, "layers", None)
+    if layers is None:
+        raise NotImplementedError("multi-device placement needs a model with model.layers (decoder-only)")
+    sizes = [0] * len(layers)
+    for key, t in state.items():
+        parts = key.split(".")
+        if len(parts) > 2 and parts[0] == "model" and parts[1] == "layers":
+            sizes[int(parts[2])] += t.numel() * t.element_size()
+    where = split_layers(sizes, budgets)
+    for i, layer in enumerate(layers):
+        layer.to(devices[where[i]])
+        _follow_inputs(layer, devices[where[i]])
+    first, last = devices[where[0]], devices[where[-1]]
+    for name, child in body.named_children():
+        if name != "layers":
+            child.to(first if "embed" in name else last)
+            _follow_inputs(child, first if "embed" in name else last)
+    head = getattr(model, "lm_head", None)
+    if head is not None:
+        head.to(last)
+        _follow_inputs(head, last)
+
+
 def load_quantized_checkpoint(save_path, device="cuda", gpu_devices=None, gpu_budget_bytes=None,
                               cpu_budget_bytes=0, *, model: nn.Module | None = None, codebook=None,
                               prepack: bool = True):
@@ -195,8 +266,8 @@ def load_quantized_checkpoint(save_path, device="cuda", gpu_devices=None, gpu_bu
     module its codebook and return the model in eval mode.
 
     Placement: everything on `device` (or gpu_devices[0]) when it fits; a checkpoint
-    above `gpu_budget_bytes` is spread over `gpu_devices` by decoder layer through
-    accelerate, as the reference does, and needs accelerate installed.
+    above `gpu_budget_bytes` is split over `gpu_devices` (and the host, with
+    `cpu_budget_bytes`) by decoder layer, see place_decoder_layers.
     Codebook: `codebook` if given, else built from the manifest's bits (and its
     stage_scales for RVQ, see codebook_for).  prepack: modules placed on a GPU re-lay
     their codes into the kernels' weight stream (stage 2 of a 3-bit layer at one byte
@@ -220,30 +291,9 @@ def load_quantized_checkpoint(save_path, device="cuda", gpu_devices=None, gpu_bu
         target = gpu_devices[0] if gpu_devices else device
         model.to(target)
     else:
-        try:
-            from accelerate import dispatch_model
-        except ImportError as e:
-            raise NotImplementedError("the checkpoint exceeds gpu_budget_bytes and spreading it over several "
-                                      "devices needs accelerate") from e
-        layer_bytes: dict = {}
-        for key, t in state.items():
-            if key.startswith("model.layers."):
-                i = int(key.split(".")[2])
-                layer_bytes[i] = layer_bytes.get(i, 0) + t.numel() * t.element_size()
         devices = list(gpu_devices) + (["cpu"] if cpu_budget_bytes else [])
         budgets = [gpu_budget_bytes] * len(gpu_devices) + ([cpu_budget_bytes] if cpu_budget_bytes else [])
-        device_map, di, used = {}, 0, 0
-        for i in sorted(layer_bytes):
-            while di < len(devices) - 1 and used + layer_bytes[i] > budgets[di]:
-                di, used = di + 1, 0
-            device_map[f"model.layers.{i}"] = devices[di]
-            used += layer_bytes[i]
-        for name, _ in model.model.named_children():
-            if name != "layers":
-                device_map[f"model.{name}"] = gpu_devices[0]
-        if hasattr(model, "lm_head"):
-            device_map["lm_head"] = gpu_devices[0]
-        model = dispatch_model(model, device_map=device_map, main_device=gpu_devices[0])
+        place_decoder_layers(model, state, devices, budgets)
 
     shared = codebook if codebook is not None else codebook_for(manifest["bits"], manifest.get("stage_scales"))
     for info in manifest["quantized_modules"]:

@@ -58,6 +58,13 @@ QS_API const char *qs_last_error(void) { return g_last_error; }
 
 QS_API int qs_device_status(qs_stream_t stream) { return device_status((cudaStream_t)stream); }
 
+QS_API int qs_set_wait_limit_ns(uint64_t ns) {
+  set_pipeline_wait_ns(ns);
+  return QS_OK;
+}
+
+QS_API uint64_t qs_wait_limit_ns(void) { return pipeline_wait_ns(); }
+
 QS_API int qs_codebook_table(int kind, float *out_host) {
   if (!out_host) return fail(QS_ERR_INVALID_ARG, "null output");
   if (kind == QS_CB_E8P) memcpy(out_host, kE8pAbsF32Host, sizeof(kE8pAbsF32Host));

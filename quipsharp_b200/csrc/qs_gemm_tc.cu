@@ -22,6 +22,7 @@
 // kernel records an error (read by qs_device_status) and winds down.
 #include <cuda.h>
 
+#include <atomic>
 #include <mutex>
 
 #include "qs_common.cuh"
@@ -39,7 +40,11 @@ constexpr int kBN = 256;
 constexpr int kBK = 64;
 constexpr int kATile = kBM * kBK * 2;  // 16 KB
 constexpr int kBTile = kBN * kBK * 2;  // 32 KB
-constexpr uint64_t kWaitLimitNs = 4000000000ull;  // 4 s: far beyond any legitimate wait
+// Drains (waiting for this CTA's own TMA loads and tensor-core ops before it
+// frees shared memory and TMEM) always use this long limit: those operations
+// complete by themselves, so only a broken GPU could exhaust it.  Pipeline waits
+// (on other warps of the CTA) use the run-time limit passed in TcArgs::wait_ns.
+constexpr uint64_t kDrainLimitNs = 4000000000ull;
 
 // Ring stages and decode groups.  A decode group waiting for the MMA to free
 // stage s for its K step ks relies on the MMA having consumed ks - 2S already
@@ -72,6 +77,7 @@ struct TcArgs {
   float *y1;
   int64_t m, m_pad, RT, batch;
   int ksteps;
+  uint64_t wait_ns;  // limit of every pipeline wait (pipeline_wait_ns())
 };
 
 __device__ __forceinline__ void set_error() { atomicExch(&g_tc_error, 1); }
@@ -164,13 +170,14 @@ __global__ void __launch_bounds__(Cfg<NST>::threads, 1) gemm_tc_kernel(const __g
   uint2 *tbl0 = reinterpret_cast<uint2 *>(base + C::ring_bytes);  // stage 0's codebook
   uint2 *tbl1 = tbl0 + C::table_entries;                            // stage 1's (RVQ)
   uint64_t *bars = reinterpret_cast<uint64_t *>(base + C::ring_bytes + C::tables_bytes);
-  // bars: full_a[S], full_b[S], empty[S], acc_full, then the TMEM address holder
+  // bars: full_a[S], full_b[S], empty[S], acc_full, drain, then the TMEM address holder
   const uint32_t bar0 = smem_u32(bars);
   auto full_a = [&](int s) { return bar0 + 8u * s; };
   auto full_b = [&](int s) { return bar0 + 8u * (S + s); };
   auto empty = [&](int s) { return bar0 + 8u * (2 * S + s); };
   const uint32_t acc_full = bar0 + 8u * (3 * S);
-  uint32_t *tmem_holder = reinterpret_cast<uint32_t *>(bars + 3 * S + 1);
+  const uint32_t drain = bar0 + 8u * (3 * S + 1);
+  uint32_t *tmem_holder = reinterpret_cast<uint32_t *>(bars + 3 * S + 2);
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int64_t m0 = static_cast<int64_t>(blockIdx.x) * kBM;
@@ -189,6 +196,7 @@ __global__ void __launch_bounds__(Cfg<NST>::threads, 1) gemm_tc_kernel(const __g
       sm100::mbar_init(empty(s), 1);
     }
     sm100::mbar_init(acc_full, 1);
+    sm100::mbar_init(drain, 1);
     sm100::fence_barrier_init();
     sm100::prefetch_tmap(&tmap_x);
   }
@@ -206,7 +214,7 @@ __global__ void __launch_bounds__(Cfg<NST>::threads, 1) gemm_tc_kernel(const __g
       int issued = 0;
       for (int ks = 0; ks < K; ++ks) {
         const int s = ks % S, use = ks / S;
-        if (use > 0 && !sm100::mbar_wait_bounded(empty(s), (use - 1) & 1, kWaitLimitNs)) {
+        if (use > 0 && !sm100::mbar_wait_bounded(empty(s), (use - 1) & 1, a.wait_ns)) {
           set_error();
           break;
         }
@@ -217,7 +225,7 @@ __global__ void __launch_bounds__(Cfg<NST>::threads, 1) gemm_tc_kernel(const __g
       }
       // wind down: every load this thread issued must have landed before the CTA exits
       for (int ks = issued > S ? issued - S : 0; ks < issued; ++ks)
-        if (!sm100::mbar_wait_bounded(full_b(ks % S), (ks / S) & 1, kWaitLimitNs)) set_error();
+        if (!sm100::mbar_wait_bounded(full_b(ks % S), (ks / S) & 1, kDrainLimitNs)) set_error();
     }
   } else if (warp == 1) {
     // ---- MMA issuer
@@ -226,8 +234,8 @@ __global__ void __launch_bounds__(Cfg<NST>::threads, 1) gemm_tc_kernel(const __g
       bool ok = true;
       for (int ks = 0; ks < K && ok; ++ks) {
         const int s = ks % S, use = ks / S;
-        ok = sm100::mbar_wait_bounded(full_a(s), use & 1, kWaitLimitNs) &&
-             sm100::mbar_wait_bounded(full_b(s), use & 1, kWaitLimitNs);
+        ok = sm100::mbar_wait_bounded(full_a(s), use & 1, a.wait_ns) &&
+             sm100::mbar_wait_bounded(full_b(s), use & 1, a.wait_ns);
         if (!ok) {
           set_error();
           break;
@@ -245,6 +253,10 @@ __global__ void __launch_bounds__(Cfg<NST>::threads, 1) gemm_tc_kernel(const __g
         sm100::umma_commit(empty(s));
       }
       sm100::umma_commit(acc_full);
+      // wind down: every MMA issued must be complete before TMEM and the ring are freed
+      // (on the error path nobody else waits for them)
+      sm100::umma_commit(drain);
+      if (!sm100::mbar_wait_bounded(drain, 0, kDrainLimitNs)) set_error();
     }
   } else {
     // ---- decode producers (group dg of 128 threads, thread r <-> tile row r)
@@ -273,7 +285,7 @@ __global__ void __launch_bounds__(Cfg<NST>::threads, 1) gemm_tc_kernel(const __g
 #pragma unroll
       for (int t = 0; t < SPG; ++t) {
         const int ks = kc * 4 + dg + G * t, s = ks % S, use = ks / S;
-        if (use > 0 && !sm100::mbar_wait_bounded(empty(s), (use - 1) & 1, kWaitLimitNs)) {
+        if (use > 0 && !sm100::mbar_wait_bounded(empty(s), (use - 1) & 1, a.wait_ns)) {
           set_error();
           ok = false;
           break;
@@ -292,7 +304,7 @@ __global__ void __launch_bounds__(Cfg<NST>::threads, 1) gemm_tc_kernel(const __g
       }
     }
     // ---- epilogue
-    if (ok && sm100::mbar_wait_bounded(acc_full, 0, kWaitLimitNs)) {
+    if (ok && sm100::mbar_wait_bounded(acc_full, 0, a.wait_ns)) {
       sm100::tc_fence_after_sync();
       const int quarter = warp & 3;  // TMEM lanes this warp may read
       const int64_t row = m0 + quarter * 32 + lane;
@@ -362,14 +374,15 @@ __global__ void __launch_bounds__(PCfg::threads, 1) gemm_tc_persistent_kernel(
   uint8_t *ring = base;
   uint2 *tbl0 = reinterpret_cast<uint2 *>(base + C::ring_bytes);
   uint64_t *bars = reinterpret_cast<uint64_t *>(base + C::ring_bytes + C::tables_bytes);
-  // bars: full_a[S], full_b[S], empty[S], acc_full[2], acc_empty[2], then the TMEM address holder
+  // bars: full_a[S], full_b[S], empty[S], acc_full[2], acc_empty[2], drain, then the TMEM address holder
   const uint32_t bar0 = smem_u32(bars);
   auto full_a = [&](int s) { return bar0 + 8u * s; };
   auto full_b = [&](int s) { return bar0 + 8u * (S + s); };
   auto empty = [&](int s) { return bar0 + 8u * (2 * S + s); };
   auto acc_full = [&](int b) { return bar0 + 8u * (3 * S + b); };
   auto acc_empty = [&](int b) { return bar0 + 8u * (3 * S + 2 + b); };
-  uint32_t *tmem_holder = reinterpret_cast<uint32_t *>(bars + 3 * S + 4);
+  const uint32_t drain = bar0 + 8u * (3 * S + 4);
+  uint32_t *tmem_holder = reinterpret_cast<uint32_t *>(bars + 3 * S + 5);
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
 
   for (int i = threadIdx.x; i < C::table_entries; i += blockDim.x)
@@ -384,6 +397,7 @@ __global__ void __launch_bounds__(PCfg::threads, 1) gemm_tc_persistent_kernel(
       sm100::mbar_init(acc_full(b), 1);
       sm100::mbar_init(acc_empty(b), 128);
     }
+    sm100::mbar_init(drain, 1);
     sm100::fence_barrier_init();
     sm100::prefetch_tmap(&tmap_x);
   }
@@ -411,7 +425,7 @@ __global__ void __launch_bounds__(PCfg::threads, 1) gemm_tc_persistent_kernel(
         for (int ks = 0; ks < K; ++ks, ++gs) {
           const int s = static_cast<int>(gs % S);
           const int64_t use = gs / S;
-          if (use > 0 && !sm100::mbar_wait_bounded(empty(s), static_cast<uint32_t>((use - 1) & 1), kWaitLimitNs)) {
+          if (use > 0 && !sm100::mbar_wait_bounded(empty(s), static_cast<uint32_t>((use - 1) & 1), a.wait_ns)) {
             set_error();
             ok = false;
             break;
@@ -422,7 +436,7 @@ __global__ void __launch_bounds__(PCfg::threads, 1) gemm_tc_persistent_kernel(
         }
       }
       for (int64_t g = issued > S ? issued - S : 0; g < issued; ++g)
-        if (!sm100::mbar_wait_bounded(full_b(static_cast<int>(g % S)), static_cast<uint32_t>((g / S) & 1), kWaitLimitNs))
+        if (!sm100::mbar_wait_bounded(full_b(static_cast<int>(g % S)), static_cast<uint32_t>((g / S) & 1), kDrainLimitNs))
           set_error();
     }
   } else if (warp == 1) {
@@ -433,7 +447,7 @@ __global__ void __launch_bounds__(PCfg::threads, 1) gemm_tc_persistent_kernel(
       bool ok = true;
       for (int i = 0; i < my_tiles && ok; ++i) {
         const int b = i & 1, u = i >> 1;
-        if (u > 0 && !sm100::mbar_wait_bounded(acc_empty(b), static_cast<uint32_t>((u - 1) & 1), kWaitLimitNs)) {
+        if (u > 0 && !sm100::mbar_wait_bounded(acc_empty(b), static_cast<uint32_t>((u - 1) & 1), a.wait_ns)) {
           set_error();
           break;
         }
@@ -441,8 +455,8 @@ __global__ void __launch_bounds__(PCfg::threads, 1) gemm_tc_persistent_kernel(
         for (int ks = 0; ks < K; ++ks, ++gs) {
           const int s = static_cast<int>(gs % S);
           const uint32_t par = static_cast<uint32_t>((gs / S) & 1);
-          ok = sm100::mbar_wait_bounded(full_a(s), par, kWaitLimitNs) &&
-               sm100::mbar_wait_bounded(full_b(s), par, kWaitLimitNs);
+          ok = sm100::mbar_wait_bounded(full_a(s), par, a.wait_ns) &&
+               sm100::mbar_wait_bounded(full_b(s), par, a.wait_ns);
           if (!ok) {
             set_error();
             break;
@@ -458,6 +472,9 @@ __global__ void __launch_bounds__(PCfg::threads, 1) gemm_tc_persistent_kernel(
         }
         sm100::umma_commit(acc_full(b));
       }
+      // wind down: every MMA issued must be complete before TMEM and the ring are freed
+      sm100::umma_commit(drain);
+      if (!sm100::mbar_wait_bounded(drain, 0, kDrainLimitNs)) set_error();
     }
   } else if (warp < PCfg::epi_warp0) {
     // ---- decode producers (group dg of 128 threads, thread r <-> tile row r)
@@ -482,7 +499,7 @@ __global__ void __launch_bounds__(PCfg::threads, 1) gemm_tc_persistent_kernel(
       const int64_t gs = static_cast<int64_t>(q) * 4 + dg;  // this group's K step of the chunk
       const int s = static_cast<int>(gs % S);
       const int64_t use = gs / S;
-      if (use > 0 && !sm100::mbar_wait_bounded(empty(s), static_cast<uint32_t>((use - 1) & 1), kWaitLimitNs)) {
+      if (use > 0 && !sm100::mbar_wait_bounded(empty(s), static_cast<uint32_t>((use - 1) & 1), a.wait_ns)) {
         set_error();
         ok = false;
         break;
@@ -499,7 +516,7 @@ __global__ void __launch_bounds__(PCfg::threads, 1) gemm_tc_persistent_kernel(
     const float ls = *a.layer_scale;
     for (int i = 0; i < my_tiles; ++i) {
       const int b = i & 1, u = i >> 1;
-      if (!sm100::mbar_wait_bounded(acc_full(b), static_cast<uint32_t>(u & 1), kWaitLimitNs)) {
+      if (!sm100::mbar_wait_bounded(acc_full(b), static_cast<uint32_t>(u & 1), a.wait_ns)) {
         set_error();
         break;
       }
@@ -609,6 +626,7 @@ int launch_matmul_tc(const void *x2ws, int64_t batch, int64_t n, int64_t m, cons
   a.RT = padded_m(m) / kRowsPerTile;
   a.batch = batch;
   a.ksteps = static_cast<int>(n_pad / kBK);
+  a.wait_ns = pipeline_wait_ns();
   const uint8_t *p = static_cast<const uint8_t *>(packed);
   for (int st = 0; st < stages; ++st) {
     a.stage[st] = p;
@@ -626,6 +644,13 @@ int launch_matmul_tc(const void *x2ws, int64_t batch, int64_t n, int64_t m, cons
   if (k0 == QS_CB_E8_1BIT && k1 == QS_CB_E8P) return run_gemm<QS_CB_E8_1BIT, QS_CB_E8P, 2>(map, a, s);
   return run_gemm<QS_CB_E8_1BIT, QS_CB_E8_1BIT, 2>(map, a, s);
 }
+
+// Limit of the kernels' pipeline waits, read by every launcher (process-wide).
+static std::atomic<uint64_t> g_wait_ns{kDefaultWaitNs};
+
+uint64_t pipeline_wait_ns() { return g_wait_ns.load(std::memory_order_relaxed); }
+
+void set_pipeline_wait_ns(uint64_t ns) { g_wait_ns.store(ns ? ns : kDefaultWaitNs, std::memory_order_relaxed); }
 
 int device_status(cudaStream_t s) {
   int flag = 0;

@@ -54,6 +54,12 @@ int launch_matmul_tc(const void *x2ws, int64_t batch, int64_t n, int64_t m, cons
                      const int *kinds, const float *stage_scales, const float *layer_scale, float *y1,
                      cudaStream_t s);
 int device_status(cudaStream_t s);
+// Limit (ns) of every bounded wait between the warps of a pipelined kernel
+// (mbarrier waits); a wait that runs out sets the device error flag.  Drains of
+// a CTA's own asynchronous copies and tensor-core work keep a fixed 4 s limit.
+constexpr uint64_t kDefaultWaitNs = 4000000000ull;
+uint64_t pipeline_wait_ns();
+void set_pipeline_wait_ns(uint64_t ns);
 // Batches of at least this many tokens use the tcgen05 GEMM.  Below it the
 // mma.sync kernel's passes of 16 tokens are faster: a 128 x 256 GEMM tile with
 // few tokens is decode-bound and leaves SMs without a row tile.

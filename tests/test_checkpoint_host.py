@@ -83,3 +83,56 @@ def test_codebook_for_rejects_bad_bits():
     with pytest.raises(ValueError):
         C.codebook_for("5bit")
     assert isinstance(C.codebook_for("2bit"), E8PCodebook)
+
+
+def test_split_layers_is_contiguous_and_proportional():
+    from quipsharp_b200.checkpoint import split_layers
+    where = split_layers([10] * 8, [100, 100])
+    assert where == [0, 0, 0, 0, 1, 1, 1, 1]
+    # budgets 3:1 -> three quarters of the bytes on the first device
+    where = split_layers([10] * 8, [300, 100])
+    assert where == [0] * 6 + [1] * 2
+    # contiguous, non-decreasing device order
+    where = split_layers([5, 30, 5, 5, 30, 5, 5, 30], [60, 60, 60])
+    assert where == sorted(where) and set(where) == {0, 1, 2}
+    with pytest.raises(ValueError):
+        split_layers([10] * 8, [30, 30])          # does not fit at all
+    with pytest.raises(ValueError):
+        split_layers([50, 50, 20], [60, 60])      # fits in total, not contiguously
+
+
+def test_place_decoder_layers_moves_inputs_between_devices():
+    """Placement over two (host) devices: every placed module receives its inputs on
+    its own device and the forward result is unchanged."""
+    import torch.nn as nn
+    from quipsharp_b200.checkpoint import place_decoder_layers
+
+    class Body(nn.Module):
+        def __init__(self):
+            super().__init__()
+            self.embed_tokens = nn.Embedding(10, 4)
+            self.layers = nn.ModuleList([nn.Linear(4, 4) for _ in range(4)])
+            self.norm = nn.LayerNorm(4)
+
+    class Model(nn.Module):
+        def __init__(self):
+            super().__init__()
+            self.model = Body()
+            self.lm_head = nn.Linear(4, 10)
+
+        def forward(self, ids):
+            h = self.model.embed_tokens(ids)
+            for layer in self.model.layers:
+                h = layer(h)
+            return self.lm_head(self.model.norm(h))
+
+    torch.manual_seed(0)
+    model = Model()
+    ids = torch.tensor([[1, 2, 3]])
+    ref = model(ids)
+    seen = []
+    for layer in model.model.layers:
+        layer.register_forward_pre_hook(lambda m, a: seen.append(a[0].device))
+    place_decoder_layers(model, model.state_dict(), ["cpu", "cpu"], [10**6, 10**6])
+    assert torch.allclose(model(ids), ref)
+    assert len(seen) == 4 and all(d.type == "cpu" for d in seen)

@@ -67,3 +67,29 @@ def test_prefill_and_decode_paths_agree():
     y_tc = mod(x)[:32].float()
     y_mma = mod(x[:32]).float()
     assert rel_l2(y_tc.cpu().numpy(), y_mma.cpu().numpy()) < 2e-3
+
+
+# Grids with more output tiles than SMs.  One-stage codebooks run the persistent
+# GEMM (one CTA per SM looping over tiles): several tiles per CTA exercise the
+# second TMEM accumulator, the accumulator-empty handshake and the ring phases
+# that carry over from tile to tile.  Two-stage RVQ runs one tile per CTA over
+# a grid far larger than the GPU.  The whole batch runs on the GPU; a seeded
+# subset of token rows is compared with the oracle (rows are independent).
+@pytest.mark.parametrize("m,n,kinds,B,dt,transform", [
+    (18944, 3584, (syn.E8P,), 2048, torch.bfloat16, "rfft"),    # config-4 gate: 1184 tiles, 8 per CTA
+    (4096, 256, (syn.E8P,), 2567, torch.float16, "rht"),        # 352 tiles (2-3 per CTA), ragged token tile
+    (8192, 8192, (syn.E8P, syn.E8_1BIT), 4096, torch.bfloat16, "rht"),  # config-5 q, RVQ-3bit: 1024 CTAs
+])
+def test_prefill_multi_tile_grid_vs_oracle(m, n, kinds, B, dt, transform):
+    lay = syn.make_layer(m, n, kinds, seed=m + n + B, transform_kind=transform, has_bias=True)
+    x = syn.make_activations(B, n, dtype=dt, seed=B + 11)
+    y = make_module(lay)(x.to(DEV))
+    torch.cuda.synchronize()
+    N.check(N.lib().qs_device_status(N.stream_of(y)))
+    assert y.shape == (B, m) and y.dtype == dt
+    g = torch.Generator().manual_seed(B)
+    rows = torch.randperm(B, generator=g)[:48].sort().values
+    rows = torch.cat([rows, torch.tensor([0, B - 1])])  # first and last (ragged) token tile too
+    got = y[rows.to(DEV)].float().cpu().numpy()
+    assert rel_l2(got, oracle_y(lay, x[rows])) < TOL[dt]
+    assert torch.isfinite(y).all()
