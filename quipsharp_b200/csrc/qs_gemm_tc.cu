@@ -75,7 +75,7 @@ struct TcArgs {
   const float *layer_scale;
   const float *rowscale;
   float *y1;
-  int64_t m, m_pad, RT, batch;
+  int64_t m, m_pad, Tq, batch;  // Tq: code groups of 8 per row (packed stream)
   int ksteps;
   uint64_t wait_ns;  // limit of every pipeline wait (pipeline_wait_ns())
 };
@@ -83,25 +83,38 @@ struct TcArgs {
 __device__ __forceinline__ void set_error() { atomicExch(&g_tc_error, 1); }
 
 // E8P: 8 codes of one row (a packed quad) -> 8 x 16-byte chunks of fp16
-// weights (shift included), written to the row's swizzled positions.
+// weights (shift included), written to the row's swizzled positions.  The
+// table holds each entry's fp16 high bytes in the sign bit-slice order of the
+// quad (coordinates 2, 0, 3, 1 and 6, 4, 7, 5, qs_pack.cu), so one AND-XOR applies
+// four flips; byte permutes then give the natural f16x2 pairs.
 __device__ __forceinline__ void decode_e8p_row(const uint4 &q, const uint2 *tbl, int reps, uint8_t *arow, int rsw) {
-  const uint32_t flo = q.z ^ (q.z << 8);
-  const uint32_t fhi = (q.w & 0x00FFFFFFu) ^ shf_l_wrap(q.z, q.w, 8);
+  const uint32_t fa = q.z ^ (q.z << 8);
+  const uint32_t fb = (q.w & 0x00FFFFFFu) ^ shf_l_wrap(q.z, q.w, 8);
 #pragma unroll
   for (int c = 0; c < 8; ++c) {
     const uint32_t src = c < 4 ? q.x : q.y;
     const uint32_t idx = (src >> (8 * (c & 3))) & 0xFFu;
     const uint2 T = tbl[idx * reps];
-    const uint32_t tl = T.x ^ ((flo << c) & 0x80808080u);
-    const uint32_t th = T.y ^ ((fhi << c) & 0x80808080u);
+    const uint32_t tl = T.x ^ ((fa << c) & 0x80808080u);
+    const uint32_t th = T.y ^ ((fb << c) & 0x80808080u);
     const uint32_t sw = 0x34003400u ^ (prmt(q.w << c, 0u, 0xB4B4u) & 0x80008000u);
     uint4 w;
-    w.x = hadd2_u32(prmt(tl, 0u, 0x1404u), sw);
-    w.y = hadd2_u32(prmt(tl, 0u, 0x3424u), sw);
-    w.z = hadd2_u32(prmt(th, 0u, 0x1404u), sw);
-    w.w = hadd2_u32(prmt(th, 0u, 0x3424u), sw);
+    w.x = hadd2_u32(prmt(tl, 0u, 0x3414u), sw);  // (0, 1)
+    w.y = hadd2_u32(prmt(tl, 0u, 0x2404u), sw);  // (2, 3)
+    w.z = hadd2_u32(prmt(th, 0u, 0x3414u), sw);  // (4, 5)
+    w.w = hadd2_u32(prmt(th, 0u, 0x2404u), sw);  // (6, 7)
     *reinterpret_cast<uint4 *>(arow + ((c ^ rsw) << 4)) = w;
   }
+}
+
+// Table row of the prefill decode: E8P high bytes reordered to the quad's
+// sign bit-slice order; 1-bit high bytes in natural order.
+__device__ __forceinline__ uint2 gemm_table_entry(int kind, int row) {
+  if (kind == QS_CB_E8P) {
+    const uint2 h = kE8pHiBytes[row];
+    return make_uint2(prmt(h.x, 0u, 0x1302u), prmt(h.y, 0u, 0x1302u));
+  }
+  return kE81BitHiBytes[row];
 }
 
 // 1-bit: 8 index bytes of one row -> 8 chunks.
@@ -134,18 +147,19 @@ struct RowChunk<QS_CB_E8_1BIT, SPG> {
 };
 
 template <int K, int G>
-__device__ __forceinline__ void load_row_chunk(const uint8_t *stage, int64_t RT, int64_t kc, int64_t R, int dg,
+__device__ __forceinline__ void load_row_chunk(const uint8_t *stage, int64_t Tq, int64_t kc, int64_t R, int dg,
                                                bool valid, RowChunk<K, 4 / G> &rc) {
-  const int64_t rtg = R >> 4, rr = R & 15, half = rr >> 3, g = rr & 7;
+  // block (row tile, code group q) of the packed stream; this row's entry in it
+  const int64_t rt = R / kRowTile, rr = R % kRowTile;
   if constexpr (K == QS_CB_E8P) {
-    const uint8_t *p = stage + (kc * RT + rtg) * 1024 + half * 512 + g * 64;
+    const uint8_t *p = stage + (rt * Tq + kc * 4) * 2048 + rr * 16;
 #pragma unroll
-    for (int u = 0; u < 4 / G; ++u) rc.q[u] = valid ? ldg_nc_v4(p + 16 * (dg + G * u)) : make_uint4(0u, 0u, 0u, 0u);
+    for (int u = 0; u < 4 / G; ++u) rc.q[u] = valid ? ldg_nc_v4(p + 2048 * (dg + G * u)) : make_uint4(0u, 0u, 0u, 0u);
   } else {
-    const uint8_t *p = stage + (kc * RT + rtg) * 512 + g * 64 + half * 8;
+    const uint8_t *p = stage + (rt * Tq + kc * 4) * 1024 + rr * 8;
 #pragma unroll
     for (int u = 0; u < 4 / G; ++u)
-      rc.q[u] = valid ? __ldg(reinterpret_cast<const uint2 *>(p + 16 * (dg + G * u))) : make_uint2(0u, 0u);
+      rc.q[u] = valid ? __ldg(reinterpret_cast<const uint2 *>(p + 1024 * (dg + G * u))) : make_uint2(0u, 0u);
   }
 }
 
@@ -186,8 +200,8 @@ __global__ void __launch_bounds__(Cfg<NST>::threads, 1) gemm_tc_kernel(const __g
   // ---- setup (independent of the previous kernel)
   for (int i = threadIdx.x; i < C::table_entries; i += blockDim.x) {
     const int row = i / C::reps;
-    tbl0[i] = K0 == QS_CB_E8P ? kE8pHiBytes[row] : kE81BitHiBytes[row];
-    if constexpr (NST == 2) tbl1[i] = K1 == QS_CB_E8P ? kE8pHiBytes[row] : kE81BitHiBytes[row];
+    tbl0[i] = gemm_table_entry(K0, row);
+    if constexpr (NST == 2) tbl1[i] = gemm_table_entry(K1, row);
   }
   if (threadIdx.x == 0) {
     for (int s = 0; s < S; ++s) {
@@ -268,19 +282,19 @@ __global__ void __launch_bounds__(Cfg<NST>::threads, 1) gemm_tc_kernel(const __g
     // codes two chunks ahead of the decode (a chunk is ~1 us of MMA work)
     RowChunk<K0, SPG> c0, n0c, nn0c;
     RowChunk<K1, SPG> c1, n1c, nn1c;
-    load_row_chunk<K0, G>(a.stage[0], a.RT, 0, R, dg, valid, c0);
-    if constexpr (NST == 2) load_row_chunk<K1, G>(a.stage[1], a.RT, 0, R, dg, valid, c1);
+    load_row_chunk<K0, G>(a.stage[0], a.Tq, 0, R, dg, valid, c0);
+    if constexpr (NST == 2) load_row_chunk<K1, G>(a.stage[1], a.Tq, 0, R, dg, valid, c1);
     if (K / 4 > 1) {
-      load_row_chunk<K0, G>(a.stage[0], a.RT, 1, R, dg, valid, n0c);
-      if constexpr (NST == 2) load_row_chunk<K1, G>(a.stage[1], a.RT, 1, R, dg, valid, n1c);
+      load_row_chunk<K0, G>(a.stage[0], a.Tq, 1, R, dg, valid, n0c);
+      if constexpr (NST == 2) load_row_chunk<K1, G>(a.stage[1], a.Tq, 1, R, dg, valid, n1c);
     }
     const int rowoff = (r >> 3) * 1024 + (r & 7) * 128;
     const int rep = lane % C::reps;  // this thread's table replica
     bool ok = true;
     for (int kc = 0; kc < K / 4 && ok; ++kc) {  // one 32-code chunk = 4 K steps
       if (kc + 2 < K / 4) {
-        load_row_chunk<K0, G>(a.stage[0], a.RT, kc + 2, R, dg, valid, nn0c);
-        if constexpr (NST == 2) load_row_chunk<K1, G>(a.stage[1], a.RT, kc + 2, R, dg, valid, nn1c);
+        load_row_chunk<K0, G>(a.stage[0], a.Tq, kc + 2, R, dg, valid, nn0c);
+        if constexpr (NST == 2) load_row_chunk<K1, G>(a.stage[1], a.Tq, kc + 2, R, dg, valid, nn1c);
       }
 #pragma unroll
       for (int t = 0; t < SPG; ++t) {
@@ -304,7 +318,9 @@ __global__ void __launch_bounds__(Cfg<NST>::threads, 1) gemm_tc_kernel(const __g
       }
     }
     // ---- epilogue
-    if (ok && sm100::mbar_wait_bounded(acc_full, 0, a.wait_ns)) {
+    // one outcome per warp: the TMEM loads below are warp-collective
+    const bool ok_warp = __all_sync(0xffffffffu, ok);
+    if (ok_warp && sm100::mbar_wait_warp(acc_full, 0, a.wait_ns)) {
       sm100::tc_fence_after_sync();
       const int quarter = warp & 3;  // TMEM lanes this warp may read
       const int64_t row = m0 + quarter * 32 + lane;
@@ -326,7 +342,7 @@ __global__ void __launch_bounds__(Cfg<NST>::threads, 1) gemm_tc_kernel(const __g
           }
         }
       }
-    } else if (ok) {
+    } else if (ok_warp) {
       set_error();
     }
   }
@@ -385,8 +401,7 @@ __global__ void __launch_bounds__(PCfg::threads, 1) gemm_tc_persistent_kernel(
   uint32_t *tmem_holder = reinterpret_cast<uint32_t *>(bars + 3 * S + 5);
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
 
-  for (int i = threadIdx.x; i < C::table_entries; i += blockDim.x)
-    tbl0[i] = K0 == QS_CB_E8P ? kE8pHiBytes[i / C::reps] : kE81BitHiBytes[i / C::reps];
+  for (int i = threadIdx.x; i < C::table_entries; i += blockDim.x) tbl0[i] = gemm_table_entry(K0, i / C::reps);
   if (threadIdx.x == 0) {
     for (int s = 0; s < S; ++s) {
       sm100::mbar_init(full_a(s), 128);
@@ -488,7 +503,7 @@ __global__ void __launch_bounds__(PCfg::threads, 1) gemm_tc_persistent_kernel(
     auto chunk_load = [&](int q, RowChunk<K0, 1> &rc) {
       const int mt = tile_of(q / KC) % tiles_m;
       const int64_t R = static_cast<int64_t>(mt) * kBM + r;
-      load_row_chunk<K0, G>(a.stage[0], a.RT, q % KC, R, dg, R < a.m_pad, rc);
+      load_row_chunk<K0, G>(a.stage[0], a.Tq, q % KC, R, dg, R < a.m_pad, rc);
     };
     RowChunk<K0, 1> c0, n0c, nn0c;
     if (nchunks > 0) chunk_load(0, c0);
@@ -516,7 +531,7 @@ __global__ void __launch_bounds__(PCfg::threads, 1) gemm_tc_persistent_kernel(
     const float ls = *a.layer_scale;
     for (int i = 0; i < my_tiles; ++i) {
       const int b = i & 1, u = i >> 1;
-      if (!sm100::mbar_wait_bounded(acc_full(b), static_cast<uint32_t>(u & 1), a.wait_ns)) {
+      if (!sm100::mbar_wait_warp(acc_full(b), static_cast<uint32_t>(u & 1), a.wait_ns)) {
         set_error();
         break;
       }
@@ -550,12 +565,15 @@ __global__ void __launch_bounds__(PCfg::threads, 1) gemm_tc_persistent_kernel(
   }
 }
 
-// ---- tensor map for the fp16 activation tiles ----------------------------
+}  // namespace
+
+// ---- tensor maps over the fp16 activation rows (x2h: rows x n_pad) ----------
 using EncodeTiledFn = CUresult (*)(CUtensorMap *, CUtensorMapDataType, cuuint32_t, void *, const cuuint64_t *,
                                    const cuuint64_t *, const cuuint32_t *, const cuuint32_t *, CUtensorMapInterleave,
                                    CUtensorMapSwizzle, CUtensorMapL2promotion, CUtensorMapFloatOOBfill);
 
-int encode_x_map(CUtensorMap *map, const void *x2h, int64_t n_pad, int64_t batch) {
+int encode_fp16_rows_map(CUtensorMap *map, const void *x2h, int64_t n_pad, int64_t rows, int box_x, int box_y,
+                         bool swizzle128) {
   static EncodeTiledFn fn = nullptr;
   static std::mutex mu;
   {
@@ -568,16 +586,19 @@ int encode_x_map(CUtensorMap *map, const void *x2h, int64_t n_pad, int64_t batch
       fn = reinterpret_cast<EncodeTiledFn>(p);
     }
   }
-  const cuuint64_t dims[2] = {static_cast<cuuint64_t>(n_pad), static_cast<cuuint64_t>(batch)};
+  const cuuint64_t dims[2] = {static_cast<cuuint64_t>(n_pad), static_cast<cuuint64_t>(rows)};
   const cuuint64_t strides[1] = {static_cast<cuuint64_t>(n_pad * 2)};
-  const cuuint32_t box[2] = {kBK, kBN};
+  const cuuint32_t box[2] = {static_cast<cuuint32_t>(box_x), static_cast<cuuint32_t>(box_y)};
   const cuuint32_t estr[2] = {1, 1};
   CUresult r = fn(map, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2, const_cast<void *>(x2h), dims, strides, box, estr,
-                  CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
-                  CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+                  CU_TENSOR_MAP_INTERLEAVE_NONE,
+                  swizzle128 ? CU_TENSOR_MAP_SWIZZLE_128B : CU_TENSOR_MAP_SWIZZLE_NONE,
+                  CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
   if (r != CUDA_SUCCESS) return fail(QS_ERR_CUDA, "cuTensorMapEncodeTiled failed (%d)", static_cast<int>(r));
   return QS_OK;
 }
+
+namespace {
 
 static int tc_num_sms() {
   static int cached[64] = {0};
@@ -623,7 +644,7 @@ int launch_matmul_tc(const void *x2ws, int64_t batch, int64_t n, int64_t m, cons
   a.y1 = y1;
   a.m = m;
   a.m_pad = padded_m(m);
-  a.RT = padded_m(m) / kRowsPerTile;
+  a.Tq = padded_T(n) / 8;
   a.batch = batch;
   a.ksteps = static_cast<int>(n_pad / kBK);
   a.wait_ns = pipeline_wait_ns();
@@ -634,7 +655,7 @@ int launch_matmul_tc(const void *x2ws, int64_t batch, int64_t n, int64_t m, cons
     p += round_up(stage_bytes(kinds[st], m, n), 256);
   }
   CUtensorMap map;
-  int st = encode_x_map(&map, x2ws, n_pad, batch);
+  int st = encode_fp16_rows_map(&map, x2ws, n_pad, batch, kBK, kBN, true);
   if (st) return st;
   const int k0 = kinds[0], k1 = stages == 2 ? kinds[1] : 0;
   if (stages == 1)
@@ -653,15 +674,19 @@ uint64_t pipeline_wait_ns() { return g_wait_ns.load(std::memory_order_relaxed); 
 void set_pipeline_wait_ns(uint64_t ns) { g_wait_ns.store(ns ? ns : kDefaultWaitNs, std::memory_order_relaxed); }
 
 int device_status(cudaStream_t s) {
-  int flag = 0;
+  int flag = 0, gemv_flag = 0;
   static const int zero = 0;
   QS_CUDA_TRY(cudaMemcpyFromSymbolAsync(&flag, g_tc_error, sizeof(int), 0, cudaMemcpyDeviceToHost, s));
   QS_CUDA_TRY(cudaStreamSynchronize(s));
   if (flag) {
     QS_CUDA_TRY(cudaMemcpyToSymbolAsync(g_tc_error, &zero, sizeof(int), 0, cudaMemcpyHostToDevice, s));
     QS_CUDA_TRY(cudaStreamSynchronize(s));
-    return fail(QS_ERR_TIMEOUT, "a pipeline wait in the prefill matmul timed out; its results are invalid");
   }
+  int st = take_gemv_error(s, &gemv_flag);
+  if (st) return st;
+  if (flag || gemv_flag)
+    return fail(QS_ERR_TIMEOUT, "a pipeline wait in the %s matmul timed out; its results are invalid",
+                flag ? "prefill" : "decode");
   return QS_OK;
 }
 

@@ -5,6 +5,8 @@
 #include <cuda_runtime.h>
 #include <stdint.h>
 
+struct CUtensorMap_st;  // CUtensorMap (cuda.h)
+
 namespace qs {
 
 // qs_decode.cu
@@ -44,7 +46,9 @@ int launch_two_pass_output(float *y1, int64_t batch, int64_t m, const float2 *ph
 int launch_pack(const int16_t *codes, int stages, const int *kinds, int64_t m, int64_t n,
                 void *packed, cudaStream_t s);
 
-// qs_gemv.cu
+// qs_gemv_tc.cu: fused decode + matmul; batches below kTcMinBatch run the
+// decode-regime kernel of this file, larger ones launch_matmul_tc
+int take_gemv_error(cudaStream_t s, int *flag);
 int launch_matmul(const void *x2ws, int64_t batch, int64_t n, int64_t m, const void *packed,
                   int stages, const int *kinds, const float *stage_scales,
                   const float *layer_scale, float *y1, cudaStream_t s);
@@ -54,15 +58,19 @@ int launch_matmul_tc(const void *x2ws, int64_t batch, int64_t n, int64_t m, cons
                      const int *kinds, const float *stage_scales, const float *layer_scale, float *y1,
                      cudaStream_t s);
 int device_status(cudaStream_t s);
+// 2-D tensor map over fp16 rows (rows x n_pad, row stride n_pad elements) with
+// a box of box_x elements x box_y rows; 128-byte swizzle or none.
+int encode_fp16_rows_map(::CUtensorMap_st *map, const void *x2h, int64_t n_pad, int64_t rows, int box_x, int box_y,
+                         bool swizzle128);
 // Limit (ns) of every bounded wait between the warps of a pipelined kernel
 // (mbarrier waits); a wait that runs out sets the device error flag.  Drains of
 // a CTA's own asynchronous copies and tensor-core work keep a fixed 4 s limit.
 constexpr uint64_t kDefaultWaitNs = 4000000000ull;
 uint64_t pipeline_wait_ns();
 void set_pipeline_wait_ns(uint64_t ns);
-// Batches of at least this many tokens use the tcgen05 GEMM.  Below it the
-// mma.sync kernel's passes of 16 tokens are faster: a 128 x 256 GEMM tile with
-// few tokens is decode-bound and leaves SMs without a row tile.
+// Batches of at least this many tokens use the tcgen05 GEMM (128 x 256 tiles,
+// decoded weights in shared memory); smaller ones the decode-regime kernel
+// (decoded weights in TMEM, 16 or 32 token columns, one pass over the weights).
 constexpr int64_t kTcMinBatch = 33;
 
 }  // namespace qs

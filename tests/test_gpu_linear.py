@@ -97,6 +97,11 @@ def test_forward_config_shapes_vs_reference(golden_configs, cfg):
     (11008, 1024, (syn.E8P,), 1, torch.float32),                  # output 5504 = 43 x 128: warp-per-column pass A
     (4096, 11008, (syn.E8P, syn.E8_1BIT), 4, torch.float16),      # input 5504: warp-per-column pass A + L1 scale
     (3584, 18944, (syn.E8P,), 2, torch.bfloat16),                 # input 9472 = 37 x 256
+    (640, 2048, (syn.E8P,), 17, torch.float16),                   # 32 token columns, one stage
+    (300, 768, (syn.E8_1BIT, syn.E8_1BIT), 24, torch.bfloat16),   # ragged rows, 1-bit stages, 32 columns
+    (8192, 8192, (syn.E8P, syn.E8_1BIT), 1, torch.bfloat16),      # Llama-3-70B q: chunk ranges cross row tiles
+    (1024, 8192, (syn.E8P, syn.E8_1BIT), 2, torch.bfloat16),      # Llama-3-70B k: few chunks per CTA
+    (128, 256, (syn.E8P,), 1, torch.float32),                     # fewer chunks than SMs
 ])
 def test_forward_shapes_vs_oracle(m, n, kinds, B, dt):
     lay = syn.make_layer(m, n, kinds, seed=m + n + B, has_bias=True)
