@@ -161,22 +161,19 @@ constexpr int kPrimeTableLen = 3 + 5 + 7 + 11 + 13 + 17 + 19 + 23 + 29 + 31 + 37
 #include "qs_tables_gen.inc"
 
 // ---- packed weight-stream geometry ----------------------------------------
-// Rows are grouped in tiles of 128 (the M of the tcgen05 matmuls; padded rows
-// hold code 0 and are never stored back).  For each row tile and each group q
-// of 8 consecutive codes (64 input features) a stage stores one block: the
-// 128 rows' 8 codes, row r at offset r * (block / 128) -- a 16-byte quad for
-// E8P (2 KB blocks), 8 index bytes for 1-bit (1 KB blocks).  Blocks are
-// ordered row-tile-major: block (rt, q) at (rt * Tq + q) * block bytes, so one
-// row tile's K range is one contiguous byte range.  The input features are
-// padded to a multiple of 256 (32 codes) with code 0 (padded features meet
-// zero activations).
-constexpr int kRowTile = 128;
-constexpr int kCodesPad = 32;
-__host__ __device__ inline int64_t padded_m(int64_t m) { return round_up(m, kRowTile); }
-__host__ __device__ inline int64_t padded_T(int64_t n) { return round_up(n / 8, kCodesPad); }
-__host__ __device__ inline int64_t group_bytes(int kind) { return kind == QS_CB_E8P ? 2048 : 1024; }
+// Item = 16 weight rows x 32 codes (256 input features).  E8P items are 1024 B,
+// 1-bit items 512 B.  Items are stored code-chunk-major: item = kc * RT + rt
+// (RT = padded rows / 16), so a warp walking consecutive items streams one
+// contiguous byte range.  Rows are padded to 16 and the input features to 256
+// with code 0 (padded rows are never stored back; padded features meet zero
+// activations).
+constexpr int kRowsPerTile = 16;
+constexpr int kCodesPerChunk = 32;
+__host__ __device__ inline int64_t padded_m(int64_t m) { return round_up(m, kRowsPerTile); }
+__host__ __device__ inline int64_t padded_T(int64_t n) { return round_up(n / 8, kCodesPerChunk); }
+__host__ __device__ inline int64_t item_bytes(int kind) { return kind == QS_CB_E8P ? 1024 : 512; }
 __host__ __device__ inline int64_t stage_bytes(int kind, int64_t m, int64_t n) {
-  return (padded_m(m) / kRowTile) * (padded_T(n) / 8) * group_bytes(kind);
+  return (padded_m(m) / kRowsPerTile) * (padded_T(n) / kCodesPerChunk) * item_bytes(kind);
 }
 
 }  // namespace qs

@@ -75,7 +75,7 @@ struct TcArgs {
   const float *layer_scale;
   const float *rowscale;
   float *y1;
-  int64_t m, m_pad, Tq, batch;  // Tq: code groups of 8 per row (packed stream)
+  int64_t m, m_pad, RT, batch;  // RT: 16-row tiles of the packed stream
   int ksteps;
   uint64_t wait_ns;  // limit of every pipeline wait (pipeline_wait_ns())
 };
@@ -147,19 +147,19 @@ struct RowChunk<QS_CB_E8_1BIT, SPG> {
 };
 
 template <int K, int G>
-__device__ __forceinline__ void load_row_chunk(const uint8_t *stage, int64_t Tq, int64_t kc, int64_t R, int dg,
+__device__ __forceinline__ void load_row_chunk(const uint8_t *stage, int64_t RT, int64_t kc, int64_t R, int dg,
                                                bool valid, RowChunk<K, 4 / G> &rc) {
-  // block (row tile, code group q) of the packed stream; this row's entry in it
-  const int64_t rt = R / kRowTile, rr = R % kRowTile;
+  // item (kc, R / 16) of the packed stream; this row's quads in it (qs_pack.cu)
+  const int64_t rtg = R >> 4, rr = R & 15, half = rr >> 3, g = rr & 7;
   if constexpr (K == QS_CB_E8P) {
-    const uint8_t *p = stage + (rt * Tq + kc * 4) * 2048 + rr * 16;
+    const uint8_t *p = stage + (kc * RT + rtg) * 1024 + half * 512 + g * 64;
 #pragma unroll
-    for (int u = 0; u < 4 / G; ++u) rc.q[u] = valid ? ldg_nc_v4(p + 2048 * (dg + G * u)) : make_uint4(0u, 0u, 0u, 0u);
+    for (int u = 0; u < 4 / G; ++u) rc.q[u] = valid ? ldg_nc_v4(p + 16 * (dg + G * u)) : make_uint4(0u, 0u, 0u, 0u);
   } else {
-    const uint8_t *p = stage + (rt * Tq + kc * 4) * 1024 + rr * 8;
+    const uint8_t *p = stage + (kc * RT + rtg) * 512 + g * 64 + half * 8;
 #pragma unroll
     for (int u = 0; u < 4 / G; ++u)
-      rc.q[u] = valid ? __ldg(reinterpret_cast<const uint2 *>(p + 1024 * (dg + G * u))) : make_uint2(0u, 0u);
+      rc.q[u] = valid ? __ldg(reinterpret_cast<const uint2 *>(p + 16 * (dg + G * u))) : make_uint2(0u, 0u);
   }
 }
 
@@ -282,19 +282,19 @@ __global__ void __launch_bounds__(Cfg<NST>::threads, 1) gemm_tc_kernel(const __g
     // codes two chunks ahead of the decode (a chunk is ~1 us of MMA work)
     RowChunk<K0, SPG> c0, n0c, nn0c;
     RowChunk<K1, SPG> c1, n1c, nn1c;
-    load_row_chunk<K0, G>(a.stage[0], a.Tq, 0, R, dg, valid, c0);
-    if constexpr (NST == 2) load_row_chunk<K1, G>(a.stage[1], a.Tq, 0, R, dg, valid, c1);
+    load_row_chunk<K0, G>(a.stage[0], a.RT, 0, R, dg, valid, c0);
+    if constexpr (NST == 2) load_row_chunk<K1, G>(a.stage[1], a.RT, 0, R, dg, valid, c1);
     if (K / 4 > 1) {
-      load_row_chunk<K0, G>(a.stage[0], a.Tq, 1, R, dg, valid, n0c);
-      if constexpr (NST == 2) load_row_chunk<K1, G>(a.stage[1], a.Tq, 1, R, dg, valid, n1c);
+      load_row_chunk<K0, G>(a.stage[0], a.RT, 1, R, dg, valid, n0c);
+      if constexpr (NST == 2) load_row_chunk<K1, G>(a.stage[1], a.RT, 1, R, dg, valid, n1c);
     }
     const int rowoff = (r >> 3) * 1024 + (r & 7) * 128;
     const int rep = lane % C::reps;  // this thread's table replica
     bool ok = true;
     for (int kc = 0; kc < K / 4 && ok; ++kc) {  // one 32-code chunk = 4 K steps
       if (kc + 2 < K / 4) {
-        load_row_chunk<K0, G>(a.stage[0], a.Tq, kc + 2, R, dg, valid, nn0c);
-        if constexpr (NST == 2) load_row_chunk<K1, G>(a.stage[1], a.Tq, kc + 2, R, dg, valid, nn1c);
+        load_row_chunk<K0, G>(a.stage[0], a.RT, kc + 2, R, dg, valid, nn0c);
+        if constexpr (NST == 2) load_row_chunk<K1, G>(a.stage[1], a.RT, kc + 2, R, dg, valid, nn1c);
       }
 #pragma unroll
       for (int t = 0; t < SPG; ++t) {
@@ -503,7 +503,7 @@ __global__ void __launch_bounds__(PCfg::threads, 1) gemm_tc_persistent_kernel(
     auto chunk_load = [&](int q, RowChunk<K0, 1> &rc) {
       const int mt = tile_of(q / KC) % tiles_m;
       const int64_t R = static_cast<int64_t>(mt) * kBM + r;
-      load_row_chunk<K0, G>(a.stage[0], a.Tq, q % KC, R, dg, R < a.m_pad, rc);
+      load_row_chunk<K0, G>(a.stage[0], a.RT, q % KC, R, dg, R < a.m_pad, rc);
     };
     RowChunk<K0, 1> c0, n0c, nn0c;
     if (nchunks > 0) chunk_load(0, c0);
@@ -644,7 +644,7 @@ int launch_matmul_tc(const void *x2ws, int64_t batch, int64_t n, int64_t m, cons
   a.y1 = y1;
   a.m = m;
   a.m_pad = padded_m(m);
-  a.Tq = padded_T(n) / 8;
+  a.RT = padded_m(m) / kRowsPerTile;
   a.batch = batch;
   a.ksteps = static_cast<int>(n_pad / kBK);
   a.wait_ns = pipeline_wait_ns();
@@ -674,19 +674,15 @@ uint64_t pipeline_wait_ns() { return g_wait_ns.load(std::memory_order_relaxed); 
 void set_pipeline_wait_ns(uint64_t ns) { g_wait_ns.store(ns ? ns : kDefaultWaitNs, std::memory_order_relaxed); }
 
 int device_status(cudaStream_t s) {
-  int flag = 0, gemv_flag = 0;
+  int flag = 0;
   static const int zero = 0;
   QS_CUDA_TRY(cudaMemcpyFromSymbolAsync(&flag, g_tc_error, sizeof(int), 0, cudaMemcpyDeviceToHost, s));
   QS_CUDA_TRY(cudaStreamSynchronize(s));
   if (flag) {
     QS_CUDA_TRY(cudaMemcpyToSymbolAsync(g_tc_error, &zero, sizeof(int), 0, cudaMemcpyHostToDevice, s));
     QS_CUDA_TRY(cudaStreamSynchronize(s));
+    return fail(QS_ERR_TIMEOUT, "a pipeline wait in the prefill matmul timed out; its results are invalid");
   }
-  int st = take_gemv_error(s, &gemv_flag);
-  if (st) return st;
-  if (flag || gemv_flag)
-    return fail(QS_ERR_TIMEOUT, "a pipeline wait in the %s matmul timed out; its results are invalid",
-                flag ? "prefill" : "decode");
   return QS_OK;
 }
 

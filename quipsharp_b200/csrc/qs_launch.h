@@ -46,9 +46,8 @@ int launch_two_pass_output(float *y1, int64_t batch, int64_t m, const float2 *ph
 int launch_pack(const int16_t *codes, int stages, const int *kinds, int64_t m, int64_t n,
                 void *packed, cudaStream_t s);
 
-// qs_gemv_tc.cu: fused decode + matmul; batches below kTcMinBatch run the
+// qs_gemv.cu: fused decode + matmul; batches below kTcMinBatch run the
 // decode-regime kernel of this file, larger ones launch_matmul_tc
-int take_gemv_error(cudaStream_t s, int *flag);
 int launch_matmul(const void *x2ws, int64_t batch, int64_t n, int64_t m, const void *packed,
                   int stages, const int *kinds, const float *stage_scales,
                   const float *layer_scale, float *y1, cudaStream_t s);
@@ -69,8 +68,8 @@ constexpr uint64_t kDefaultWaitNs = 4000000000ull;
 uint64_t pipeline_wait_ns();
 void set_pipeline_wait_ns(uint64_t ns);
 // Batches of at least this many tokens use the tcgen05 GEMM (128 x 256 tiles,
-// decoded weights in shared memory); smaller ones the decode-regime kernel
-// (decoded weights in TMEM, 16 or 32 token columns, one pass over the weights).
+// decoded weights in shared memory); smaller ones the mma.sync decode-regime
+// kernel (weights decoded in registers, passes of 8 or 16 tokens).
 constexpr int64_t kTcMinBatch = 33;
 
 }  // namespace qs

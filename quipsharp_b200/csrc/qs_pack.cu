@@ -1,7 +1,12 @@
 // Re-lays QuantizedLinear codes (int16, (stages, m, n/8), quipsharp/checkpoint.py:99-103)
-// into the weight stream the fused matmuls read (geometry in qs_common.cuh: per
-// 128-row tile and group of 8 codes, one block holding row r's 8 codes at r * 16
-// (E8P) or r * 8 (1-bit) bytes).
+// into the weight stream the fused matmuls read.
+//
+// Geometry (qs_common.cuh): an "item" is 16 weight rows x 32 codes; items are
+// stored code-chunk-major.  Inside an item, lane l = 4*g + t of the consuming
+// warp owns rows g and g+8 and codes [8t, 8t+8) of each; its bytes are
+// contiguous:
+//   E8P item (1024 B): [half h (row g+8h)][lane l] -> 16 B quad of 8 codes;
+//   1-bit item (512 B): [lane l] -> 8 index bytes of row g, then 8 of row g+8.
 //
 //   E8P quad (16 B) of 8 codes of one row:
 //     w0 = abs index bytes of codes 0..3, w1 = abs index bytes of codes 4..7,
@@ -32,13 +37,12 @@ __device__ __forceinline__ int sign_slice_coord(int j) {
   return (order >> (4 * j)) & 7;
 }
 
-__global__ void pack_e8p_kernel(const int16_t *codes, int64_t m, int64_t T, int64_t Tq, int64_t rows,
+__global__ void pack_e8p_kernel(const int16_t *codes, int64_t m, int64_t T, int64_t RT, int64_t Tq,
                                 uint8_t *out) {
   const int64_t tid = blockIdx.x * static_cast<int64_t>(blockDim.x) + threadIdx.x;
-  if (tid >= rows * Tq) return;
-  // consecutive threads take consecutive rows of one code group: coalesced stores
-  const int64_t rt = tid / (kRowTile * Tq), rem = tid % (kRowTile * Tq);
-  const int64_t q = rem / kRowTile, rr = rem % kRowTile, r = rt * kRowTile + rr;
+  const int64_t mp = RT * kRowsPerTile;
+  if (tid >= mp * Tq) return;
+  const int64_t r = tid / Tq, q = tid % Tq;  // row, quad of 8 codes
   uint32_t w0 = 0, w1 = 0, w2 = 0, w3 = 0;
 #pragma unroll
   for (int c = 0; c < 8; ++c) {
@@ -63,16 +67,19 @@ __global__ void pack_e8p_kernel(const int16_t *codes, int64_t m, int64_t T, int6
     }
     w3 |= ((code & 1u) ^ 1u) << (31 - c);
   }
-  uint4 *dst = reinterpret_cast<uint4 *>(out + (rt * Tq + q) * 2048 + rr * 16);
+  const int64_t rt = r / kRowsPerTile, rr = r % kRowsPerTile;
+  const int64_t kc = q / 4, t = q % 4;
+  const int64_t h = rr / 8, lane = (rr % 8) * 4 + t;
+  uint4 *dst = reinterpret_cast<uint4 *>(out + (kc * RT + rt) * 1024 + h * 512 + lane * 16);
   *dst = make_uint4(w0, w1, w2, w3);
 }
 
-__global__ void pack_1bit_kernel(const int16_t *codes, int64_t m, int64_t T, int64_t Tq, int64_t rows,
+__global__ void pack_1bit_kernel(const int16_t *codes, int64_t m, int64_t T, int64_t RT, int64_t Tq,
                                  uint8_t *out) {
   const int64_t tid = blockIdx.x * static_cast<int64_t>(blockDim.x) + threadIdx.x;
-  if (tid >= rows * Tq) return;
-  const int64_t rt = tid / (kRowTile * Tq), rem = tid % (kRowTile * Tq);
-  const int64_t q = rem / kRowTile, rr = rem % kRowTile, r = rt * kRowTile + rr;
+  const int64_t mp = RT * kRowsPerTile;
+  if (tid >= mp * Tq) return;
+  const int64_t r = tid / Tq, q = tid % Tq;
   uint32_t lo = 0, hi = 0;
   bool bad = false;
 #pragma unroll
@@ -84,14 +91,17 @@ __global__ void pack_1bit_kernel(const int16_t *codes, int64_t m, int64_t T, int
     else hi |= (code & 0xFFu) << (8 * (c - 4));
   }
   if (bad) atomicExch(&g_pack_error, 1);
-  uint2 *dst = reinterpret_cast<uint2 *>(out + (rt * Tq + q) * 1024 + rr * 8);
+  const int64_t rt = r / kRowsPerTile, rr = r % kRowsPerTile;
+  const int64_t kc = q / 4, t = q % 4;
+  const int64_t h = rr / 8, lane = (rr % 8) * 4 + t;
+  uint2 *dst = reinterpret_cast<uint2 *>(out + (kc * RT + rt) * 512 + lane * 16 + h * 8);
   *dst = make_uint2(lo, hi);
 }
 
 int launch_pack(const int16_t *codes, int stages, const int *kinds, int64_t m, int64_t n,
                 void *packed, cudaStream_t s) {
-  const int64_t T = n / 8, Tq = padded_T(n) / 8, rows = padded_m(m);
-  const int64_t threads = rows * Tq;
+  const int64_t T = n / 8, RT = padded_m(m) / kRowsPerTile, Tq = padded_T(n) / 8;
+  const int64_t threads = padded_m(m) * Tq;
   static const int zero = 0;
   QS_CUDA_TRY(cudaMemcpyToSymbolAsync(g_pack_error, &zero, sizeof(int), 0, cudaMemcpyHostToDevice, s));
   uint8_t *dst = static_cast<uint8_t *>(packed);
@@ -99,9 +109,9 @@ int launch_pack(const int16_t *codes, int stages, const int *kinds, int64_t m, i
   for (int st = 0; st < stages; ++st) {
     const int16_t *src = codes + st * m * T;
     if (kinds[st] == QS_CB_E8P) {
-      pack_e8p_kernel<<<ceil_div(threads, 256), 256, 0, s>>>(src, m, T, Tq, rows, dst);
+      pack_e8p_kernel<<<ceil_div(threads, 256), 256, 0, s>>>(src, m, T, RT, Tq, dst);
     } else {
-      pack_1bit_kernel<<<ceil_div(threads, 256), 256, 0, s>>>(src, m, T, Tq, rows, dst);
+      pack_1bit_kernel<<<ceil_div(threads, 256), 256, 0, s>>>(src, m, T, RT, Tq, dst);
       check = true;
     }
     int e = check_launch("pack");

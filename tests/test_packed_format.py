@@ -1,6 +1,6 @@
 """CPU check of the packed weight-stream format and of the integer recipes the
 fused matmul kernels use to decode it (quipsharp_b200/csrc/qs_pack.cu,
-qs_gemv_tc.cu, qs_gemm_tc.cu): pack 8 codes into a 16-byte quad, then rebuild
+qs_gemv.cu, qs_gemm_tc.cu): pack 8 codes into a 16-byte quad, then rebuild
 each code's eight fp16 weights with the same shifts / XORs / byte permutes /
 f16x2 adds, and compare with the oracle decode (bit-exact)."""
 import numpy as np
@@ -97,9 +97,9 @@ def shift_words_tmem(w3):
 
 
 def decode_quad_like_gemv(q):
-    """Mirror of the decode matmul (qs_gemv_tc.cu): sign*|t| words of the natural
-    pairs (one AND-XOR each) plus the +-1/4 shift words the tensor core adds
-    against per-code activation sums."""
+    """Mirror of the decode matmul (qs_gemv.cu e8p_words / shift_words): sign*|t|
+    words of the natural pairs (one AND-XOR each) plus the +-1/4 shift words the
+    tensor core adds against per-code activation sums."""
     w0, w1, _, w3 = q
     fa, fb = flips(q)
     shift = np.zeros(8, np.float32)
