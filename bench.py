@@ -1,21 +1,38 @@
 #!/usr/bin/env python
-"""Benchmark of the quantized-linear forward (QuantizedLinear.forward) on B200.
+"""Benchmark of the quantized-linear forward path (QuantizedLinear.forward) on B200.
 
-Default workload: 3-bit RVQ linear (E8P 2-bit stage +
-1-bit E8 residual stage), in=4096 -> out=11008, RFFT incoherence on both sides
-(2048-point FFT in, 5504-point IFFT out), fp16 activations N(0,1), batch 1.
+Default workload (the configuration the multi-GPU
+scaling claim is made on): the seven linears of a Llama-3-70B-shaped decoder
+layer (q, o 8192->8192; k, v 8192->1024; gate, up 8192->28672; down
+28672->8192) as 3-bit RVQ (E8P 2-bit + 1-bit residual), random codes / signs /
+stage scales from seeds, bf16 activations N(0,1), decode batch 1.  A step
+pushes one batch through the whole layer set in decoder order, each layer
+taking the latest earlier output of its input width (q takes the layer input;
+k, v and o take q's output in place of the attention input / output; gate and up
+take o's output; down takes up's output in place of act(gate) * up).
 
-A step pushes one batch of tokens through a stack of `--stack` quantized
-linears of that shape (independent layers, same input), cycling over L distinct
-weight copies whose total size (> 2x the 126 MB L2) keeps every weight read an
-HBM read.  value = tokens x layers / s, i.e. the per-layer token throughput.
+One GPU runs the layers unsharded.  N GPUs (torchrun, one process per GPU) run
+them column-sharded over output rows (TPQuantizedLinear: each rank decodes and
+multiplies its rows, the float32 row shards are all-gathered, every rank applies
+the full output transform): strong scaling, the same tokens per step at every N.
+Each rank cycles over enough distinct weight copies that its weights exceed
+twice the 126 MB L2 (every weight read is an HBM read).
 
-Prints one JSON line (rank 0).  `--impl reference` times the CPU port of the
+value: tokens through the layer set per second, CUDA-graph replay of the
+modules' forward, CUDA events on the launching stream, max over ranks.
+e2e: the same through the public module called eagerly from Python (no graph),
+with the pinned host input copied in and the output copied back every step.
+roofline: the fused decode + matmul kernel of the set, timed alone.
+At one GPU the line also carries `decode_c2` (3-bit RVQ
+4096 -> 11008 at batch 1) and `prefill_c4` (Qwen2.5-7B MLP
+at 2048 tokens) sub-records.  `--impl reference` times the CPU port of the
 reference algorithm (oracle/, numpy, all host cores) on the same workload.
+Prints one JSON line (rank 0).
 """
 from __future__ import annotations
 
 import argparse
+import datetime
 import json
 import math
 import os
@@ -29,25 +46,21 @@ ROOT = os.path.dirname(os.path.abspath(__file__))
 sys.path.insert(0, ROOT)
 
 L2_BYTES = 126 * 1024 * 1024
-
-# dram__bytes_read.sum + dram__bytes_write.sum per launch of the fused decode+matmul
-# kernel, from the ncu capture summarised in profiles/gemv_c2_b1.md
-NCU_TRAFFIC = {("c2_rvq3_4096to11008", 1): 16.98688e6}
+DEFAULT_CONFIG = "c5_llama3_70b_rvq3"
 
 
 def parse():
     p = argparse.ArgumentParser()
     p.add_argument("--gpus", type=int, default=1)
-    p.add_argument("--steps", type=int, default=20)
+    p.add_argument("--steps", type=int, default=10)
     p.add_argument("--warmup", type=int, default=3)
     p.add_argument("--impl", default="ours", choices=["ours", "reference"])
-    p.add_argument("--config", default="c2_rvq3_4096to11008")
+    p.add_argument("--config", default=DEFAULT_CONFIG)
     p.add_argument("--batch", type=int, default=1)
-    p.add_argument("--stack", type=int, default=8192, help="layers per step")
-    p.add_argument("--cpu-sample-s", type=float, default=15.0)
-    p.add_argument("--tp", action="store_true",
-                   help="tensor-parallel mode (not the default contract): the config's layer set "
-                        "column-sharded over the ranks, strong scaling")
+    p.add_argument("--passes", type=int, default=0,
+                   help="layer-set passes per step (0: about 2k layer forwards per step at decode batches)")
+    p.add_argument("--cpu-sample-s", type=float, default=20.0)
+    p.add_argument("--no-extras", action="store_true", help="skip the decode_c2 / prefill_c4 sub-records")
     return p.parse_args()
 
 
@@ -59,13 +72,14 @@ def dist_env():
 
 
 def measured_peaks():
+    """(hbm GB/s, bf16 burst TFLOP/s, bf16 sustained TFLOP/s, source)."""
     path = os.path.join(ROOT, "MEASURED_PEAKS.json")
     try:
         with open(path) as f:
             d = json.load(f)
-        return float(d["hbm_gbs"]), float(d["bf16_tflops"]), "measured"
+        return float(d["hbm_gbs"]), float(d["bf16_tflops"]), float(d.get("bf16_tflops_sustained", 1400.0)), "measured"
     except Exception:
-        return 6650.0, 1590.0, "fallback"
+        return 6650.0, 1590.0, 1400.0, "fallback"
 
 
 class ClockSampler:
@@ -138,12 +152,15 @@ def config_spec(name):
     return spec["layers"], spec["kinds"], spec["dtype"]
 
 
-def algorithmic_bytes(m, n, kinds, batch, elem=2):
-    """Survey 8(d): codes at the paper bit rate (2 bits/weight per E8P stage,
-    1 bit/weight per 1-bit stage) + activations in + outputs out + transform
-    vectors (+ nothing for bias here)."""
-    bits = sum(2 if k == "e8p" else 1 for k in kinds)
-    return m * n * bits // 8 + batch * n * elem + batch * m * elem + (m + n) * 4
+def layer_sources(layers):
+    """Input of each layer of a set: the latest earlier layer output of matching
+    width, else the set's input (-1).  In decoder order this gives q <- input;
+    k, v, o <- q; gate, up <- o; down <- up."""
+    src, latest = [], {}
+    for li, (_, m, n) in enumerate(layers):
+        src.append(latest.get(n, -1))
+        latest[m] = li
+    return src
 
 
 def gemv_bytes(m, n, kinds, batch):
@@ -154,8 +171,7 @@ def gemv_bytes(m, n, kinds, batch):
 
 
 def _two_pass_width(N):
-    """The library's two-pass RFFT width rule (qs_xform2.cu two_pass_rfft): N = P * 2^a
-    >= 4096 with one odd prime P <= 43 (not squared) and 2^a >= 64."""
+    """The library's two-pass RFFT width rule (qs_xform2.cu two_pass_rfft)."""
     if N < 4096:
         return False
     P = 0
@@ -170,26 +186,43 @@ def _two_pass_width(N):
     return N1 >= 64 and N1 & (N1 - 1) == 0
 
 
-def kernels_per_forward(m, n, batch, sms):
-    """This library's kernel launches for one forward of an (n -> m) layer: input
-    transform (two kernels for a two-pass RFFT width: many rows always, few rows in
-    decode), matmul (batches 9-32: one launch per 16 tokens), output transform (two
-    kernels for a two-pass width)."""
+def kernels_per_forward(m, n, batch, sms, shards=1):
+    """This library's kernel launches for one forward of an (n -> m) layer (m the full
+    output width): input transform (two kernels for a two-pass RFFT width), matmul
+    (batches 9-32: one launch per 16 tokens), output transform (two kernels for a
+    two-pass width; the shard-aware output step is one kernel)."""
     pow2 = lambda v: v & (v - 1) == 0
     matmul = 1 if batch >= 33 or batch <= 8 else math.ceil(batch / 16)
-    if pow2(m) and pow2(n):  # RHT both sides
+    if pow2(m) and pow2(n):
         return 1 + matmul + 1
     inp = 2 if _two_pass_width(n // 2) and (batch >= 33 or 2 * batch <= sms) else 1
-    out = 2 if _two_pass_width(m // 2) else 1
+    out = 2 if shards == 1 and _two_pass_width(m // 2) else 1
     return inp + matmul + out
 
 
-def cpu_oracle_forward(m, n, kinds, batch, dtype):
-    """A callable running the numpy port of the reference forward (oracle/)
-    on one synthetic layer of the workload's shape, on this host's cores."""
+def load_traffic_table():
+    """DRAM bytes per launch set of the fused decode+matmul, measured with ncu and
+    recorded in profiles/gemv_dram_traffic.md (lines `traffic <config> <batch> <world>
+    <bytes>`).  Returns {(config, batch, world): bytes}."""
+    out = {}
+    try:
+        with open(os.path.join(ROOT, "profiles", "gemv_dram_traffic.md")) as f:
+            for line in f:
+                parts = line.strip().strip("`").split()
+                if len(parts) == 5 and parts[0] == "traffic":
+                    out[(parts[1], int(parts[2]), int(parts[3]))] = float(parts[4])
+    except OSError:
+        pass
+    return out
+
+
+# ---------------------------------------------------------------- CPU (reference port)
+def cpu_oracle_forward(m, n, kinds, batch, dtype, seed=1):
+    """A callable running the numpy port of the reference forward (oracle/) on one
+    synthetic layer of the workload's shape, on this host's cores."""
     from oracle import quipsharp_oracle as O
     from quipsharp_b200 import synthetic as syn
-    lay = syn.make_layer(m, n, kinds, seed=1)
+    lay = syn.make_layer(m, n, kinds, seed=seed)
     x = syn.make_activations(batch, n, dtype=dtype, seed=2).float().numpy()
     t = lambda v: None if v is None else v.numpy()
     args = dict(su=t(lay.su), sv=t(lay.sv), phase_u=t(lay.phase_u), phase_v=t(lay.phase_v))
@@ -198,15 +231,17 @@ def cpu_oracle_forward(m, n, kinds, batch, dtype):
     return lambda: O.linear_forward(x, codes, list(lay.kinds), ss, lay.layer_scale, lay.transform_kind, **args)
 
 
-def cpu_oracle_forward_time(m, n, kinds, batch, dtype, budget_s, warmup=2):
-    run = cpu_oracle_forward(m, n, kinds, batch, dtype)
-    for _ in range(warmup):
-        run()
-    times = []
-    t_end = time.perf_counter() + budget_s
+def cpu_set_time(layers, kinds, batch, dtype, budget_s):
+    """Median time of whole passes over the layer set (numpy port), within budget_s
+    after one warm-up pass (at least one timed pass)."""
+    runs = [cpu_oracle_forward(m, n, kinds, batch, dtype, seed=1 + li) for li, (_, m, n) in enumerate(layers)]
+    for r in runs:
+        r()
+    times, t_end = [], time.perf_counter() + budget_s
     while not times or time.perf_counter() < t_end:
         t0 = time.perf_counter()
-        run()
+        for r in runs:
+            r()
         times.append(time.perf_counter() - t0)
     return statistics.median(times), len(times)
 
@@ -216,7 +251,7 @@ def run_reference(args):
     if rank != 0:
         return
     layers, kinds, dtype = config_spec(args.config)
-    runs = [cpu_oracle_forward(m, n, kinds, args.batch, dtype) for _, m, n in layers]
+    runs = [cpu_oracle_forward(m, n, kinds, args.batch, dtype, seed=1 + li) for li, (_, m, n) in enumerate(layers)]
     for _ in range(args.warmup):
         for run in runs:
             run()
@@ -226,381 +261,351 @@ def run_reference(args):
         for run in runs:
             run()
         per_step.append(time.perf_counter() - t0)
-    m, n = layers[0][1], layers[0][2]
     total = sum(per_step)
     value = args.batch * len(per_step) / total
     cores = os.cpu_count()
+    sample = (f"{len(per_step)} timed passes (after {args.warmup} warm-up) over the full {len(layers)}-layer set, "
+              f"batch {args.batch}: numpy port of the reference algorithm (oracle/quipsharp_oracle.py), "
+              f"BLAS threads = all {cores} host cores")
     line = {
-        "impl": "reference", "metric": f"quantized-linear tokens/s ({args.config}, batch {args.batch})",
+        "impl": "reference", "metric": f"quantized-linear tokens/s ({args.config} layer set, batch {args.batch})",
         "value": value, "unit": "tokens/s", "n_gpus": args.gpus, "steps": args.steps, "warmup": args.warmup,
-        "ms_per_step": 1000 * total / len(per_step), "higher_is_better": True, "scaling": "weak",
-        "vs_baseline": None, "dtype": "f32", "data": "synthetic",
+        "ms_per_step": 1000 * total / len(per_step), "higher_is_better": True,
+        "scaling": "strong" if args.gpus > 1 else "weak", "vs_baseline": None, "dtype": "f32", "data": "synthetic",
         "config": {"workload": args.config, "batch": args.batch, "layers": [list(l) for l in layers],
-                   "kinds": list(kinds), "step": "one full forward of every layer of the set on the host CPU"},
-        "cpu_baseline": {"value": value, "unit": "tokens/s", "cores": cores, "kind": "port",
-                         "sample": f"{len(per_step)} passes over the layer set (numpy port of the reference "
-                                   f"algorithm, oracle/quipsharp_oracle.py), BLAS threads = all {cores} host cores"},
+                   "kinds": list(kinds), "step": "one forward of every layer of the set on the host CPU"},
+        "cpu_baseline": {"value": value, "unit": "tokens/s", "cores": cores, "kind": "port", "sample": sample},
         "e2e": {"value": value, "unit": "tokens/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
     }
     print(json.dumps(line), flush=True)
 
 
+# ---------------------------------------------------------------- GPU
+def make_full_module(name, m, n, kinds, li, copy_id, dev, chained):
+    """A QuantizedLinear filled from a seeded synthetic layer; copy_id varies the codes
+    so distinct copies are distinct weights."""
+    import torch
+    from quipsharp_b200 import synthetic as syn
+    from quipsharp_b200.checkpoint import QuantizedLinear
+    from quipsharp_b200.codebooks import E8PCodebook, E8OneBitCodebook
+    from quipsharp_b200.quantize import RVQCodebookAdapter
+    from quipsharp_b200.rvq import RVQStage
+    base = syn.make_layer(m, n, kinds, seed=1 + li, layer_scale=(1.0 / math.sqrt(1.2 * n)) if chained else None)
+    mod = QuantizedLinear(n, m, 8, base.transform_kind, num_stages=len(kinds)).to(dev)
+    with torch.no_grad():
+        c = base.codes.to(dev)
+        if copy_id:
+            if c.dim() == 2:
+                c ^= (copy_id * 0x9E37) & 0x7FFF
+            else:
+                c[0] ^= (copy_id * 0x9E37) & 0x7FFF
+                c[1] ^= (copy_id * 37) & 0xFF if kinds[1] == "e8_1bit" else (copy_id * 0x9E37) & 0x7FFF
+        mod.codes.copy_(c)
+        mod.scale.fill_(base.layer_scale)
+        if base.transform_kind == "rht":
+            mod.su.copy_(base.su)
+            mod.sv.copy_(base.sv)
+        else:
+            mod.phase_u.copy_(base.phase_u)
+            mod.phase_v.copy_(base.phase_v)
+    cb = lambda k: E8PCodebook() if k == "e8p" else E8OneBitCodebook()
+    mod.codebook = cb(kinds[0]) if len(kinds) == 1 else RVQCodebookAdapter(
+        [RVQStage(cb(k), sc) for k, sc in zip(kinds, base.stage_scales)])
+    return mod
+
+
+class LayerSet:
+    """Copies of a config's layer set on this rank (sharded when world > 1)."""
+
+    def __init__(self, config, batch, dev, world, rank, copies=None):
+        import torch
+        from quipsharp_b200 import _native as N
+        from quipsharp_b200.tensor_parallel import TPQuantizedLinear
+        self.layers, self.kinds, self.dtype = config_spec(config)
+        self.config, self.B, self.dev, self.world = config, batch, dev, world
+        self.prefill = batch >= 33
+        self.src = layer_sources(self.layers)
+        karr = N.int_array([N.QS_CB_E8P if k == "e8p" else N.QS_CB_E8_1BIT for k in self.kinds])
+        self.rank_bytes = sum(N.lib().qs_packed_bytes(len(self.kinds), karr, m // world, n)
+                              for _, m, n in self.layers)
+        if copies is None:
+            copies = 1 if self.prefill else max(1, math.ceil(2 * L2_BYTES / self.rank_bytes))
+        self.L = copies
+        chained = len(self.layers) > 1
+        self.mods = []  # [copy][layer]
+        for c in range(copies):
+            row = []
+            for li, (name, m, n) in enumerate(self.layers):
+                full = make_full_module(name, m, n, self.kinds, li, c * 131 + rank * 7 + 1, dev, chained)
+                if world > 1:
+                    row.append(TPQuantizedLinear(full))
+                    del full
+                else:
+                    full.kernel()  # pack once, outside every timed region
+                    row.append(full)
+            self.mods.append(row)
+        torch.cuda.synchronize(dev)
+
+    def forward(self, x, copy):
+        outs = []
+        for li, mod in enumerate(self.mods[copy]):
+            outs.append(mod(x if self.src[li] < 0 else outs[self.src[li]]))
+        return outs[-1]
+
+    def kernels(self, li, copy):
+        mod = self.mods[copy][li]
+        return mod.local if self.world > 1 else mod.kernel()
+
+
+def _timed(fn, steps, warmup, stream, dev, world):
+    import torch
+    import torch.distributed as dist
+    for _ in range(warmup):
+        fn()
+    if world > 1:
+        dist.barrier()
+    torch.cuda.synchronize(dev)
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record(stream)
+    for _ in range(steps):
+        fn()
+    e1.record(stream)
+    torch.cuda.synchronize(dev)
+    if world > 1:
+        dist.barrier()
+    ms = e0.elapsed_time(e1)
+    if world > 1:
+        t = torch.tensor([ms], device=dev)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        ms = float(t.item())
+    return ms
+
+
+def _capture(fn, stream, dev):
+    import torch
+    g = torch.cuda.CUDAGraph()
+    with torch.cuda.stream(stream):
+        fn()  # warm (kernel attributes, packing, communicators)
+        torch.cuda.synchronize(dev)
+        with torch.cuda.graph(g, stream=stream):
+            out = fn()
+    torch.cuda.synchronize(dev)
+    return g, out
+
+
+def measure_set(ls, steps, warmup, stream, dev, world, passes, clocks=None):
+    """value (graph replay of the modules), matmul-only timing, eager e2e and graph
+    e2e for one LayerSet.  Returns a dict of raw timings."""
+    import torch
+    from quipsharp_b200 import _native as N
+    from quipsharp_b200 import synthetic as syn
+    B, L = ls.B, ls.L
+    n_in = ls.layers[0][2]
+    x_host = syn.make_activations(B, n_in, dtype=ls.dtype, seed=2).pin_memory()
+    x_dev = torch.empty(B, n_in, dtype=ls.dtype, device=dev)
+    x_dev.copy_(x_host)
+    # fail fast on a broken pipeline (a bounded wait that ran out)
+    with torch.no_grad():
+        ls.forward(x_dev, 0)
+    torch.cuda.synchronize(dev)
+    N.check(N.lib().qs_device_status(torch.cuda.current_stream(dev).cuda_stream))
+
+    def one_step():
+        y = None
+        for _ in range(passes):
+            for c in range(L):
+                y = ls.forward(x_dev, c)
+        return y
+
+    with torch.no_grad():
+        g_step, y_graph = _capture(one_step, stream, dev)
+
+        def replay():
+            with torch.cuda.stream(stream):
+                g_step.replay()
+        if clocks is not None:
+            with clocks:
+                ms_value = _timed(replay, steps, warmup, stream, dev, world)
+        else:
+            ms_value = _timed(replay, steps, warmup, stream, dev, world)
+
+        # matmul-only: every layer's fused decode + matmul on this rank's rows
+        ws, y1 = {}, {}
+        for li, (_, m, n) in enumerate(ls.layers):
+            k = ls.kernels(li, 0)
+            if n not in ws:
+                x = torch.randn(B, n, device=dev).to(ls.dtype)
+                ws[n] = k.input(x, None)
+            y1[li] = torch.empty(B, k.m, dtype=torch.float32, device=dev)
+
+        def mm_step():
+            for _ in range(passes):
+                for c in range(L):
+                    for li, (_, m, n) in enumerate(ls.layers):
+                        ls.kernels(li, c).matmul(ws[n], B, y1[li])
+        g_mm, _ = _capture(mm_step, stream, dev)
+
+        def replay_mm():
+            with torch.cuda.stream(stream):
+                g_mm.replay()
+        mm_steps = max(3, steps // 2)
+        ms_mm = _timed(replay_mm, mm_steps, 2, stream, dev, world)
+
+        # e2e: the public module called eagerly, host input in and output out per step
+        y_host = torch.empty(B, ls.layers[-1][1], dtype=ls.dtype).pin_memory()
+
+        def eager():
+            with torch.cuda.stream(stream):
+                x_dev.copy_(x_host, non_blocking=True)
+                y = one_step()
+                y_host.copy_(y, non_blocking=True)
+        ms_e2e = _timed(eager, steps, max(2, warmup), stream, dev, world)
+
+        def graph_e2e():
+            with torch.cuda.stream(stream):
+                x_dev.copy_(x_host, non_blocking=True)
+                g_step.replay()
+                y_host.copy_(y_graph, non_blocking=True)
+        ms_e2e_graph = _timed(graph_e2e, steps, warmup, stream, dev, world)
+    del g_step, g_mm
+    return dict(ms_value=ms_value, ms_mm=ms_mm, mm_steps=mm_steps, ms_e2e=ms_e2e, ms_e2e_graph=ms_e2e_graph,
+                h2d=x_host.numel() * x_host.element_size(), d2h=y_host.numel() * y_host.element_size())
+
+
+def default_passes(ls):
+    if ls.prefill:
+        return 1
+    per_pass = ls.L * len(ls.layers)
+    return max(1, math.ceil(2048 / per_pass))
+
+
+def sub_record_decode(dev, stream):
+    """BASELINE configs[1] (3-bit RVQ 4096 -> 11008, fp16, batch 1): per-layer token
+    throughput and the fused decode + matmul against HBM bandwidth."""
+    hbm, _, _, src = measured_peaks()
+    ls = LayerSet("c2_rvq3_4096to11008", 1, dev, 1, 0)
+    passes = max(1, math.ceil(4096 / ls.L))
+    r = measure_set(ls, 5, 3, stream, dev, 1, passes)
+    m, n = ls.layers[0][1], ls.layers[0][2]
+    forwards = passes * ls.L
+    us_mm = 1e3 * r["ms_mm"] / (r["mm_steps"] * forwards)
+    gb = gemv_bytes(m, n, ls.kinds, 1)
+    out = {"workload": "c2_rvq3_4096to11008", "batch": 1, "unit": "tokens/s",
+           "value": forwards * 5 / (r["ms_value"] / 1e3), "us_per_forward": 1e3 * r["ms_value"] / (5 * forwards),
+           "kernel_us": us_mm, "kernel_gbs": gb / us_mm / 1e3, "kernel_frac_hbm": gb / us_mm / 1e3 / hbm,
+           "distinct_copies": ls.L, "peak_source": src}
+    del ls
+    return out
+
+
+def sub_record_prefill(dev, stream):
+    """BASELINE configs[3] (Qwen2.5-7B MLP gate, up, down as E8P 2-bit, bf16, 2048
+    tokens): tokens/s, and TFLOP/s of the tcgen05 GEMM and of the whole layer set."""
+    _, burst, sust, src = measured_peaks()
+    ls = LayerSet("c4_qwen25_7b_prefill", 2048, dev, 1, 0)
+    r = measure_set(ls, 5, 3, stream, dev, 1, 1)
+    flops = sum(2.0 * 2048 * m * n for _, m, n in ls.layers)
+    gemm_tf = flops * r["mm_steps"] / (r["ms_mm"] / 1e3) / 1e12
+    set_tf = flops * 5 / (r["ms_value"] / 1e3) / 1e12
+    out = {"workload": "c4_qwen25_7b_prefill", "batch": 2048, "unit": "tokens/s",
+           "value": 2048 * 5 / (r["ms_value"] / 1e3), "ms_per_layer_set": r["ms_value"] / 5,
+           "gemm_tflops": gemm_tf, "gemm_frac_burst": gemm_tf / burst, "gemm_frac_sustained": gemm_tf / sust,
+           "set_tflops": set_tf, "set_frac_burst": set_tf / burst, "peak_source": src}
+    del ls
+    return out
+
+
 def run_ours(args):
     import torch
     import torch.distributed as dist
-    from quipsharp_b200 import _native as N
-    from quipsharp_b200 import synthetic as syn
-    from quipsharp_b200.checkpoint import QuantizedLinear
-    from quipsharp_b200.codebooks import E8PCodebook, E8OneBitCodebook
-    from quipsharp_b200.quantize import RVQCodebookAdapter
-    from quipsharp_b200.rvq import RVQStage
 
     world, rank, local = dist_env()
     if world > 1:
-        import datetime
-        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120))
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120),
+                                device_id=torch.device("cuda", local))
     torch.cuda.set_device(local)
     dev = torch.device("cuda", local)
-    layers, kinds, dtype = config_spec(args.config)
-    B = args.batch
-    prefill = B >= 33  # kTcMinBatch: the tcgen05 GEMM
-    chained = len(layers) > 1
-    karr = N.int_array([N.QS_CB_E8P if k == "e8p" else N.QS_CB_E8_1BIT for k in kinds])
-    set_bytes = sum(N.lib().qs_packed_bytes(len(kinds), karr, m, n) for _, m, n in layers)
-    # decode regime: cycle distinct copies of the layer set so weights always come from HBM
-    L = 1 if prefill else max(1, math.ceil(2 * L2_BYTES / set_bytes))
-    cb = lambda k: E8PCodebook() if k == "e8p" else E8OneBitCodebook()
-
-    mods = []  # [copy][layer]
-    for l in range(L):
-        row = []
-        for li, (name, m, n) in enumerate(layers):
-            base = syn.make_layer(m, n, kinds, seed=1 + li,
-                                  layer_scale=(1.0 / math.sqrt(1.2 * n)) if chained else None)
-            mod = QuantizedLinear(n, m, 8, base.transform_kind, num_stages=len(kinds)).to(dev)
-            with torch.no_grad():
-                c = base.codes.to(dev)
-                if c.dim() == 2:
-                    c ^= (l * 0x9E37 + rank * 0x3B1) & 0x7FFF
-                else:
-                    c[0] ^= (l * 0x9E37 + rank * 0x3B1) & 0x7FFF
-                    c[1] ^= (l * 37 + rank) & 0xFF if kinds[1] == "e8_1bit" else (l * 0x9E37) & 0x7FFF
-                mod.codes.copy_(c)
-                mod.scale.fill_(base.layer_scale)
-                if base.transform_kind == "rht":
-                    mod.su.copy_(base.su)
-                    mod.sv.copy_(base.sv)
-                else:
-                    mod.phase_u.copy_(base.phase_u)
-                    mod.phase_v.copy_(base.phase_v)
-            mod.codebook = cb(kinds[0]) if len(kinds) == 1 else RVQCodebookAdapter(
-                [RVQStage(cb(k), sc) for k, sc in zip(kinds, base.stage_scales)])
-            mod.kernel()  # pack once, outside every timed region
-            row.append(mod)
-        mods.append(row)
-    # layers per step: whole passes over the copies, at least --stack layer forwards
-    R = max(1, math.ceil(args.stack / (L * len(layers)))) if not prefill else max(1, args.stack // 8192)
-    passes = R * L
-    n_in = layers[0][2]
     stream = torch.cuda.Stream(dev)
-    x_host = syn.make_activations(B, n_in, dtype=dtype, seed=2).pin_memory()
-    x_dev = torch.empty(B, n_in, dtype=dtype, device=dev)
-    x_dev.copy_(x_host)
-    io = N.IO_DTYPES[dtype]
+    hbm, burst, sust, peak_src = measured_peaks()
 
-    # ---- buffers of the direct C-ABI pass (value): chain each layer's input by dimension
-    max_in = max(n for _, _, n in layers)
-    max_out = max(m for _, m, _ in layers)
-    ws_in_b = max(N.lib().qs_linear_input_bytes(B, n) for _, _, n in layers)
-    ws_in = torch.empty(ws_in_b, dtype=torch.uint8, device=dev)
-    y1 = torch.empty(B * max_out, dtype=torch.float32, device=dev)
-    outs = {}
-    plan = []  # (kernel, input tensor, output tensor)
-    for li, (name, m, n) in enumerate(layers):
-        src = x_dev if n == n_in and li == 0 else outs.get(n, x_dev if n == n_in else None)
-        if src is None:
-            src = syn.make_activations(B, n, dtype=dtype, seed=10 + li).to(dev)
-        out = torch.empty(B, m, dtype=dtype, device=dev)
-        outs[m] = out
-        plan.append((li, src, out, m, n))
-    result = plan[-1][2]
-
-    def one_pass(copy, s, matmul_only=False):
-        for li, src, out, m, n in plan:
-            k = mods[copy][li].kernel()
-            if not matmul_only:
-                N.check(N.lib().qs_linear_input(N.ptr(src), io, B, n, k.transform, N.ptr(k.sv), N.ptr(k.phase_v),
-                                                N.ptr(ws_in), ws_in_b, None if prefill else N.ptr(y1), m, s))
-            N.check(N.lib().qs_linear_matmul(N.ptr(ws_in), B, n, m, N.ptr(k.packed), len(k.kinds), k._kinds_c,
-                                             k._ss_c, N.ptr(k.scale), N.ptr(y1), s))
-            if not matmul_only:
-                N.check(N.lib().qs_linear_output(N.ptr(y1), m, 1, B, m, k.transform, N.ptr(k.su),
-                                                 N.ptr(k.phase_u), N.ptr(k.bias), N.ptr(out), io, s))
-
-    def capture(fn):
-        g = torch.cuda.CUDAGraph()
-        with torch.cuda.stream(stream):
-            fn(stream.cuda_stream)  # warm (sets kernel attributes)
-            torch.cuda.synchronize(dev)
-            with torch.cuda.graph(g, stream=stream):
-                fn(stream.cuda_stream)
-        torch.cuda.synchronize(dev)
-        return g
-
-    g_pass = capture(lambda s: [one_pass(c, s) for c in range(L)])
-    g_mm = capture(lambda s: [one_pass(c, s, matmul_only=True) for c in range(L)])
-
-    def barrier():
-        if world > 1:
-            dist.barrier()
-        torch.cuda.synchronize(dev)
-
-    def timed(fn, steps, warmup):
-        for _ in range(warmup):
-            fn()
-        barrier()
-        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-        e0.record(stream)
-        for _ in range(steps):
-            fn()
-        e1.record(stream)
-        barrier()
-        ms = e0.elapsed_time(e1)
-        if world > 1:
-            t = torch.tensor([ms], device=dev)
-            dist.all_reduce(t, op=dist.ReduceOp.MAX)
-            ms = float(t.item())
-        return ms
-
-    def step_value():
-        with torch.cuda.stream(stream):
-            for _ in range(R):
-                g_pass.replay()
-
-    # ---- value: device-resident inputs
-    with ClockSampler(local) as clk:
-        ms_total = timed(step_value, args.steps, args.warmup)
-    ms_step = ms_total / args.steps
-    tokens = B * passes * args.steps * world
-    value = tokens / (ms_total / 1e3)
-    flops_set = sum(2.0 * B * m * n for _, m, n in layers)
-
-    # ---- dominant kernel, timed alone on the same stream
-    def step_mm():
-        with torch.cuda.stream(stream):
-            for _ in range(R):
-                g_mm.replay()
-    mm_steps = max(3, args.steps // 2)
-    ms_mm = timed(step_mm, mm_steps, 2)
-    launches_mm = mm_steps * R * L * len(layers)
-    us_per_mm = 1e3 * ms_mm / launches_mm
-    hbm_peak, tc_peak, peak_kind = measured_peaks()
-    if prefill:
-        achieved = flops_set * mm_steps * R * L / (ms_mm / 1e3) / 1e12
-        try:
-            with open(os.path.join(ROOT, "MEASURED_PEAKS.json")) as f:
-                tc_sust = float(json.load(f)["bf16_tflops_sustained"])
-        except Exception:
-            tc_sust = 1400.0
-        roofline = {"bound": "tensor", "achieved": achieved, "peak": tc_sust, "unit": "TFLOP/s",
-                    "frac": achieved / tc_sust, "traffic": None,
+    ls = LayerSet(args.config, args.batch, dev, world, rank)
+    passes = args.passes or default_passes(ls)
+    clk = ClockSampler(local)
+    r = measure_set(ls, args.steps, args.warmup, stream, dev, world, passes, clocks=clk)
+    B = args.batch
+    tokens = B * passes * args.steps
+    value = tokens / (r["ms_value"] / 1e3)
+    ms_step = r["ms_value"] / args.steps
+    flops_set = sum(2.0 * B * m * n for _, m, n in ls.layers)
+    launches_mm = r["mm_steps"] * passes * ls.L * len(ls.layers)
+    us_per_mm = 1e3 * r["ms_mm"] / launches_mm
+    if ls.prefill:
+        achieved = flops_set / world * r["mm_steps"] * passes * ls.L / (r["ms_mm"] / 1e3) / 1e12
+        roofline = {"bound": "tensor", "achieved": achieved, "peak": sust, "unit": "TFLOP/s",
+                    "frac": achieved / sust, "traffic": None,
                     "kernel": "qs::gemm_tc_kernel (fused decode + tcgen05 GEMM, 128x256 tiles)",
-                    "algorithmic_flops_per_layer_set": flops_set, "us_per_launch": us_per_mm,
-                    "peak_source": f"{peak_kind} (MEASURED_PEAKS.json bf16_tflops_sustained; burst {tc_peak})"}
+                    "algorithmic_flops_per_layer_set_per_rank": flops_set / world, "us_per_launch": us_per_mm,
+                    "peak_source": f"{peak_src} (MEASURED_PEAKS.json bf16_tflops_sustained; burst {burst})"}
     else:
-        gb = sum(gemv_bytes(m, n, kinds, B) for _, m, n in layers)
-        achieved = gb * mm_steps * R * L / (ms_mm / 1e3) / 1e9
-        # DRAM bytes per launch of the dominant kernel from an ncu capture of this
-        # workload (profiles/gemv_c2_b1.md); other workloads have none yet
-        traffic = NCU_TRAFFIC.get((args.config, B))
-        roofline = {"bound": "hbm", "achieved": achieved, "peak": hbm_peak, "unit": "GB/s",
-                    "frac": achieved / hbm_peak, "traffic": traffic,
+        gb = sum(gemv_bytes(m // world, n, ls.kinds, B) for _, m, n in ls.layers)
+        achieved = gb * r["mm_steps"] * passes * ls.L / (r["ms_mm"] / 1e3) / 1e9
+        traffic = load_traffic_table().get((args.config, B, world))
+        roofline = {"bound": "hbm", "achieved": achieved, "peak": hbm, "unit": "GB/s", "frac": achieved / hbm,
+                    "traffic": traffic,
+                    "traffic_basis": "ncu dram__bytes_read.sum + dram__bytes_write.sum summed over one launch of "
+                                     "each layer of the set on one rank (profiles/gemv_dram_traffic.md)",
                     "kernel": "qs::gemv_kernel (fused decode + mma.sync matmul)",
-                    "algorithmic_bytes_per_layer_set": gb, "us_per_launch": us_per_mm,
-                    "peak_source": f"{peak_kind} (MEASURED_PEAKS.json hbm_gbs)"}
-
-    # ---- e2e: public module API; pinned host input in, the chain's result out, every step
-    def fwd_all(s):
-        o = None
-        for c in range(L):
-            cur = {n_in: x_dev}
-            for li, (name, m, n) in enumerate(layers):
-                inp = cur.get(n)
-                if inp is None:
-                    inp = plan[li][1]
-                cur[m] = mods[c][li](inp)
-            o = cur[layers[-1][1]]
-        return o
-
-    g_api = torch.cuda.CUDAGraph()
-    with torch.cuda.stream(stream):
-        fwd_all(None)
-        torch.cuda.synchronize(dev)
-        with torch.cuda.graph(g_api, stream=stream):
-            api_out = fwd_all(None)
-    torch.cuda.synchronize(dev)
-    y_host = torch.empty(api_out.shape, dtype=api_out.dtype).pin_memory()
-
-    def step_e2e():
-        with torch.cuda.stream(stream):
-            x_dev.copy_(x_host, non_blocking=True)
-            for _ in range(R):
-                g_api.replay()
-            y_host.copy_(api_out, non_blocking=True)
-    ms_e2e = timed(step_e2e, args.steps, args.warmup)
-    e2e_value = tokens / (ms_e2e / 1e3)
+                    "algorithmic_bytes_per_layer_set_per_rank": gb, "us_per_launch": us_per_mm,
+                    "peak_source": f"{peak_src} (MEASURED_PEAKS.json hbm_gbs)"}
 
     cpu = None
     if rank == 0 and world == 1 and args.cpu_sample_s > 0:
-        t_set, cnt = 0.0, 0
-        budget = args.cpu_sample_s / len(layers)
-        for _, m, n in layers:
-            t, c_ = cpu_oracle_forward_time(m, n, kinds, B, dtype, budget_s=budget)
-            t_set += t
-            cnt += c_
+        t_set, cnt = cpu_set_time(ls.layers, ls.kinds, B, ls.dtype, args.cpu_sample_s)
         cpu = {"value": B / t_set, "unit": "tokens/s", "cores": os.cpu_count(), "kind": "port",
-               "sample": f"{cnt} full layer forwards over the {len(layers)}-layer set, batch {B} (numpy port of the "
-                         f"reference algorithm, oracle/quipsharp_oracle.py); median per layer summed = {t_set:.3f} s"}
+               "sample": f"{cnt} timed full passes (after one warm-up) over the {len(ls.layers)}-layer set at batch "
+                         f"{B}: numpy port of the reference algorithm (oracle/quipsharp_oracle.py) on all host "
+                         f"cores; median pass {t_set:.2f} s"}
+    sms = torch.cuda.get_device_properties(dev).multi_processor_count
+    launches = args.steps * passes * ls.L * sum(kernels_per_forward(m, n, B, sms, world) for _, m, n in ls.layers)
+    copies = ls.L
+    del ls
+    extras = {}
+    if world == 1 and not args.no_extras:
+        extras["decode_c2"] = sub_record_decode(dev, stream)
+        extras["prefill_c4"] = sub_record_prefill(dev, stream)
 
     if rank == 0:
         c = clk.summary()
-        bits = sum(2 if k == "e8p" else 1 for k in kinds)
-        metric = (f"quantized-linear prefill tokens/s ({args.config}, batch {B})" if prefill
-                  else f"quantized-linear tokens/s ({args.config}, batch {B})")
+        layers, kinds, dtype = config_spec(args.config)
         line = {
-            "metric": metric, "value": value, "unit": "tokens/s", "n_gpus": world, "steps": args.steps,
-            "warmup": args.warmup, "ms_per_step": ms_step, "higher_is_better": True, "scaling": "weak",
-            "vs_baseline": None, "dtype": "f16" if dtype == torch.float16 else "bf16", "data": "synthetic",
+            "metric": f"quantized-linear tokens/s ({args.config} layer set, batch {B})",
+            "value": value, "unit": "tokens/s", "n_gpus": world, "steps": args.steps, "warmup": args.warmup,
+            "ms_per_step": ms_step, "higher_is_better": True, "scaling": "strong" if world > 1 else "weak",
+            "vs_baseline": None, "dtype": "bf16" if dtype == torch.bfloat16 else "f16", "data": "synthetic",
             "config": {"workload": args.config, "batch": B, "layers": [list(l) for l in layers], "kinds": list(kinds),
-                       "layer_set_passes_per_step": passes, "distinct_copies": L,
-                       "weight_bytes_per_copy": set_bytes,
-                       "l2": (f"inputs larger than L2: {L} distinct copies = {L * set_bytes / 1e6:.0f} MB of packed "
-                              f"weights cycled per pass (L2 126 MB)") if not prefill else
-                             "inputs larger than L2: per-layer y1 / activations of the batch exceed 126 MB",
-                       "bits_per_weight": bits},
+                       "parallelism": f"tp{world} (column-sharded output rows)" if world > 1 else "single GPU",
+                       "layer_set_passes_per_step": passes,
+                       "distinct_copies_per_rank": copies,
+                       "l2": "inputs larger than L2: distinct weight copies cycled so each rank streams more than "
+                             "2 x 126 MB per pass" if B < 33 else
+                             "inputs larger than L2: activations / y1 of the batch exceed 126 MB",
+                       "bits_per_weight": sum(2 if k == "e8p" else 1 for k in kinds)},
             "us_per_layer_set": 1e3 * ms_step / passes,
-            "hbm_gbs_per_forward": sum(algorithmic_bytes(m, n, kinds, B) for _, m, n in layers) * passes * args.steps
-                                   / (ms_total / 1e3) / 1e9,
-            "tflops": flops_set * passes * args.steps / (ms_total / 1e3) / 1e12,
+            "tflops": flops_set * passes * args.steps / (r["ms_value"] / 1e3) / 1e12,
             "roofline": roofline,
             "cpu_baseline": cpu,
-            "e2e": {"value": e2e_value, "unit": "tokens/s", "h2d_bytes_per_step": B * n_in * x_host.element_size(),
-                    "d2h_bytes_per_step": y_host.numel() * y_host.element_size(),
-                    "path": "QuantizedLinear.forward (public module) over the layer set x passes per step, replayed "
-                            "as a CUDA graph; pinned host input copied in and the last layer's output copied out "
-                            "each step"},
-            "gpu_launches": args.steps * R * L * sum(
-                kernels_per_forward(m, n, B, torch.cuda.get_device_properties(dev).multi_processor_count)
-                for _, m, n in layers),
+            "e2e": {"value": tokens / (r["ms_e2e"] / 1e3), "unit": "tokens/s", "h2d_bytes_per_step": r["h2d"],
+                    "d2h_bytes_per_step": r["d2h"],
+                    "path": "QuantizedLinear.forward (TPQuantizedLinear.forward at N > 1) called eagerly from "
+                            "Python over the layer set x passes per step; pinned host input copied in and the last "
+                            "layer's output copied out each step"},
+            "e2e_graph": {"value": tokens / (r["ms_e2e_graph"] / 1e3), "unit": "tokens/s",
+                          "path": "the same step captured once as a CUDA graph and replayed"},
+            "gpu_launches": launches,
             "clocks": {"sm_mhz": c["sm_mhz"], "sm_max_mhz": c["sm_max_mhz"], "reasons": c["reasons"]},
         }
+        line.update(extras)
         print(json.dumps(line), flush=True)
-    del g_pass, g_mm, g_api
-    if world > 1:
-        dist.barrier()
-        dist.destroy_process_group()
-
-
-def run_tp(args):
-    """Tensor-parallel mode: every layer of the config's set column-sharded over the
-    ranks (TPQuantizedLinear: local fused matmul, NCCL all-gather of the float32 y1
-    shards, full-width output transform on every rank).  Strong scaling: one batch
-    through the whole set per step, replayed as a CUDA graph (collectives included)
-    and timed with CUDA events (max over ranks); at one rank the unsharded module
-    runs, as the baseline."""
-    import datetime
-    import torch
-    import torch.distributed as dist
-    from quipsharp_b200 import synthetic as syn
-    from quipsharp_b200.checkpoint import QuantizedLinear
-    from quipsharp_b200.codebooks import E8PCodebook, E8OneBitCodebook
-    from quipsharp_b200.quantize import RVQCodebookAdapter
-    from quipsharp_b200.rvq import RVQStage
-    from quipsharp_b200.tensor_parallel import TPQuantizedLinear
-
-    world, rank, local = dist_env()
-    if world > 1:
-        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120))
-    torch.cuda.set_device(local)
-    dev = torch.device("cuda", local)
-    layers, kinds, dtype = config_spec(args.config)
-    B = args.batch
-    cb = lambda k: E8PCodebook() if k == "e8p" else E8OneBitCodebook()
-    mods = []
-    for li, (name, m, n) in enumerate(layers):
-        base = syn.make_layer(m, n, kinds, seed=1 + li, layer_scale=1.0 / math.sqrt(1.2 * n))
-        full = QuantizedLinear(n, m, 8, base.transform_kind, num_stages=len(kinds)).to(dev)
-        with torch.no_grad():
-            full.codes.copy_(base.codes.to(dev))
-            full.scale.fill_(base.layer_scale)
-            if base.transform_kind == "rht":
-                full.su.copy_(base.su)
-                full.sv.copy_(base.sv)
-            else:
-                full.phase_u.copy_(base.phase_u)
-                full.phase_v.copy_(base.phase_v)
-        full.codebook = cb(kinds[0]) if len(kinds) == 1 else RVQCodebookAdapter(
-            [RVQStage(cb(k), sc) for k, sc in zip(kinds, base.stage_scales)])
-        if world > 1:
-            mods.append((n, m, TPQuantizedLinear(full)))
-            del full
-        else:
-            full.kernel()
-            mods.append((n, m, full))
-    x0 = syn.make_activations(B, layers[0][2], dtype=dtype, seed=2).to(dev)
-
-    def step():
-        latest = {x0.shape[1]: x0}
-        for n, m, mod in mods:
-            latest[m] = mod(latest[n])
-
-    stream = torch.cuda.Stream(dev)
-    graph = None
-
-    def timed(k):
-        if world > 1:
-            dist.barrier()
-        torch.cuda.synchronize()
-        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-        with torch.cuda.stream(stream):
-            e0.record(stream)
-            for _ in range(k):
-                if graph is not None:
-                    graph.replay()
-                else:
-                    step()
-            e1.record(stream)
-        torch.cuda.synchronize()
-        ms = torch.tensor([e0.elapsed_time(e1)], device=dev)
-        if world > 1:
-            dist.all_reduce(ms, op=dist.ReduceOp.MAX)
-        return float(ms.item())
-
-    with torch.no_grad():
-        timed(max(args.warmup, 3))  # eager warm-up (packing, NCCL communicator set-up)
-        # one step (kernels and the NCCL all-gathers) captured as a CUDA graph and replayed
-        graph = torch.cuda.CUDAGraph()
-        with torch.cuda.stream(stream):
-            torch.cuda.synchronize()
-            with torch.cuda.graph(graph, stream=stream):
-                step()
-        torch.cuda.synchronize()
-        timed(max(args.warmup, 3))
-        with ClockSampler(local) as clk:
-            ms = timed(args.steps)
-    graph = None  # release the graph (it holds NCCL work) before the process group goes
-    if rank == 0:
-        c = clk.summary()
-        print(json.dumps({
-            "metric": f"quantized-linear tokens/s ({args.config}, batch {B}, tensor-parallel)",
-            "value": B * args.steps / (ms / 1000.0), "unit": "tokens/s", "n_gpus": world,
-            "steps": args.steps, "warmup": max(args.warmup, 3), "ms_per_step": ms / args.steps,
-            "higher_is_better": True, "scaling": "strong", "vs_baseline": None,
-            "dtype": str(dtype).replace("torch.", "").replace("bfloat16", "bf16").replace("float16", "f16"),
-            "data": "synthetic", "config": {"workload": args.config, "batch": B, "tp": world,
-                                            "layers": [list(l) for l in layers], "timing": "CUDA graph replay, max over ranks"},
-            "clocks": {"sm_mhz": c["sm_mhz"], "sm_max_mhz": c["sm_max_mhz"], "reasons": c["reasons"]},
-        }), flush=True)
     if world > 1:
         dist.barrier()
         dist.destroy_process_group()
@@ -610,8 +615,6 @@ def main():
     args = parse()
     if args.impl == "reference":
         run_reference(args)
-    elif args.tp:
-        run_tp(args)
     else:
         run_ours(args)
 
