@@ -13,8 +13,10 @@ take o's output; down takes up's output in place of act(gate) * up).
 
 One GPU runs the layers unsharded.  N GPUs (torchrun, one process per GPU) run
 them column-sharded over output rows (TPQuantizedLinear: each rank decodes and
-multiplies its rows, the float32 row shards are all-gathered, every rank applies
-the full output transform): strong scaling, the same tokens per step at every N.
+multiplies its rows, pushes its float32 row shard into every rank's receive
+buffer over NVLink with a flag in peer memory, and every rank applies the full
+output transform to the gathered rows): strong scaling, the same tokens per
+step at every N.
 Each rank cycles over enough distinct weight copies that its weights exceed
 twice the 126 MB L2 (every weight read is an HBM read).
 
@@ -189,15 +191,17 @@ def _two_pass_width(N):
 def kernels_per_forward(m, n, batch, sms, shards=1):
     """This library's kernel launches for one forward of an (n -> m) layer (m the full
     output width): input transform (two kernels for a two-pass RFFT width), matmul
-    (batches 9-32: one launch per 16 tokens), output transform (two kernels for a
-    two-pass width; the shard-aware output step is one kernel)."""
+    (batches 9-32: one launch per 16 tokens), with shards > 1 the push of the row
+    shard to every rank, output transform (two kernels for a two-pass width; the
+    gathered output step of a sharded layer is one kernel)."""
     pow2 = lambda v: v & (v - 1) == 0
     matmul = 1 if batch >= 33 or batch <= 8 else math.ceil(batch / 16)
+    push = 1 if shards > 1 else 0
     if pow2(m) and pow2(n):
-        return 1 + matmul + 1
+        return 1 + matmul + push + 1
     inp = 2 if _two_pass_width(n // 2) and (batch >= 33 or 2 * batch <= sms) else 1
     out = 2 if shards == 1 and _two_pass_width(m // 2) else 1
-    return inp + matmul + out
+    return inp + matmul + push + out
 
 
 def load_traffic_table():

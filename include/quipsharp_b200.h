@@ -203,6 +203,71 @@ int qs_linear_output(float *y1, int64_t ld_y1, int64_t shards, int64_t batch, in
                      int transform, const float *su, const void *phase_u, const float *bias,
                      void *y, int y_dtype, qs_stream_t stream);
 
+/* ---- column-sharded tensor parallelism over peer memory -------------------
+ * No counterpart in the reference (it places whole decoder layers on devices,
+ * quipsharp/checkpoint.py:236-262); this is the scale-out of one layer over the
+ * GPUs of a node.  Rank r of `world` holds weight rows [r m/world, (r+1)
+ * m/world) (its own qs_pack_codes stream of those rows).  Every rank allocates
+ * (zeroed) a float32 receive buffer of two regions of recv_floats each, an
+ * int32 flag array [2][world] and two uint32 control words; it exports the
+ * receive buffer and the flags with qs_ipc_export, exchanges the handles with
+ * its peers (any host channel) and maps theirs with qs_ipc_import; qs_tp_peers
+ * then lists every rank's buffers as mapped in this process.  Each call pushes
+ * this rank's y1 shard into every rank's receive buffer (stores over NVLink)
+ * and announces it through the flags; the region a call uses follows a call
+ * counter kept in the control words on the device, so calls may be captured
+ * in CUDA graphs and replayed in any mix with direct calls.  All ranks must
+ * make the same sequence of calls on one peer set; calls are stream-ordered;
+ * ranks synchronise only through the flags, whose waits are bounded
+ * (qs_set_wait_limit_ns; a wait that runs out sets the qs_device_status flag
+ * and the call's output is invalid). */
+#define QS_TP_MAX_RANKS 8
+typedef struct qs_tp_peers {
+  int world;                            /* ranks, 1..QS_TP_MAX_RANKS */
+  int rank;                             /* this process's rank */
+  float *recv[QS_TP_MAX_RANKS];         /* every rank's receive buffer (float32 [2][recv_floats]) */
+  int *flags[QS_TP_MAX_RANKS];          /* every rank's flags (int32 [2][world]) */
+  unsigned *ctl;                        /* this rank's control words (uint32 [2], 8-byte aligned) */
+  int64_t recv_floats;                  /* floats per region (>= batch * m of every call) */
+} qs_tp_peers;
+
+/* CUDA IPC of a device pointer (any pointer into a cudaMalloc allocation):
+ * handle is 64 bytes (cudaIpcMemHandle_t), offset the pointer's offset in its
+ * allocation.  qs_ipc_import maps a peer's allocation (peer access enabled
+ * lazily) and returns the pointer at the same offset; qs_ipc_close unmaps it. */
+int qs_ipc_export(const void *ptr, void *handle, int64_t *offset);
+int qs_ipc_import(const void *handle, int64_t offset, void **ptr);
+int qs_ipc_close(void *ptr, int64_t offset);
+
+/* Workspace bytes of qs_linear_fwd_tp: the x2 workspace of qs_linear_input
+ * and this rank's private y1 shard (batch, m_local) float32. */
+int64_t qs_linear_tp_workspace_bytes(int64_t batch, int64_t n, int64_t m_local);
+
+/* QuantizedLinear.forward of one column-sharded layer on this rank
+ * (quipsharp/checkpoint.py:141-146 -> quipsharp/quantize.py:116-124, the rows
+ * split over ranks): input step, fused decode + matmul of this rank's rows
+ * (packed: this rank's row shard, m / world rows) into a private y1 shard,
+ * push of the shard to every rank, output step over the gathered y1.  m, su,
+ * phase_u, bias and y are the full layer's (every rank ends with the whole
+ * output).  workspace: qs_linear_tp_workspace_bytes(batch, n, m / world)
+ * bytes, 256-byte aligned. */
+int qs_linear_fwd_tp(const void *x, int x_dtype, int64_t batch, int64_t n, int64_t m,
+                     const void *packed, int stages, const int *kinds, const float *stage_scales,
+                     const float *layer_scale, int transform, const float *su, const float *sv,
+                     const void *phase_u, const void *phase_v, const float *bias, void *y,
+                     void *workspace, int64_t workspace_bytes, const qs_tp_peers *peers,
+                     qs_stream_t stream);
+/* The last two steps alone, for callers that compute the shard themselves:
+ * qs_tp_push copies this rank's y1 shard (batch, m_local) float32 into every
+ * rank's receive buffer (after the work before it on the stream) and
+ * announces it; qs_linear_output_peers waits for all ranks' shards of the
+ * call and applies the output step to the gathered y1 (m = m_local * world). */
+int qs_tp_push(const qs_tp_peers *peers, const float *y1, int64_t batch, int64_t m_local,
+               qs_stream_t stream);
+int qs_linear_output_peers(const qs_tp_peers *peers, int64_t batch, int64_t m, int transform,
+                           const float *su, const void *phase_u, const float *bias, void *y,
+                           int y_dtype, qs_stream_t stream);
+
 #ifdef __cplusplus
 }
 #endif

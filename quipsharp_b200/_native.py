@@ -61,7 +61,27 @@ _SIGS = {
     "qs_linear_input": (_I, [_P, _I, _L, _L, _I, _P, _P, _P, _L, _P, _L, _P]),
     "qs_linear_matmul": (_I, [_P, _L, _L, _L, _P, _I, _P, _P, _P, _P, _P]),
     "qs_linear_output": (_I, [_P, _L, _L, _L, _L, _I, _P, _P, _P, _P, _I, _P]),
+    "qs_ipc_export": (_I, [_P, _P, _P]),
+    "qs_ipc_import": (_I, [_P, _L, _P]),
+    "qs_ipc_close": (_I, [_P, _L]),
+    "qs_linear_tp_workspace_bytes": (_L, [_L, _L, _L]),
+    "qs_tp_push": (_I, [_P, _P, _L, _L, _P]),
+    "qs_linear_output_peers": (_I, [_P, _L, _L, _I, _P, _P, _P, _P, _I, _P]),
+    "qs_linear_fwd_tp": (_I, [_P, _I, _L, _L, _L, _P, _I, _P, _P, _P, _I, _P, _P, _P, _P, _P, _P, _P, _L, _P,
+                              _P]),
 }
+
+QS_TP_MAX_RANKS = 8
+
+
+class TPPeers(ctypes.Structure):
+    """qs_tp_peers (include/quipsharp_b200.h): every rank's receive buffer and
+    flag array as mapped in this process, and this rank's control words."""
+    _fields_ = [("world", ctypes.c_int), ("rank", ctypes.c_int),
+                ("recv", ctypes.c_void_p * QS_TP_MAX_RANKS),
+                ("flags", ctypes.c_void_p * QS_TP_MAX_RANKS),
+                ("ctl", ctypes.c_void_p),
+                ("recv_floats", ctypes.c_int64)]
 EXPORTS = tuple(_SIGS)
 
 _lib = None

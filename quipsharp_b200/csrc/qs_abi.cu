@@ -236,6 +236,72 @@ QS_API int qs_linear_output(float *y1, int64_t ld_y1, int64_t shards, int64_t ba
                               bias, y, y_dtype, (cudaStream_t)stream);
 }
 
+QS_API int qs_ipc_export(const void *ptr, void *handle, int64_t *offset) {
+  if (!ptr || !handle || !offset) return fail(QS_ERR_INVALID_ARG, "null pointer");
+  return ipc_export(ptr, handle, offset);
+}
+
+QS_API int qs_ipc_import(const void *handle, int64_t offset, void **ptr) {
+  if (!handle || !ptr || offset < 0) return fail(QS_ERR_INVALID_ARG, "bad argument");
+  return ipc_import(handle, offset, ptr);
+}
+
+QS_API int qs_ipc_close(void *ptr, int64_t offset) {
+  if (!ptr || offset < 0) return fail(QS_ERR_INVALID_ARG, "bad argument");
+  return ipc_close(ptr, offset);
+}
+
+QS_API int64_t qs_linear_tp_workspace_bytes(int64_t batch, int64_t n, int64_t m_local) {
+  if (batch < 0 || n <= 0 || m_local <= 0) return -1;
+  return tp_workspace_bytes(batch, n, m_local);
+}
+
+QS_API int qs_tp_push(const qs_tp_peers *peers, const float *y1, int64_t batch, int64_t m_local,
+                      qs_stream_t stream) {
+  if (batch < 0 || m_local <= 0) return fail(QS_ERR_INVALID_ARG, "bad shape");
+  if (batch > 0 && !y1) return fail(QS_ERR_INVALID_ARG, "null pointer");
+  return launch_tp_push(peers, y1, batch, m_local, (cudaStream_t)stream);
+}
+
+QS_API int qs_linear_output_peers(const qs_tp_peers *peers, int64_t batch, int64_t m, int transform,
+                                  const float *su, const void *phase_u, const float *bias, void *y, int y_dtype,
+                                  qs_stream_t stream) {
+  if (!valid_io_dtype(y_dtype)) return fail(QS_ERR_INVALID_ARG, "bad dtype %d", y_dtype);
+  int st = check_transform_args(transform, m, transform == QS_RHT ? 1 : 2, su, su, phase_u, phase_u);
+  if (st) return st;
+  if (batch < 0) return fail(QS_ERR_INVALID_ARG, "bad batch");
+  if (batch == 0) return QS_OK;  // nothing to read (the matching push still counted the call)
+  if (!y) return fail(QS_ERR_INVALID_ARG, "null pointer");
+  return launch_output_peers(peers, batch, m, transform, su, phase_u, bias, y, y_dtype, (cudaStream_t)stream);
+}
+
+QS_API int qs_linear_fwd_tp(const void *x, int x_dtype, int64_t batch, int64_t n, int64_t m, const void *packed,
+                            int stages, const int *kinds, const float *stage_scales, const float *layer_scale,
+                            int transform, const float *su, const float *sv, const void *phase_u,
+                            const void *phase_v, const float *bias, void *y, void *workspace,
+                            int64_t workspace_bytes, const qs_tp_peers *peers, qs_stream_t stream) {
+  int st = check_kinds(stages, kinds);
+  if (st) return st;
+  if (!valid_io_dtype(x_dtype)) return fail(QS_ERR_INVALID_ARG, "bad dtype %d", x_dtype);
+  if (!peers || peers->world < 1 || peers->world > QS_TP_MAX_RANKS || peers->rank < 0 || peers->rank >= peers->world)
+    return fail(QS_ERR_INVALID_ARG, "bad peers");
+  if (batch < 0 || n <= 0 || m <= 0 || n % 8 || m % peers->world) return fail(QS_ERR_INVALID_ARG, "bad shape");
+  st = check_transform_args(transform, m, n, su, sv, phase_u, phase_v);
+  if (st) return st;
+  if (transform == QS_RFFT && (m / peers->world) % 2)
+    return fail(QS_ERR_INVALID_ARG, "RFFT shards must hold an even number of columns");
+  if (batch == 0) return QS_OK;  // every rank skips the call: no push, no wait
+  if (!x || !y || !packed || !layer_scale || !workspace) return fail(QS_ERR_INVALID_ARG, "null pointer");
+  if (stages == 2 && !stage_scales) return fail(QS_ERR_INVALID_ARG, "RVQ needs stage scales");
+  if (workspace_bytes < tp_workspace_bytes(batch, n, m / peers->world))
+    return fail(QS_ERR_WORKSPACE, "workspace too small");
+  if (!aligned(workspace, 256) || !aligned(packed, 256))
+    return fail(QS_ERR_ALIGNMENT, "workspace/packed must be 256-byte aligned");
+  if (batch * m > peers->recv_floats) return fail(QS_ERR_WORKSPACE, "receive buffers too small");
+  return launch_linear_fwd_tp(x, x_dtype, batch, n, m, packed, stages, kinds, stage_scales, layer_scale, transform,
+                              su, sv, phase_u, phase_v, bias, y, workspace, peers, (cudaStream_t)stream);
+}
+
 QS_API int qs_linear_fwd(const void *x, int x_dtype, int64_t batch, int64_t n, int64_t m,
                          const void *packed, int stages, const int *kinds,
                          const float *stage_scales, const float *layer_scale, int transform,

@@ -673,6 +673,20 @@ uint64_t pipeline_wait_ns() { return g_wait_ns.load(std::memory_order_relaxed); 
 
 void set_pipeline_wait_ns(uint64_t ns) { g_wait_ns.store(ns ? ns : kDefaultWaitNs, std::memory_order_relaxed); }
 
+int *device_error_flag() {
+  static int *cached[64] = {nullptr};
+  static std::mutex mu;
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess || dev >= 64) return nullptr;
+  std::lock_guard<std::mutex> lock(mu);
+  if (!cached[dev]) {
+    void *p = nullptr;
+    if (cudaGetSymbolAddress(&p, g_tc_error) != cudaSuccess) return nullptr;
+    cached[dev] = static_cast<int *>(p);
+  }
+  return cached[dev];
+}
+
 int device_status(cudaStream_t s) {
   int flag = 0;
   static const int zero = 0;
@@ -681,7 +695,8 @@ int device_status(cudaStream_t s) {
   if (flag) {
     QS_CUDA_TRY(cudaMemcpyToSymbolAsync(g_tc_error, &zero, sizeof(int), 0, cudaMemcpyHostToDevice, s));
     QS_CUDA_TRY(cudaStreamSynchronize(s));
-    return fail(QS_ERR_TIMEOUT, "a pipeline wait in the prefill matmul timed out; its results are invalid");
+    return fail(QS_ERR_TIMEOUT, "a bounded wait ran out (prefill matmul pipeline or tensor-parallel shard arrival); "
+                "the results of that launch are invalid");
   }
   return QS_OK;
 }

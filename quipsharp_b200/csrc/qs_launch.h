@@ -5,6 +5,8 @@
 #include <cuda_runtime.h>
 #include <stdint.h>
 
+#include "../../include/quipsharp_b200.h"
+
 struct CUtensorMap_st;  // CUtensorMap (cuda.h)
 
 namespace qs {
@@ -27,9 +29,10 @@ int64_t linear_input_bytes(int64_t batch, int64_t n);
 int launch_linear_input(const void *x, int x_dtype, int64_t batch, int64_t n, int transform,
                         const float *sv, const void *phase_v, void *x2ws, float *y1,
                         int64_t m_local, cudaStream_t s);
+struct XPeerGather;
 int launch_linear_output(float *y1, int64_t ld_y1, int64_t shards, int64_t batch, int64_t m,
                          int transform, const float *su, const void *phase_u, const float *bias,
-                         void *y, int y_dtype, cudaStream_t s);
+                         void *y, int y_dtype, cudaStream_t s, const XPeerGather *pg = nullptr);
 int check_fft_size(int64_t n_complex);
 int check_fwht_size(int64_t n);
 
@@ -41,6 +44,19 @@ int launch_two_pass_input(const void *x, int dtype, int64_t batch, int64_t n, co
                           cudaStream_t s);
 int launch_two_pass_output(float *y1, int64_t batch, int64_t m, const float2 *phase, const float *bias, float scale,
                            void *y, int dtype, cudaStream_t s);
+
+// qs_tp.cu: column-sharded tensor parallelism over peer memory
+int ipc_export(const void *ptr, void *handle, int64_t *offset);
+int ipc_import(const void *handle, int64_t offset, void **ptr);
+int ipc_close(void *ptr, int64_t offset);
+int64_t tp_workspace_bytes(int64_t batch, int64_t n, int64_t m_local);
+int launch_tp_push(const qs_tp_peers *pe, const float *y1, int64_t batch, int64_t m_local, cudaStream_t s);
+int launch_output_peers(const qs_tp_peers *pe, int64_t batch, int64_t m, int transform, const float *su,
+                        const void *phase_u, const float *bias, void *y, int y_dtype, cudaStream_t s);
+int launch_linear_fwd_tp(const void *x, int x_dtype, int64_t batch, int64_t n, int64_t m, const void *packed,
+                         int stages, const int *kinds, const float *stage_scales, const float *layer_scale,
+                         int transform, const float *su, const float *sv, const void *phase_u, const void *phase_v,
+                         const float *bias, void *y, void *workspace, const qs_tp_peers *pe, cudaStream_t s);
 
 // qs_pack.cu
 int launch_pack(const int16_t *codes, int stages, const int *kinds, int64_t m, int64_t n,
@@ -57,6 +73,8 @@ int launch_matmul_tc(const void *x2ws, int64_t batch, int64_t n, int64_t m, cons
                      const int *kinds, const float *stage_scales, const float *layer_scale, float *y1,
                      cudaStream_t s);
 int device_status(cudaStream_t s);
+// Device address (current device) of the error flag qs_device_status reports.
+int *device_error_flag();
 // 2-D tensor map over fp16 rows (rows x n_pad, row stride n_pad elements) with
 // a box of box_x elements x box_y rows; 128-byte swizzle or none.
 int encode_fp16_rows_map(::CUtensorMap_st *map, const void *x2h, int64_t n_pad, int64_t rows, int box_x, int box_y,

@@ -326,12 +326,13 @@ int launch_linear_input(const void *x, int x_dtype, int64_t batch, int64_t n, in
 
 int launch_linear_output(float *y1, int64_t ld_y1, int64_t shards, int64_t batch, int64_t m, int transform,
                          const float *su, const void *phase_u, const float *bias, void *y, int y_dtype,
-                         cudaStream_t s) {
+                         cudaStream_t s, const XPeerGather *pg) {
   XPlan p;
   XLaunch L;
   int st;
   if (transform == QS_RHT) {
     if ((st = make_fwht_plan(m, batch, p, L))) return st;
+    if (pg) L.pg = *pg;
     const float sc = inv_sqrt_f32(m);
     return p.C > 1 ? run_xoutput_rht<true>(L, s, y1, ld_y1, shards, batch, p, su, bias, sc, y, y_dtype)
                    : run_xoutput_rht<false>(L, s, y1, ld_y1, shards, batch, p, su, bias, sc, y, y_dtype);
@@ -342,9 +343,10 @@ int launch_linear_output(float *y1, int64_t ld_y1, int64_t shards, int64_t batch
   // the two-pass store loop reads phase / bias and writes y two complex values at a time
   const bool aligned16 = (reinterpret_cast<uintptr_t>(ph) & 15) == 0 && (reinterpret_cast<uintptr_t>(bias) & 15) == 0 &&
                          (reinterpret_cast<uintptr_t>(y) & 15) == 0;
-  if (shards == 1 && ld_y1 == m && aligned16 && two_pass_rfft(m / 2, batch, nullptr, nullptr))
+  if (!pg && shards == 1 && ld_y1 == m && aligned16 && two_pass_rfft(m / 2, batch, nullptr, nullptr))
     return launch_two_pass_output(y1, batch, m, ph, bias, sc, y, y_dtype, s);
   if ((st = make_fft_plan(m / 2, batch, p, L))) return st;
+  if (pg) L.pg = *pg;
   switch (p.big) {
 #define QS_CASE(B)                                                                                                \
   case B:                                                                                                         \

@@ -955,13 +955,66 @@ __device__ __forceinline__ int64_t xy1_offset(int64_t row, int64_t col, int64_t 
 // two buffers of xbuf_elems<T>(E) elements.  A cluster needs no barrier before
 // exit: after the row transform's last barrier every CTA reads only its own
 // buffers (and, in the input kernels, the group reduction ends with a barrier).
+// Output step of a column-sharded layer whose y1 shards every rank pushed into
+// this rank's receive buffer (tensor parallelism over peer memory): the call's
+// parity region base + (seq & 1) * stride holds the rank-major gathered layout
+// of xy1_offset, complete once every flags[(seq & 1) * nflags + r] has reached
+// the call's sequence number seq (set by rank r after its pushed data,
+// system-scope release).  flags == null: y1 is the kernel's y1 argument.
+constexpr int kMaxPeers = 8;
+struct XPeerGather {
+  const float *base;     // this rank's receive buffer (parity region 0): gathered rank-major shards
+  int64_t stride;        // floats between the two parity regions
+  const int *flags;       // this rank's arrival flags, int32 [2][nflags]
+  const unsigned *seq;    // this rank's call sequence number (written by its push kernel)
+  int nflags;
+  uint64_t wait_ns;
+  int *error;  // set when the flags did not all arrive within wait_ns
+};
+
 struct XRowArgs {
   int64_t row_base;
   int C;
   int early;  // release the dependent kernel at the start (few rows) or only at exit (many rows)
   int warm;   // input kernels, one CTA per row: may run a dry pass before waiting (see xinput_rfft_kernel)
   int *busy;  // device flag: set while a few-row output step runs (a hint, see xbusy_flag)
+  XPeerGather pg;
 };
+
+// Waits (every CTA, bounded) until every rank's shard of this call has arrived
+// in this rank's receive buffer and returns the parity region holding them;
+// nullptr on timeout (error flag set, the caller then reads zeros).  The call's
+// sequence number was written by this rank's push kernel, complete before the
+// caller's pdl_wait returned; each rank stores the sequence number into flag
+// [parity][its rank] after its pushed data.
+__device__ __forceinline__ const float *xwait_peers(const XPeerGather &pg) {
+  __shared__ int s_par;
+  if (threadIdx.x == 0) {
+    const unsigned seq = *reinterpret_cast<const volatile unsigned *>(pg.seq);
+    const int par = static_cast<int>(seq & 1u);
+    const int *fl = pg.flags + par * pg.nflags;
+    bool ok = true;
+    uint64_t t0 = 0;
+    for (int r = 0; r < pg.nflags && ok; ++r) {
+      for (;;) {
+        int v;
+        asm volatile("ld.acquire.sys.global.b32 %0, [%1];" : "=r"(v) : "l"(fl + r) : "memory");
+        if (static_cast<int>(static_cast<unsigned>(v) - seq) >= 0) break;
+        uint64_t t;
+        asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
+        if (!t0) t0 = t;
+        if (t - t0 > pg.wait_ns) {
+          ok = false;
+          atomicExch(pg.error, 1);
+          break;
+        }
+      }
+    }
+    s_par = ok ? par : -1;
+  }
+  __syncthreads();
+  return s_par < 0 ? nullptr : pg.base + s_par * pg.stride;
+}
 
 // Hint flag for the input kernels' dry pass: few-row output steps set it at
 // their start (they release the next kernel at once) and clear it at their
@@ -1119,9 +1172,11 @@ __global__ void __launch_bounds__(kXMaxThreads, 1) xoutput_rfft_kernel(
     xprefetch_l2(bias, 8 * static_cast<int64_t>(N), rank, plan.C);
   }
   build_xtw(tw, N);
-  pdl_wait();  // y1 comes from the matmul (or the all-gather)
+  pdl_wait();  // y1 comes from the matmul (or the all-gather, or the ranks' pushes)
+  const float *src = ra.pg.flags ? xwait_peers(ra.pg) : y1;
   auto gsrc = [&](int e) {
-    return *reinterpret_cast<const float2 *>(y1 + xy1_offset(row, 2 * e, ld_y1, shards, mp, batch));
+    return src ? *reinterpret_cast<const float2 *>(src + xy1_offset(row, 2 * e, ld_y1, shards, mp, batch))
+               : float2{0.f, 0.f};
   };
   auto sink = [&](int e, float2 z) {
     z.x *= scale;
@@ -1245,8 +1300,9 @@ __global__ void __launch_bounds__(kXMaxThreads, 1) xoutput_rht_kernel(
     xprefetch_l2(su, 4 * static_cast<int64_t>(m), rank, plan.C);
     xprefetch_l2(bias, 4 * static_cast<int64_t>(m), rank, plan.C);
   }
-  pdl_wait();
-  auto gsrc = [&](int i) { return y1[xy1_offset(row, i, ld_y1, shards, mp, batch)]; };
+  pdl_wait();  // y1 comes from the matmul (or the all-gather, or the ranks' pushes)
+  const float *src = ra.pg.flags ? xwait_peers(ra.pg) : y1;
+  auto gsrc = [&](int i) { return src ? src[xy1_offset(row, i, ld_y1, shards, mp, batch)] : 0.f; };
   auto sink = [&](int i, float v) {
     v = v * scale * su[i];
     if (bias) v += bias[i];
@@ -1262,6 +1318,7 @@ struct XLaunch {
   size_t smem;
   int64_t rows;
   int warm = 0;  // input kernels: dry pass allowed (XRowArgs::warm; few rows, one CTA per row)
+  XPeerGather pg = {};  // output kernels: y1 shards pushed by the ranks (flags == null: none)
 };
 
 template <int BIG, bool CL>
@@ -1333,7 +1390,7 @@ int xlaunch(const char *what, void (*kern)(KArgs...), const XLaunch &L, int C, c
     // prologue at once.  Many rows: its CTAs would take SMs this grid still
     // needs, so it is released only at exit.
     const int early = L.rows * 2 <= xlaunch_sms() ? 1 : 0;
-    XRowArgs ra{r0, C, early, early && L.warm && !CL ? 1 : 0, xbusy_flag()};
+    XRowArgs ra{r0, C, early, early && L.warm && !CL ? 1 : 0, xbusy_flag(), L.pg};
     const cudaError_t e = xlaunch_ex(cfg, kern, args..., ra);
     if (e != cudaSuccess) return fail(QS_ERR_CUDA, "%s launch failed: %s", what, cudaGetErrorString(e));
   }

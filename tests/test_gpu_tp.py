@@ -1,7 +1,9 @@
-"""Tensor parallelism on GPUs: two NCCL ranks (one process per GPU) run
-TPQuantizedLinear (column-sharded fused matmul, NCCL all-gather of the float32
-y1 shards, shard-aware output transform) and must reproduce the unsharded
-QuantizedLinear forward on every rank.  Needs two GPUs; skipped otherwise."""
+"""Tensor parallelism on GPUs: two ranks (one process per GPU) run
+TPQuantizedLinear (column-sharded fused matmul, push of the float32 y1 shards
+into every rank's receive buffer over NVLink, flags in peer memory, gathered
+output transform) and must reproduce the unsharded QuantizedLinear forward on
+every rank, over several calls (alternating receive regions) and through a
+CUDA graph replayed between eager calls.  Needs two GPUs; skipped otherwise."""
 import os
 import socket
 import sys
@@ -41,15 +43,39 @@ def _rank_main(rank, world, port, m, n, kinds, transform, B, dtype_name, q):
         lay = syn.make_layer(m, n, kinds, seed=11, transform_kind=transform, has_bias=True)
         x = syn.make_activations(B, n, dtype=dt, seed=12).cuda()
         full = make_module(lay)          # on cuda:rank (current device)
-        y_ref = full(x)
         tp = TPQuantizedLinear(full)
-        y_tp = tp(x)
+        err, same = 0.0, True
+
+        def check(y_tp, xin):
+            nonlocal err, same
+            y_ref = full(xin)
+            torch.cuda.synchronize()
+            err = max(err, rel_l2(y_tp.float().cpu().numpy(), y_ref.float().cpu().numpy()))
+            ys = [torch.empty_like(y_tp) for _ in range(world)]  # every rank holds the same output
+            dist.all_gather(ys, y_tp)
+            same = same and all(torch.equal(ys[0], t) for t in ys[1:])
+
+        for call in range(3):
+            xc = syn.make_activations(B, n, dtype=dt, seed=12 + call).cuda()
+            check(tp(xc), xc)
+        # one captured call (odd), replayed between eager calls
+        g = torch.cuda.CUDAGraph()
+        s = torch.cuda.Stream()
+        s.wait_stream(torch.cuda.current_stream())
+        with torch.cuda.stream(s), torch.cuda.graph(g, stream=s):
+            yg = tp(x)
+        torch.cuda.current_stream().wait_stream(s)
+        for step in range(3):
+            x.copy_(syn.make_activations(B, n, dtype=dt, seed=40 + step).cuda())
+            g.replay()
+            check(yg, x)
+            if step != 1:
+                check(tp(x), x)
+        from quipsharp_b200 import _native as N
         torch.cuda.synchronize()
-        err = rel_l2(y_tp.float().cpu().numpy(), y_ref.float().cpu().numpy())
-        # every rank holds the same full output
-        ys = [torch.empty_like(y_tp) for _ in range(world)]
-        dist.all_gather(ys, y_tp)
-        same = all(torch.equal(ys[0], t) for t in ys[1:])
+        if N.lib().qs_device_status(N.stream_of(x)) != 0:
+            err = "device status flag set"
+        del g
         q.put((rank, err, same))
         dist.barrier()
         dist.destroy_process_group()

@@ -1,7 +1,8 @@
 """Tensor-parallel host logic on CPU with world_size 2 over gloo.
 
 Each rank computes its row shard of y1 with the oracle, the shards are
-all-gathered exactly as TPQuantizedLinear does (rank-major, one flat buffer),
+gathered in the layout TPQuantizedLinear's push kernels write into every
+rank's receive buffer (rank-major, one flat buffer),
 the gathered buffer is read through `gathered_offset` (the index function of
 the output-transform kernel), and the output transform is applied; the result
 must equal the unsharded forward.  A second test kills one rank before the
