@@ -203,6 +203,25 @@ int qs_linear_output(float *y1, int64_t ld_y1, int64_t shards, int64_t batch, in
                      int transform, const float *su, const void *phase_u, const float *bias,
                      void *y, int y_dtype, qs_stream_t stream);
 
+/* ---- codebook construction: stage-scale sweeps ----------------------------
+ * build_codebook (quipsharp/checkpoint.py:60-77) rebuilds an RVQ codebook from
+ * (bits, seed) by sweeping candidate scales (quipsharp/rvq.py:28-66):
+ *   fit_stage_scale:          mse(s) = mean ||x - s Q(x / s)||^2
+ *   fit_residual_stage_scale: the same on x - RVQ_prev(x)
+ * over Gaussian samples x (samples x 8 float32, device).  Q is one codebook
+ * (rvq == 0: kinds[0]) or an RVQ of `stages` codebooks with stage_scales
+ * (rvq == 1, quipsharp/rvq.py:69-80); prev_stages (0..2) codebooks with
+ * prev_scales are quantized away first.  candidates: host float32 array of
+ * ncand (1..128) scales.  Writes mse (device double[ncand]) and best (device
+ * int: the first candidate with the smallest mse).  Kinds and scales are host
+ * arrays.  workspace: qs_fit_workspace_bytes(samples, ncand) bytes. */
+int64_t qs_fit_workspace_bytes(int64_t samples, int ncand);
+int qs_fit_scale_sweep(const float *x, int64_t samples, int prev_stages, const int *prev_kinds,
+                       const float *prev_scales, int rvq, int stages, const int *kinds,
+                       const float *stage_scales, const float *candidates, int ncand,
+                       void *workspace, int64_t workspace_bytes, double *mse, int *best,
+                       qs_stream_t stream);
+
 /* ---- column-sharded tensor parallelism over peer memory -------------------
  * No counterpart in the reference (it places whole decoder layers on devices,
  * quipsharp/checkpoint.py:236-262); this is the scale-out of one layer over the

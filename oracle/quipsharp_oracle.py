@@ -278,3 +278,79 @@ def linear_forward(x: np.ndarray, codes, kinds, stage_scales, layer_scale: float
     if bias is not None:
         y = (y + np.asarray(bias, np.float32)).astype(np.float32)
     return y if out_dtype is None else y.astype(out_dtype)
+
+
+# ---- codebook construction: nearest-point search and the scale sweep --------------
+
+def e8p_nearest(y: np.ndarray) -> np.ndarray:
+    """E8PCodebook.quantize values (quipsharp/codebooks/e8p.py:104-160), float32.
+
+    For z = y + 1/4 and z = y - 1/4, each of the 256 base rows takes the signs
+    agreeing with z (flip where z_i a_i < 0), repaired to even parity by toggling
+    the coordinate with the smallest |z_i a_i| (first on ties); the row nearest to
+    z wins (first on ties), the + side wins ties between sides, and the value is
+    v - 1/4 (+ side) or v + 1/4 (- side).  y: (S, 8) float32."""
+    abs_tab, _ = _tables()
+    y = np.asarray(y, dtype=np.float32)
+
+    def side(z):
+        prod = z[:, None, :] * abs_tab[None]                       # (S, 256, 8)
+        flip = prod < 0
+        wrong = flip.sum(-1) % 2 == 1
+        mc = np.abs(prod).argmin(-1)                               # first smallest
+        s_idx, k_idx = np.nonzero(wrong)
+        flip[s_idx, k_idx, mc[s_idx, k_idx]] ^= True
+        vals = np.where(flip, -abs_tab[None], abs_tab[None]).astype(np.float32)
+        d2 = ((z[:, None, :] - vals) ** 2).sum(-1, dtype=np.float32)
+        k = d2.argmin(-1)                                          # first nearest row
+        r = np.arange(z.shape[0])
+        return vals[r, k], d2[r, k]
+
+    pv, pd = side((y + np.float32(0.25)).astype(np.float32))
+    mv, md = side((y - np.float32(0.25)).astype(np.float32))
+    plus = (pd <= md)[:, None]
+    return np.where(plus, pv - np.float32(0.25), mv + np.float32(0.25)).astype(np.float32)
+
+
+def e8_1bit_nearest(y: np.ndarray) -> np.ndarray:
+    """E8OneBitCodebook.quantize values (quipsharp/codebooks/e8_1bit.py:81-84):
+    the table row nearest to y (first on ties), float32."""
+    _, tab = _tables()
+    y = np.asarray(y, dtype=np.float32)
+    d2 = ((y[:, None, :] - tab[None]) ** 2).sum(-1, dtype=np.float32)
+    return tab[d2.argmin(-1)]
+
+
+def stage_nearest(kind: str, y: np.ndarray) -> np.ndarray:
+    return e8p_nearest(y) if kind == E8P else e8_1bit_nearest(y)
+
+
+def rvq_quantize_vals(x: np.ndarray, stages) -> np.ndarray:
+    """rvq_quantize values (quipsharp/rvq.py:69-80): per stage (kind, scale),
+    q = Q(r / s), total += q s, r -= q s, in float32."""
+    r = np.asarray(x, dtype=np.float32)
+    total = np.zeros_like(r)
+    for kind, s in stages:
+        s = np.float32(s)
+        q = stage_nearest(kind, (r / s).astype(np.float32))
+        qs = (q * s).astype(np.float32)
+        total = (total + qs).astype(np.float32)
+        r = (r - qs).astype(np.float32)
+    return total
+
+
+def sweep_scale_mse(x: np.ndarray, stages, candidates, rvq: bool, prev=()) -> np.ndarray:
+    """Per candidate s: mean (x' - s Q(x' / s))^2 over all elements, float64, where
+    x' = x - rvq_quantize(x, prev) (rvq.py:28-37, 53-66).  Q is the plain codebook
+    stages[0][0] (rvq False) or the RVQ of `stages` (rvq True)."""
+    x = np.asarray(x, dtype=np.float32)
+    if prev:
+        x = (x - rvq_quantize_vals(x, prev)).astype(np.float32)
+    out = []
+    for s in candidates:
+        s = np.float32(s)
+        y = (x / s).astype(np.float32)
+        q = rvq_quantize_vals(y, stages) if rvq else stage_nearest(stages[0][0], y)
+        e = (x - (q * s).astype(np.float32)).astype(np.float32)
+        out.append(float(np.mean((e * e).astype(np.float32), dtype=np.float64)))
+    return np.array(out)

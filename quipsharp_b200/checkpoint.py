@@ -11,12 +11,11 @@ the int16 codes are re-laid into the kernel's weight stream once and cached
 Checkpoints: a directory with the model's state dict (`quantized_state.pt`) and a
 JSON manifest (`quip_config.json`: model_id, bits, block_size, seed and one entry per
 quantized module), written and read exactly as the reference does, so checkpoints
-saved by either side load in the other.  The reference rebuilds a 3/4-bit RVQ
-codebook at load time by re-fitting its stage scales (a quantization sweep, offline
-work this package does not carry); here the stage scales come from the caller's
-codebook or from an optional `stage_scales` manifest entry that
-`save_quantized_checkpoint` writes (the reference's loader ignores it).  A 2-bit
-codebook needs no scales.
+saved by either side load in the other.  A 3/4-bit RVQ codebook is rebuilt at load
+time as the reference does: `build_codebook` re-runs the seeded stage-scale sweeps
+(on the GPU, `quipsharp_b200.rvq.fit_stage_scale`); a `stage_scales` manifest entry
+(written by this package's `save_quantized_checkpoint`, ignored by the reference's
+loader) or the caller's codebook skips the sweep.  A 2-bit codebook needs no scales.
 """
 from __future__ import annotations
 
@@ -130,19 +129,44 @@ def replace_with_quantized_linear_(parent: nn.Module, attr: str, layer: Quantize
     return qlin
 
 
-def codebook_for(bits: str, stage_scales=None):
+def build_codebook(bits: str, device=None, seed: int = 0):
+    """checkpoint.py:60-77: the codebook of `bits` and its fitted input scale,
+    deterministic given `seed`: E8P (2-bit) or an RVQ of [E8P, E8-1bit] (3-bit) /
+    [E8P, E8P] (4-bit) whose stage scales come from the reference's sweeps (E8P on
+    N(0, I) with seed; the second stage on stage 1's residuals with seed + 1; the
+    returned scale for the whole RVQ with seed + 2; 20,000 samples each).  The
+    sweeps run on `device` when it is a CUDA device, else on the current one."""
+    from .codebooks import E8PCodebook, E8OneBitCodebook
+    from .rvq import RVQStage, fit_stage_scale, fit_residual_stage_scale
+    if bits not in ("2bit", "3bit", "4bit"):
+        raise ValueError(f"unknown bits {bits!r}")
+    e8p = E8PCodebook()
+    e8p_scale = fit_stage_scale(e8p, seed=seed, device=device, n_samples=20_000)
+    if bits == "2bit":
+        return e8p, e8p_scale
+    second = E8OneBitCodebook() if bits == "3bit" else E8PCodebook()
+    second_scale = fit_residual_stage_scale([RVQStage(e8p, e8p_scale)], second, seed=seed + 1, device=device,
+                                            n_samples=20_000)
+    rvq_cb = RVQCodebookAdapter([RVQStage(e8p, e8p_scale), RVQStage(second, second_scale)])
+    rvq_scale = fit_stage_scale(rvq_cb, seed=seed + 2, device=device, n_samples=20_000)
+    return rvq_cb, rvq_scale
+
+
+def codebook_for(bits: str, stage_scales=None, seed: int = 0, device=None):
     """The codebook a `bits` checkpoint decodes with (checkpoint.py:60-77 builds the
-    same objects): 2-bit: E8P; 3-bit: RVQ [E8P, E8-1bit]; 4-bit: RVQ [E8P, E8P], with
-    the two RVQ stage scales given (they are fitted offline)."""
+    same objects): 2-bit: E8P; 3-bit: RVQ [E8P, E8-1bit]; 4-bit: RVQ [E8P, E8P].
+    The two RVQ stage scales are `stage_scales` when given, else rebuilt from the
+    manifest's `seed` by `build_codebook`'s sweeps."""
     from .codebooks import E8PCodebook, E8OneBitCodebook
     from .rvq import RVQStage
     if bits == "2bit":
         return E8PCodebook()
     if bits not in ("3bit", "4bit"):
         raise ValueError(f"unknown bits {bits!r}")
-    if stage_scales is None or len(stage_scales) != 2:
-        raise ValueError(f"a {bits} codebook needs its two RVQ stage scales: pass codebook= (e.g. the "
-                         "quantizer's) or save the checkpoint with stage_scales")
+    if stage_scales is None:
+        return build_codebook(bits, device, seed)[0]
+    if len(stage_scales) != 2:
+        raise ValueError(f"a {bits} codebook has two RVQ stage scales, got {len(stage_scales)}")
     second = E8OneBitCodebook() if bits == "3bit" else E8PCodebook()
     return RVQCodebookAdapter([RVQStage(E8PCodebook(), float(stage_scales[0])),
                                RVQStage(second, float(stage_scales[1]))])
@@ -268,8 +292,9 @@ def load_quantized_checkpoint(save_path, device="cuda", gpu_devices=None, gpu_bu
     Placement: everything on `device` (or gpu_devices[0]) when it fits; a checkpoint
     above `gpu_budget_bytes` is split over `gpu_devices` (and the host, with
     `cpu_budget_bytes`) by decoder layer, see place_decoder_layers.
-    Codebook: `codebook` if given, else built from the manifest's bits (and its
-    stage_scales for RVQ, see codebook_for).  prepack: modules placed on a GPU re-lay
+    Codebook: `codebook` if given, else built from the manifest's bits (RVQ: its
+    stage_scales when present, else the seeded sweeps of build_codebook, run on the
+    first CUDA device the model uses; see codebook_for).  prepack: modules placed on a GPU re-lay
     their codes into the kernels' weight stream (stage 2 of a 3-bit layer at one byte
     per code) now rather than at their first forward."""
     save_path = Path(save_path)
@@ -295,7 +320,11 @@ def load_quantized_checkpoint(save_path, device="cuda", gpu_devices=None, gpu_bu
         budgets = [gpu_budget_bytes] * len(gpu_devices) + ([cpu_budget_bytes] if cpu_budget_bytes else [])
         place_decoder_layers(model, state, devices, budgets)
 
-    shared = codebook if codebook is not None else codebook_for(manifest["bits"], manifest.get("stage_scales"))
+    if codebook is None:
+        cuda = [d for d in ([device] + list(gpu_devices or [])) if torch.device(d).type == "cuda"]
+        codebook = codebook_for(manifest["bits"], manifest.get("stage_scales"), manifest.get("seed", 0),
+                                cuda[0] if cuda else None)
+    shared = codebook
     for info in manifest["quantized_modules"]:
         # the kernels carry their own tables: one codebook object serves every device
         q = model.get_submodule(info["name"])

@@ -236,6 +236,36 @@ QS_API int qs_linear_output(float *y1, int64_t ld_y1, int64_t shards, int64_t ba
                               bias, y, y_dtype, (cudaStream_t)stream);
 }
 
+QS_API int64_t qs_fit_workspace_bytes(int64_t samples, int ncand) {
+  if (samples < 1 || ncand < 1 || ncand > kFitMaxCandidates) return -1;
+  return fit_workspace_bytes(samples, ncand);
+}
+
+QS_API int qs_fit_scale_sweep(const float *x, int64_t samples, int prev_stages, const int *prev_kinds,
+                              const float *prev_scales, int rvq, int stages, const int *kinds,
+                              const float *stage_scales, const float *candidates, int ncand, void *workspace,
+                              int64_t workspace_bytes, double *mse, int *best, qs_stream_t stream) {
+  if (!x || !candidates || !mse || !best || !workspace || !kinds) return fail(QS_ERR_INVALID_ARG, "null pointer");
+  if (samples < 1 || samples > (int64_t(1) << 31) / 8) return fail(QS_ERR_INVALID_ARG, "bad sample count");
+  if (ncand < 1 || ncand > kFitMaxCandidates) return fail(QS_ERR_INVALID_ARG, "1..%d candidates", kFitMaxCandidates);
+  if (prev_stages < 0 || prev_stages > kFitMaxStages || (prev_stages && (!prev_kinds || !prev_scales)))
+    return fail(QS_ERR_INVALID_ARG, "bad previous stages");
+  if (rvq != 0 && rvq != 1) return fail(QS_ERR_INVALID_ARG, "rvq must be 0 or 1");
+  if (stages < 1 || stages > (rvq ? kFitMaxStages : 1) || (rvq && !stage_scales))
+    return fail(QS_ERR_INVALID_ARG, "bad swept stages");
+  int st = check_kinds(stages, kinds);
+  if (st) return st;
+  if (prev_stages && (st = check_kinds(prev_stages, prev_kinds))) return st;
+  for (int i = 0; i < prev_stages; ++i)
+    if (!(prev_scales[i] != 0.f)) return fail(QS_ERR_INVALID_ARG, "zero previous-stage scale");
+  for (int c = 0; c < ncand; ++c)
+    if (!(candidates[c] != 0.f)) return fail(QS_ERR_INVALID_ARG, "zero candidate scale");
+  if (workspace_bytes < fit_workspace_bytes(samples, ncand)) return fail(QS_ERR_WORKSPACE, "workspace too small");
+  if (!aligned(workspace, 8)) return fail(QS_ERR_ALIGNMENT, "workspace must be 8-byte aligned");
+  return launch_fit_sweep(x, samples, prev_stages, prev_kinds, prev_scales, rvq, stages, kinds, stage_scales,
+                          candidates, ncand, workspace, mse, best, (cudaStream_t)stream);
+}
+
 QS_API int qs_ipc_export(const void *ptr, void *handle, int64_t *offset) {
   if (!ptr || !handle || !offset) return fail(QS_ERR_INVALID_ARG, "null pointer");
   return ipc_export(ptr, handle, offset);

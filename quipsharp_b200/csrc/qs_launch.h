@@ -45,6 +45,14 @@ int launch_two_pass_input(const void *x, int dtype, int64_t batch, int64_t n, co
 int launch_two_pass_output(float *y1, int64_t batch, int64_t m, const float2 *phase, const float *bias, float scale,
                            void *y, int dtype, cudaStream_t s);
 
+// qs_fit.cu: stage-scale sweeps of RVQ codebook construction
+constexpr int kFitMaxStages = 2;
+constexpr int kFitMaxCandidates = 128;
+int64_t fit_workspace_bytes(int64_t samples, int ncand);
+int launch_fit_sweep(const float *x, int64_t samples, int nprev, const int *prev_kinds, const float *prev_scales,
+                     int rvq, int nst, const int *kinds, const float *stage_scales, const float *candidates,
+                     int ncand, void *workspace, double *mse, int *best, cudaStream_t s);
+
 // qs_tp.cu: column-sharded tensor parallelism over peer memory
 int ipc_export(const void *ptr, void *handle, int64_t *offset);
 int ipc_import(const void *handle, int64_t offset, void **ptr);
