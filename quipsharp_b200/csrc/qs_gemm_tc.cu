@@ -695,7 +695,7 @@ int device_status(cudaStream_t s) {
   if (flag) {
     QS_CUDA_TRY(cudaMemcpyToSymbolAsync(g_tc_error, &zero, sizeof(int), 0, cudaMemcpyHostToDevice, s));
     QS_CUDA_TRY(cudaStreamSynchronize(s));
-    return fail(QS_ERR_TIMEOUT, "a bounded wait ran out (prefill matmul pipeline or tensor-parallel shard arrival); "
+    return fail(QS_ERR_TIMEOUT, "a bounded wait timed out (prefill matmul pipeline or tensor-parallel shard arrival); "
                 "the results of that launch are invalid");
   }
   return QS_OK;

@@ -45,6 +45,15 @@ int launch_two_pass_input(const void *x, int dtype, int64_t batch, int64_t n, co
 int launch_two_pass_output(float *y1, int64_t batch, int64_t m, const float2 *phase, const float *bias, float scale,
                            void *y, int dtype, cudaStream_t s);
 
+// qs_xsmall.cu: decode-batch FWHT row kernels of the linear input / output steps
+constexpr int64_t kSmallRhtMaxRows = 32;
+bool small_rht_ok(int64_t n, int64_t rows);
+int launch_small_input_rht(const void *x, int dtype, int64_t rows, int64_t n, const float *sv, float scale,
+                           __half *x2h, float *rowscale, int n_pad, float *y1, int64_t m_local, cudaStream_t s);
+int launch_small_output_rht(const float *y1, int64_t ld_y1, int64_t shards, int64_t batch, int64_t m,
+                            const float *su, const float *bias, float scale, void *y, int y_dtype,
+                            const XPeerGather *pg, cudaStream_t s);
+
 // qs_fit.cu: stage-scale sweeps of RVQ codebook construction
 constexpr int kFitMaxStages = 2;
 constexpr int kFitMaxCandidates = 128;

@@ -301,6 +301,8 @@ int launch_linear_input(const void *x, int x_dtype, int64_t batch, int64_t n, in
   L.warm = 1;
   int st;
   if (transform == QS_RHT) {
+    if (small_rht_ok(n, batch))  // decode batches: one-barrier row kernel
+      return launch_small_input_rht(x, x_dtype, batch, n, sv, inv_sqrt_f32(n), x2h, rowscale, np, y1, m_local, s);
     if ((st = make_fwht_plan(n, batch, p, L))) return st;
     const float sc = inv_sqrt_f32(n);
     return p.C > 1 ? run_xinput_rht<true>(L, s, x, x_dtype, p, sv, sc, x2h, rowscale, np, y1, m_local)
@@ -331,6 +333,9 @@ int launch_linear_output(float *y1, int64_t ld_y1, int64_t shards, int64_t batch
   XLaunch L;
   int st;
   if (transform == QS_RHT) {
+    const int64_t mp = m / shards;
+    if (small_rht_ok(m, batch) && (shards == 1 || (mp & (mp - 1)) == 0))  // decode batches
+      return launch_small_output_rht(y1, ld_y1, shards, batch, m, su, bias, inv_sqrt_f32(m), y, y_dtype, pg, s);
     if ((st = make_fwht_plan(m, batch, p, L))) return st;
     if (pg) L.pg = *pg;
     const float sc = inv_sqrt_f32(m);

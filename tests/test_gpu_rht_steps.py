@@ -1,0 +1,71 @@
+"""The RHT input and output steps of the fused forward at every power-of-two
+width from 2^10 to 2^14 and decode batches (1 to 32 rows: the one-CTA row
+kernels) plus a batch above them (the general row engine), through the split
+C ABI, against the oracle (quipsharp/incoherence.py:86-93):
+  input:  x2 = fwht(x * sv) / sqrt(n), stored as fp16 times a power-of-two row
+          scale, with y1 zeroed;
+  output: y = fwht(y1) / sqrt(m) * su + bias, cast; also from the rank-major
+          layout of P gathered shards."""
+import numpy as np
+import pytest
+import torch
+
+from oracle import quipsharp_oracle as O
+from quipsharp_b200 import _native as N
+from conftest import rel_l2
+
+pytestmark = pytest.mark.gpu
+DEV = "cuda"
+
+
+def _signs(n, seed):
+    g = torch.Generator().manual_seed(seed)
+    return (torch.randint(0, 2, (n,), generator=g) * 2 - 1).float()
+
+
+@pytest.mark.parametrize("lg", [10, 11, 12, 13, 14])
+@pytest.mark.parametrize("B,dt", [(1, torch.bfloat16), (5, torch.float16), (32, torch.float32), (40, torch.float16)])
+def test_rht_input_step(lg, B, dt):
+    n, m_local = 1 << lg, 300
+    g = torch.Generator().manual_seed(lg * 100 + B)
+    x = torch.randn(B, n, generator=g).to(dt)
+    sv = _signs(n, lg)
+    nb = N.lib().qs_linear_input_bytes(B, n)
+    ws = torch.empty(nb, dtype=torch.uint8, device=DEV)
+    y1 = torch.full((B, m_local), 7.0, device=DEV)
+    xd, svd = x.to(DEV), sv.to(DEV)
+    N.check(N.lib().qs_linear_input(N.ptr(xd), N.IO_DTYPES[dt], B, n, N.QS_RHT, N.ptr(svd), None, N.ptr(ws), nb,
+                                    N.ptr(y1), m_local, N.stream_of(xd)))
+    torch.cuda.synchronize()
+    n_pad = n  # powers of two >= 256 need no padding
+    x2h = ws[: B * n_pad * 2].view(torch.float16).reshape(B, n_pad).float().cpu().numpy()
+    off = (B * n_pad * 2 + 255) // 256 * 256
+    inv = ws[off: off + 4 * B].view(torch.float32).cpu().numpy()
+    got = x2h[:, :n] * inv[:, None]
+    ref = O.rht_transform_input(x.float().numpy(), sv.numpy())
+    assert rel_l2(got, ref) < 1e-3
+    # the operand fills the fp16 range: max |x2h| in [2^11, 2^12)
+    mx = np.abs(x2h).max(axis=1)
+    assert np.all((mx >= 2048) & (mx < 4096))
+    assert torch.count_nonzero(y1).item() == 0
+
+
+@pytest.mark.parametrize("lg", [10, 11, 12, 13, 14])
+@pytest.mark.parametrize("B,dt,P", [(1, torch.bfloat16, 1), (3, torch.float32, 1), (32, torch.float16, 1),
+                                    (40, torch.float32, 1), (1, torch.float32, 2), (2, torch.float32, 8)])
+def test_rht_output_step(lg, B, dt, P):
+    m = 1 << lg
+    g = torch.Generator().manual_seed(lg * 10 + B + P)
+    y1 = torch.randn(B, m, generator=g) * 30
+    su = _signs(m, lg + 1)
+    bias = torch.randn(m, generator=g)
+    mp = m // P
+    buf = y1.reshape(B, P, mp).permute(1, 0, 2).contiguous().reshape(-1) if P > 1 else y1.reshape(-1)
+    bd, sud, biasd = buf.to(DEV), su.to(DEV), bias.to(DEV)
+    y = torch.empty(B, m, dtype=dt, device=DEV)
+    N.check(N.lib().qs_linear_output(N.ptr(bd), m, P, B, m, N.QS_RHT, N.ptr(sud), None, N.ptr(biasd), N.ptr(y),
+                                     N.IO_DTYPES[dt], N.stream_of(y)))
+    torch.cuda.synchronize()
+    ref = O.rht_transform_output(y1.numpy(), su.numpy()) + bias.numpy()
+    tol = {torch.float32: 1e-5, torch.float16: 1e-3, torch.bfloat16: 8e-3}[dt]
+    assert rel_l2(y.float().cpu().numpy(), ref) < tol
