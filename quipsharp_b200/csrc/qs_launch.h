@@ -53,6 +53,12 @@ int launch_small_input_rht(const void *x, int dtype, int64_t rows, int64_t n, co
 int launch_small_output_rht(const float *y1, int64_t ld_y1, int64_t shards, int64_t batch, int64_t m,
                             const float *su, const float *bias, float scale, void *y, int y_dtype,
                             const XPeerGather *pg, cudaStream_t s);
+bool small_rfft_ok(int64_t n_complex, int64_t rows);
+int launch_small_input_rfft(const void *x, int dtype, int64_t rows, int64_t n, const float2 *phase, float scale,
+                            __half *x2h, float *rowscale, int n_pad, float *y1, int64_t m_local, cudaStream_t s);
+int launch_small_output_rfft(const float *y1, int64_t ld_y1, int64_t shards, int64_t batch, int64_t m,
+                             const float2 *phase, const float *bias, float scale, void *y, int y_dtype,
+                             const XPeerGather *pg, cudaStream_t s);
 
 // qs_fit.cu: stage-scale sweeps of RVQ codebook construction
 constexpr int kFitMaxStages = 2;

@@ -283,6 +283,12 @@ int launch_rfft(int inverse, const void *x, int64_t ld_x, void *y, int64_t ld_y,
 // and keeps every row inside fp16 range whatever the activation magnitudes.
 static int64_t n_padded(int64_t n) { return padded_T(n) * 8; }
 
+// Pointer aligned for loads / stores of element pairs of `dtype` (null passes).
+static bool pair_aligned(const void *p, int dtype) {
+  const uintptr_t a = dtype == QS_F32 ? 8 : 4;
+  return (reinterpret_cast<uintptr_t>(p) % a) == 0;
+}
+
 // Layout: [x2h][rowscale][two-pass scratch (float32 rows + L1 partial sums),
 // only for batches and sizes that use the two-pass RFFT].
 int64_t linear_input_bytes(int64_t batch, int64_t n) {
@@ -310,6 +316,8 @@ int launch_linear_input(const void *x, int x_dtype, int64_t batch, int64_t n, in
   }
   const float2 *ph = static_cast<const float2 *>(phase_v);
   const float sc = inv_sqrt_f32(n / 2);
+  if (small_rfft_ok(n / 2, batch) && pair_aligned(x, x_dtype))  // decode batches: one-barrier row kernel
+    return launch_small_input_rfft(x, x_dtype, batch, n, ph, sc, x2h, rowscale, np, y1, m_local, s);
   if (two_pass_rfft(n / 2, batch, nullptr, nullptr) && (!y1 || few_rows(batch))) {
     void *scratch = static_cast<char *>(x2ws) + round_up(batch * n_pad * 2, 256) + round_up(batch * 4, 256);
     return launch_two_pass_input(x, x_dtype, batch, n, ph, sc, x2h, rowscale, np, scratch, y1, m_local, s);
@@ -345,6 +353,10 @@ int launch_linear_output(float *y1, int64_t ld_y1, int64_t shards, int64_t batch
   if (ld_y1 % 2) return fail(QS_ERR_ALIGNMENT, "RFFT y1 row stride must be even");
   const float2 *ph = static_cast<const float2 *>(phase_u);
   const float sc = inv_sqrt_f32(m / 2);
+  const int64_t mp = m / shards;
+  if (small_rfft_ok(m / 2, batch) && (shards == 1 || (mp >= 2 && (mp & (mp - 1)) == 0)) &&
+      (pg || pair_aligned(y1, QS_F32)) && pair_aligned(bias, QS_F32) && pair_aligned(y, y_dtype))
+    return launch_small_output_rfft(y1, ld_y1, shards, batch, m, ph, bias, sc, y, y_dtype, pg, s);
   // the two-pass store loop reads phase / bias and writes y two complex values at a time
   const bool aligned16 = (reinterpret_cast<uintptr_t>(ph) & 15) == 0 && (reinterpret_cast<uintptr_t>(bias) & 15) == 0 &&
                          (reinterpret_cast<uintptr_t>(y) & 15) == 0;

@@ -227,7 +227,320 @@ int log2_exact(int64_t n) {
   return (int64_t(1) << lg) == n ? lg : -1;
 }
 
+// ---- decode-batch FFT rows (RFFT layers, quipsharp/rfft.py:37-60) -----------
+// N = 2^(5 + LV + LW) complex points, one CTA of T = 32 * 2^LW threads per row,
+// V = 2^LV points per thread.  Three-factor Cooley-Tukey with the input index
+// i = t + T r (t the thread, register digit r slowest) and the output index
+// k = k_r + V (k_w + W k_l):
+//   1. V-point DFT over r in registers, then twiddle w_N^{t k_r};
+//   2. shared-memory transpose: thread (w', lane) takes k_r = w' + W j and all w;
+//   3. W-point DFT over w in registers, then twiddle w_N^{V lane k_w};
+//   4. 32-point DFT over the lanes by warp shuffles (radix-2 decimation in
+//      frequency: lane l ends with k_l = bitreverse5(l));
+//   5. the results are staged in shared memory by k (padded one slot per V W
+//      points, so a warp's stores hit distinct bank pairs) and leave in natural
+//      order: thread t handles k = t + T i, so global loads of the layer's
+//      phases / bias and stores of the result are coalesced.
+// The in-register DFTs are radix-2 decimation in frequency (natural input,
+// bit-reversed output positions) with w_32^e constants from the constant bank.
+// Twiddles of steps 1, 3 and 4 come from a table of w_8192^e rounded from
+// double and are loaded before the dependent-launch wait, with the layer's
+// phases; the inverse transform uses conjugates.
+
+#include "qs_twiddle_gen.inc"  // kTwiddle8192, kTw32
+
+constexpr int kTwLog = 13;
+
+__device__ __forceinline__ float2 cadd(float2 a, float2 b) { return make_float2(a.x + b.x, a.y + b.y); }
+__device__ __forceinline__ float2 csub(float2 a, float2 b) { return make_float2(a.x - b.x, a.y - b.y); }
+__device__ __forceinline__ float2 cmul(float2 a, float2 b) {
+  return make_float2(fmaf(a.x, b.x, -a.y * b.y), fmaf(a.x, b.y, a.y * b.x));
+}
+template <bool INV>
+__device__ __forceinline__ float2 cj(float2 t) { return INV ? make_float2(t.x, -t.y) : t; }
+
+template <bool INV>
+__device__ __forceinline__ float2 twiddle(int e, int lgN) {  // w_N^e, e in [0, N)
+  return cj<INV>(__ldg(&kTwiddle8192[e << (kTwLog - lgN)]));
+}
+
+__host__ __device__ constexpr int bitrev(int x, int bits) {
+  int r = 0;
+  for (int b = 0; b < bits; ++b) r |= ((x >> b) & 1) << (bits - 1 - b);
+  return r;
+}
+
+// In-register DFT of R <= 32 points (radix-2 DIF): v[p] ends holding k = bitrev(p).
+template <int R, bool INV>
+__device__ __forceinline__ void dft_regs(float2 (&v)[R]) {
+#pragma unroll
+  for (int h = R / 2; h >= 1; h >>= 1)
+#pragma unroll
+    for (int j = 0; j < R; ++j)
+      if (!(j & h)) {
+        const float2 a = v[j], b = v[j + h];
+        v[j] = cadd(a, b);
+        const int e = (j & (h - 1)) * (16 / h);  // w_{2h}^(j mod h) = w_32^e
+        v[j + h] = e ? cmul(csub(a, b), cj<INV>(kTw32[e])) : csub(a, b);
+      }
+}
+
+template <int LV, int LW, bool INV>
+struct FftRow {
+  static constexpr int V = 1 << LV, W = 1 << LW, T = 32 * W, N = T * V, LN = 5 + LV + LW;
+  static constexpr int kStage = N + N / (V * W);  // staging slots (padded)
+  float2 t1[V];  // w_N^{t k_r}, by register position p (k_r = bitrev(p))
+  float2 t3[W];  // w_N^{V lane k_w}, by position q (k_w = bitrev(q))
+  float2 tl[5];  // lane stages: w_{2m}^{lane mod m}, m = 16, 8, 4, 2, 1
+
+  __device__ __forceinline__ void prefetch_twiddles() {
+    const int lane = threadIdx.x & 31, t = threadIdx.x;
+#pragma unroll
+    for (int p = 0; p < V; ++p) t1[p] = twiddle<INV>((t * bitrev(p, LV)) & (N - 1), LN);
+#pragma unroll
+    for (int q = 0; q < W; ++q) t3[q] = twiddle<INV>((V * lane * bitrev(q, LW)) & (N - 1), LN);
+#pragma unroll
+    for (int s = 0; s < 5; ++s) {
+      const int m = 16 >> s;
+      tl[s] = twiddle<INV>((lane & (m - 1)) * (N / (2 * m)), LN);
+    }
+  }
+
+  __device__ __forceinline__ static int slot(int k) { return k + (k >> (LV + LW)); }
+
+  // v: v[r] = input point t + T r.  Leaves output k at stage[slot(k)] (call
+  // __syncthreads before reading it); sm and stage are distinct buffers.
+  __device__ __forceinline__ void run(float2 (&v)[V], float2 *sm, float2 *stage) const {
+    const int lane = threadIdx.x & 31, w = threadIdx.x >> 5;
+    dft_regs<V, INV>(v);
+#pragma unroll
+    for (int p = 1; p < V; ++p) v[p] = cmul(v[p], t1[p]);
+#pragma unroll
+    for (int p = 0; p < V; ++p) sm[lane + 32 * (w + W * bitrev(p, LV))] = v[p];
+    __syncthreads();
+#pragma unroll
+    for (int j = 0; j < V / W; ++j) {
+      float2 u[W];
+#pragma unroll
+      for (int ww = 0; ww < W; ++ww) u[ww] = sm[lane + 32 * (ww + W * (w + W * j))];
+      dft_regs<W, INV>(u);
+#pragma unroll
+      for (int q = 0; q < W; ++q) v[j * W + q] = q ? cmul(u[q], t3[q]) : u[q];
+    }
+#pragma unroll
+    for (int s = 0; s < 5; ++s) {
+      const int m = 16 >> s;
+      const bool hi = lane & m;
+#pragma unroll
+      for (int i = 0; i < V; ++i) {
+        const float2 pv = make_float2(__shfl_xor_sync(0xffffffffu, v[i].x, m), __shfl_xor_sync(0xffffffffu, v[i].y, m));
+        v[i] = hi ? cmul(csub(pv, v[i]), tl[s]) : cadd(v[i], pv);
+      }
+    }
+    const int kl = V * W * bitrev(lane, 5);
+#pragma unroll
+    for (int j = 0; j < V / W; ++j)
+#pragma unroll
+      for (int q = 0; q < W; ++q) stage[slot((w + W * j) + V * bitrev(q, LW) + kl)] = v[j * W + q];
+  }
+};
+
+__device__ __forceinline__ float2 load_pair(const void *p, int64_t i, int dtype) {  // elements i, i + 1
+  if (dtype == QS_F16) return __half22float2(*reinterpret_cast<const __half2 *>(static_cast<const __half *>(p) + i));
+  if (dtype == QS_BF16)
+    return __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162 *>(static_cast<const __nv_bfloat16 *>(p) + i));
+  return *reinterpret_cast<const float2 *>(static_cast<const float *>(p) + i);
+}
+
+__device__ __forceinline__ void store_pair(void *p, int64_t i, int dtype, float2 v) {
+  if (dtype == QS_F16) *reinterpret_cast<__half2 *>(static_cast<__half *>(p) + i) = __floats2half2_rn(v.x, v.y);
+  else if (dtype == QS_BF16)
+    *reinterpret_cast<__nv_bfloat162 *>(static_cast<__nv_bfloat16 *>(p) + i) = __floats2bfloat162_rn(v.x, v.y);
+  else *reinterpret_cast<float2 *>(static_cast<float *>(p) + i) = v;
+}
+
+struct SmallInF {
+  const void *x;
+  int dtype;
+  const float2 *phase;  // phase_v (N)
+  float scale;          // 1 / sqrt(N)
+  __half *x2h;
+  float *rowscale;
+  int n_pad;
+  float *y1;
+  int64_t m_local;
+};
+
+template <int LV, int LW>
+__global__ void __launch_bounds__(32 << LW) xsmall_input_rfft_kernel(SmallInF a) {
+  using F = FftRow<LV, LW, false>;
+  constexpr int V = F::V, W = F::W, T = F::T, N = F::N;
+  extern __shared__ float2 smf_small[];
+  float2 *const stage = smf_small + N;
+  __shared__ float red[W];
+  pdl_launch_dependents();
+  const int64_t row = blockIdx.x;
+  const int t = threadIdx.x;
+  F f;
+  f.prefetch_twiddles();
+  float2 ph[V];
+#pragma unroll
+  for (int r = 0; r < V; ++r) ph[r] = __ldg(a.phase + t + T * r);  // layer constant
+  pdl_wait();  // x may be the previous kernel's output; y1 may still be read by it
+  if (a.y1) xzero_row(a.y1, row, a.m_local, 0, a.m_local);
+  float2 v[V];
+#pragma unroll
+  for (int r = 0; r < V; ++r) v[r] = cmul(load_pair(a.x, row * (2 * N) + 2 * (t + T * r), a.dtype), ph[r]);
+  f.run(v, smf_small, stage);
+  float amax = 0.f;
+#pragma unroll
+  for (int i = 0; i < V; ++i) amax = fmaxf(amax, fmaxf(fabsf(v[i].x), fabsf(v[i].y)));
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, o));
+  if ((t & 31) == 0) red[t >> 5] = amax;
+  __syncthreads();  // the row maximum and the staged results
+#pragma unroll
+  for (int k = 0; k < W; ++k) amax = fmaxf(amax, red[k]);
+  float sc, inv;
+  xpow2_scale(amax * a.scale, sc, inv);
+  sc *= a.scale;
+  __half2 *out = reinterpret_cast<__half2 *>(a.x2h + row * a.n_pad);
+#pragma unroll
+  for (int i = 0; i < V; ++i) {
+    const int k = t + T * i;
+    const float2 z = stage[F::slot(k)];
+    out[k] = __floats2half2_rn(z.x * sc, z.y * sc);
+  }
+  if (t == 0) a.rowscale[row] = inv;
+}
+
+struct SmallOutF {
+  const float *y1;
+  int64_t ld_y1;
+  int64_t batch;
+  int shard_log2;       // shards > 1: log2(m / shards); else -1
+  const float2 *phase;  // phase_u (N)
+  const float *bias;
+  float scale;          // 1 / sqrt(N)
+  void *y;
+  int dtype;
+  int *busy;
+  XPeerGather pg;
+};
+
+template <int LV, int LW>
+__global__ void __launch_bounds__(32 << LW) xsmall_output_rfft_kernel(SmallOutF a) {
+  using F = FftRow<LV, LW, true>;
+  constexpr int V = F::V, T = F::T, N = F::N;
+  extern __shared__ float2 smf_small[];
+  float2 *const stage = smf_small + N;
+  const int64_t row = blockIdx.x;
+  const int t = threadIdx.x;
+  const bool flag = row == 0 && t == 0;
+  if (flag) xbusy_set(a.busy, 1);  // before the release: the next input step reads it at its start
+  pdl_launch_dependents();
+  F f;
+  f.prefetch_twiddles();
+  constexpr bool kBiasEarly = V <= 16;  // registers: 32 points per thread leave no room for the bias
+  const float2 *bias2 = reinterpret_cast<const float2 *>(a.bias);
+  float2 ph[V], bb[kBiasEarly ? V : 1];
+#pragma unroll
+  for (int i = 0; i < V; ++i) {  // layer constants of the outputs k = t + T i
+    const float2 p = __ldg(a.phase + t + T * i);
+    ph[i] = make_float2(p.x * a.scale, -p.y * a.scale);  // scale * conj(phase)
+    if constexpr (kBiasEarly) bb[i] = bias2 ? __ldg(bias2 + t + T * i) : make_float2(0.f, 0.f);
+  }
+  pdl_wait();  // y1 comes from the matmul (or the ranks' pushes)
+  const float *src = a.pg.flags ? xwait_peers(a.pg) : a.y1;
+  float2 v[V];
+#pragma unroll
+  for (int r = 0; r < V; ++r) {
+    const int c = 2 * (t + T * r);  // real index of the complex point's first half
+    int64_t off;
+    if (a.shard_log2 < 0) off = row * a.ld_y1 + c;
+    else off = ((static_cast<int64_t>(c >> a.shard_log2) * a.batch + row) << a.shard_log2) + (c & ((1 << a.shard_log2) - 1));
+    v[r] = src ? *reinterpret_cast<const float2 *>(src + off) : make_float2(0.f, 0.f);
+  }
+  f.run(v, smf_small, stage);
+  __syncthreads();
+#pragma unroll
+  for (int i = 0; i < V; ++i) {
+    const int k = t + T * i;
+    const float2 z = cmul(stage[F::slot(k)], ph[i]);
+    float2 b2;
+    if constexpr (kBiasEarly) b2 = bb[i];
+    else b2 = bias2 ? __ldg(bias2 + k) : make_float2(0.f, 0.f);
+    store_pair(a.y, row * (2 * N) + 2 * k, a.dtype, make_float2(z.x + b2.x, z.y + b2.y));
+  }
+  if (flag) xbusy_set(a.busy, 0);
+}
+
+template <int LV, int LW>
+struct RunInF {
+  static int run(const SmallInF &a, int64_t rows, cudaStream_t s) {
+    constexpr int bytes = 8 * ((32 << (LV + LW)) + FftRow<LV, LW, false>::kStage);
+    auto k = xsmall_input_rfft_kernel<LV, LW>;
+    QS_CUDA_TRY(cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, bytes));
+    return launch_pdl("xsmall_input_rfft", k, dim3(static_cast<unsigned>(rows)), dim3(32 << LW), bytes, s, a);
+  }
+};
+
+template <int LV, int LW>
+struct RunOutF {
+  static int run(const SmallOutF &a, int64_t rows, cudaStream_t s) {
+    constexpr int bytes = 8 * ((32 << (LV + LW)) + FftRow<LV, LW, true>::kStage);
+    auto k = xsmall_output_rfft_kernel<LV, LW>;
+    QS_CUDA_TRY(cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, bytes));
+    return launch_pdl("xsmall_output_rfft", k, dim3(static_cast<unsigned>(rows)), dim3(32 << LW), bytes, s, a);
+  }
+};
+
+// (LV, LW) per log2(N) of the complex length: 2^10 .. 2^13.
+template <template <int, int> class F, typename... Args>
+int dispatch_small_fft(int lg, Args &&...args) {
+  switch (lg) {
+    case 10: return F<3, 2>::run(args...);
+    case 11: return F<3, 3>::run(args...);
+    case 12: return F<4, 3>::run(args...);
+    case 13: return F<5, 3>::run(args...);
+    default: return fail(QS_ERR_UNSUPPORTED, "no decode-batch FFT for 2^%d points", lg);
+  }
+}
+
 }  // namespace
+
+bool small_rfft_ok(int64_t n_complex, int64_t rows) {
+  const int lg = log2_exact(n_complex);
+  return lg >= 10 && lg <= 13 && rows >= 1 && rows <= kSmallRhtMaxRows;
+}
+
+int launch_small_input_rfft(const void *x, int dtype, int64_t rows, int64_t n, const float2 *phase, float scale,
+                            __half *x2h, float *rowscale, int n_pad, float *y1, int64_t m_local, cudaStream_t s) {
+  SmallInF a{x, dtype, phase, scale, x2h, rowscale, n_pad, y1, m_local};
+  return dispatch_small_fft<RunInF>(log2_exact(n / 2), a, rows, s);
+}
+
+int launch_small_output_rfft(const float *y1, int64_t ld_y1, int64_t shards, int64_t batch, int64_t m,
+                             const float2 *phase, const float *bias, float scale, void *y, int y_dtype,
+                             const XPeerGather *pg, cudaStream_t s) {
+  SmallOutF a{};
+  a.y1 = y1;
+  a.ld_y1 = ld_y1;
+  a.batch = batch;
+  a.shard_log2 = -1;
+  if (shards > 1) {
+    a.shard_log2 = log2_exact(m / shards);
+    if (a.shard_log2 < 1) return fail(QS_ERR_UNSUPPORTED, "shard width is not an even power of two");
+  }
+  a.phase = phase;
+  a.bias = bias;
+  a.scale = scale;
+  a.y = y;
+  a.dtype = y_dtype;
+  a.busy = xbusy_flag();
+  if (pg) a.pg = *pg;
+  return dispatch_small_fft<RunOutF>(log2_exact(m / 2), a, batch, s);
+}
 
 bool small_rht_ok(int64_t n, int64_t rows) {
   const int lg = log2_exact(n);
