@@ -85,6 +85,44 @@ __device__ __forceinline__ int point_a(int r) {
   return (threadIdx.x & 31) + 32 * (r + V * (threadIdx.x >> 5));
 }
 
+// Zeroing of the y1 row the matmul accumulates into.  Plain stores from the
+// row's CTA competed with its loads (a 28672-float row cost more than the
+// transform); instead one thread hands the row to the bulk-copy engine as
+// asynchronous copies of a zeroed shared-memory block (no multicast; 16-byte
+// aligned, sizes in multiples of 16 bytes) and waits for them at the end.
+constexpr int kZeroBlockBytes = 4096;
+
+struct BulkZero {
+  bool pending = false;
+
+  // Call with all threads after the dependent-launch wait; zblk: kZeroBlockBytes of
+  // shared memory this CTA does not otherwise use.
+  __device__ __forceinline__ void start(float *row, int64_t floats, float4 *zblk) {
+    const bool bulk = (reinterpret_cast<uintptr_t>(row) & 15) == 0 && (floats & 3) == 0;
+    if (!bulk) {
+      for (int64_t i = threadIdx.x; i < floats; i += blockDim.x) row[i] = 0.f;
+      return;
+    }
+    for (int i = threadIdx.x; i < kZeroBlockBytes / 16; i += blockDim.x) zblk[i] = make_float4(0.f, 0.f, 0.f, 0.f);
+    asm volatile("fence.proxy.async.shared::cta;" ::: "memory");  // the zeros, to the bulk-copy engine
+    __syncthreads();
+    if (threadIdx.x == 0) {
+      const uint32_t src = static_cast<uint32_t>(__cvta_generic_to_shared(zblk));
+      char *dst = reinterpret_cast<char *>(row);
+      for (int64_t off = 0, bytes = floats * 4; off < bytes; off += kZeroBlockBytes) {
+        const uint32_t n = static_cast<uint32_t>(bytes - off < kZeroBlockBytes ? bytes - off : kZeroBlockBytes);
+        asm volatile("cp.async.bulk.global.shared::cta.bulk_group [%0], [%1], %2;" ::"l"(dst + off), "r"(src), "r"(n)
+                     : "memory");
+      }
+      asm volatile("cp.async.bulk.commit_group;" ::: "memory");
+      pending = true;
+    }
+  }
+  __device__ __forceinline__ void finish() {
+    if (pending) asm volatile("cp.async.bulk.wait_group 0;" ::: "memory");
+  }
+};
+
 struct SmallIn {
   const void *x;
   int dtype;
@@ -95,6 +133,7 @@ struct SmallIn {
   int n_pad;
   float *y1;
   int64_t m_local;
+  int64_t rows;
 };
 
 template <int LV, int LW>
@@ -102,16 +141,18 @@ __global__ void __launch_bounds__(32 << LW) xsmall_input_rht_kernel(SmallIn a) {
   constexpr int V = 1 << LV, W = 1 << LW, n = 32 * V * W;
   extern __shared__ float sm_small[];
   __shared__ float red[W];
+  __shared__ float4 zblk[kZeroBlockBytes / 16];
   pdl_launch_dependents();
   const int64_t row = blockIdx.x;
   float sg[V];
 #pragma unroll
   for (int r = 0; r < V; ++r) sg[r] = __ldg(a.sv + point_a<LV>(r));  // layer constant
   pdl_wait();  // x may be the previous kernel's output; y1 may still be read by it
-  if (a.y1) xzero_row(a.y1, row, a.m_local, 0, a.m_local);
   float v[V];
 #pragma unroll
   for (int r = 0; r < V; ++r) v[r] = load_as_float(a.x, row * n + point_a<LV>(r), a.dtype) * sg[r];
+  BulkZero bz;
+  if (a.y1) bz.start(a.y1 + row * a.m_local, a.m_local, zblk);
   fwht_row_small<LV, LW>(v, sm_small);
   float amax = 0.f;
 #pragma unroll
@@ -133,6 +174,7 @@ __global__ void __launch_bounds__(32 << LW) xsmall_input_rht_kernel(SmallIn a) {
 #pragma unroll
     for (int k = 0; k < W; ++k) out[point_b<LV, LW>(j, k)] = __float2half_rn(v[j * W + k] * sc);
   if (threadIdx.x == 0) a.rowscale[row] = inv;
+  bz.finish();
 }
 
 struct SmallOut {
@@ -259,9 +301,22 @@ __device__ __forceinline__ float2 cmul(float2 a, float2 b) {
 template <bool INV>
 __device__ __forceinline__ float2 cj(float2 t) { return INV ? make_float2(t.x, -t.y) : t; }
 
+// A read-only load the compiler issues where it stands and keeps in registers
+// (a plain __ldg may be re-issued after the dependent-launch wait instead).
+__device__ __forceinline__ float2 ldg_pinned(const float2 *p) {
+  float2 v;
+  asm volatile("ld.global.nc.v2.f32 {%0, %1}, [%2];" : "=f"(v.x), "=f"(v.y) : "l"(p));
+  return v;
+}
+
 template <bool INV>
 __device__ __forceinline__ float2 twiddle(int e, int lgN) {  // w_N^e, e in [0, N)
   return cj<INV>(__ldg(&kTwiddle8192[e << (kTwLog - lgN)]));
+}
+
+template <bool INV>
+__device__ __forceinline__ float2 twiddle_pinned(int e, int lgN) {
+  return cj<INV>(ldg_pinned(&kTwiddle8192[e << (kTwLog - lgN)]));
 }
 
 __host__ __device__ constexpr int bitrev(int x, int bits) {
@@ -296,13 +351,13 @@ struct FftRow {
   __device__ __forceinline__ void prefetch_twiddles() {
     const int lane = threadIdx.x & 31, t = threadIdx.x;
 #pragma unroll
-    for (int p = 0; p < V; ++p) t1[p] = twiddle<INV>((t * bitrev(p, LV)) & (N - 1), LN);
+    for (int p = 0; p < V; ++p) t1[p] = twiddle_pinned<INV>((t * bitrev(p, LV)) & (N - 1), LN);
 #pragma unroll
-    for (int q = 0; q < W; ++q) t3[q] = twiddle<INV>((V * lane * bitrev(q, LW)) & (N - 1), LN);
+    for (int q = 0; q < W; ++q) t3[q] = twiddle_pinned<INV>((V * lane * bitrev(q, LW)) & (N - 1), LN);
 #pragma unroll
     for (int s = 0; s < 5; ++s) {
       const int m = 16 >> s;
-      tl[s] = twiddle<INV>((lane & (m - 1)) * (N / (2 * m)), LN);
+      tl[s] = twiddle_pinned<INV>((lane & (m - 1)) * (N / (2 * m)), LN);
     }
   }
 
@@ -369,6 +424,7 @@ struct SmallInF {
   int n_pad;
   float *y1;
   int64_t m_local;
+  int64_t rows;
 };
 
 template <int LV, int LW>
@@ -378,6 +434,7 @@ __global__ void __launch_bounds__(32 << LW) xsmall_input_rfft_kernel(SmallInF a)
   extern __shared__ float2 smf_small[];
   float2 *const stage = smf_small + N;
   __shared__ float red[W];
+  __shared__ float4 zblk[kZeroBlockBytes / 16];
   pdl_launch_dependents();
   const int64_t row = blockIdx.x;
   const int t = threadIdx.x;
@@ -385,12 +442,13 @@ __global__ void __launch_bounds__(32 << LW) xsmall_input_rfft_kernel(SmallInF a)
   f.prefetch_twiddles();
   float2 ph[V];
 #pragma unroll
-  for (int r = 0; r < V; ++r) ph[r] = __ldg(a.phase + t + T * r);  // layer constant
+  for (int r = 0; r < V; ++r) ph[r] = ldg_pinned(a.phase + t + T * r);  // layer constant
   pdl_wait();  // x may be the previous kernel's output; y1 may still be read by it
-  if (a.y1) xzero_row(a.y1, row, a.m_local, 0, a.m_local);
   float2 v[V];
 #pragma unroll
   for (int r = 0; r < V; ++r) v[r] = cmul(load_pair(a.x, row * (2 * N) + 2 * (t + T * r), a.dtype), ph[r]);
+  BulkZero bz;
+  if (a.y1) bz.start(a.y1 + row * a.m_local, a.m_local, zblk);
   f.run(v, smf_small, stage);
   float amax = 0.f;
 #pragma unroll
@@ -412,6 +470,7 @@ __global__ void __launch_bounds__(32 << LW) xsmall_input_rfft_kernel(SmallInF a)
     out[k] = __floats2half2_rn(z.x * sc, z.y * sc);
   }
   if (t == 0) a.rowscale[row] = inv;
+  bz.finish();
 }
 
 struct SmallOutF {
@@ -446,9 +505,9 @@ __global__ void __launch_bounds__(32 << LW) xsmall_output_rfft_kernel(SmallOutF 
   float2 ph[V], bb[kBiasEarly ? V : 1];
 #pragma unroll
   for (int i = 0; i < V; ++i) {  // layer constants of the outputs k = t + T i
-    const float2 p = __ldg(a.phase + t + T * i);
+    const float2 p = ldg_pinned(a.phase + t + T * i);
     ph[i] = make_float2(p.x * a.scale, -p.y * a.scale);  // scale * conj(phase)
-    if constexpr (kBiasEarly) bb[i] = bias2 ? __ldg(bias2 + t + T * i) : make_float2(0.f, 0.f);
+    if constexpr (kBiasEarly) bb[i] = bias2 ? ldg_pinned(bias2 + t + T * i) : make_float2(0.f, 0.f);
   }
   pdl_wait();  // y1 comes from the matmul (or the ranks' pushes)
   const float *src = a.pg.flags ? xwait_peers(a.pg) : a.y1;
@@ -516,7 +575,7 @@ bool small_rfft_ok(int64_t n_complex, int64_t rows) {
 
 int launch_small_input_rfft(const void *x, int dtype, int64_t rows, int64_t n, const float2 *phase, float scale,
                             __half *x2h, float *rowscale, int n_pad, float *y1, int64_t m_local, cudaStream_t s) {
-  SmallInF a{x, dtype, phase, scale, x2h, rowscale, n_pad, y1, m_local};
+  SmallInF a{x, dtype, phase, scale, x2h, rowscale, n_pad, y1, m_local, rows};
   return dispatch_small_fft<RunInF>(log2_exact(n / 2), a, rows, s);
 }
 
@@ -549,7 +608,7 @@ bool small_rht_ok(int64_t n, int64_t rows) {
 
 int launch_small_input_rht(const void *x, int dtype, int64_t rows, int64_t n, const float *sv, float scale,
                            __half *x2h, float *rowscale, int n_pad, float *y1, int64_t m_local, cudaStream_t s) {
-  SmallIn a{x, dtype, sv, scale, x2h, rowscale, n_pad, y1, m_local};
+  SmallIn a{x, dtype, sv, scale, x2h, rowscale, n_pad, y1, m_local, rows};
   return dispatch_small<RunIn>(log2_exact(n), a, rows, s);
 }
 
