@@ -554,11 +554,15 @@ def run_ours(args):
     else:
         gb = sum(gemv_bytes(m // world, n, ls.kinds, B) for _, m, n in ls.layers)
         achieved = gb * r["mm_steps"] * passes * ls.L / (r["ms_mm"] / 1e3) / 1e9
-        traffic = load_traffic_table().get((args.config, B, world))
+        table = load_traffic_table()
+        traffic, basis = table.get((args.config, B, world)), "measured at this rank count"
+        if traffic is None and (args.config, B, 1) in table:  # a rank streams its m/N rows
+            full = sum(gemv_bytes(m, n, ls.kinds, B) for _, m, n in ls.layers)
+            traffic, basis = table[(args.config, B, 1)] * gb / full, "one-GPU capture scaled to this rank's rows"
         roofline = {"bound": "hbm", "achieved": achieved, "peak": hbm, "unit": "GB/s", "frac": achieved / hbm,
                     "traffic": traffic,
                     "traffic_basis": "ncu dram__bytes_read.sum + dram__bytes_write.sum summed over one launch of "
-                                     "each layer of the set on one rank (profiles/gemv_dram_traffic.md)",
+                                     f"each layer of the set on one rank, {basis} (profiles/gemv_dram_traffic.md)",
                     "kernel": "qs::gemv_kernel (fused decode + mma.sync matmul)",
                     "algorithmic_bytes_per_layer_set_per_rank": gb, "us_per_launch": us_per_mm,
                     "peak_source": f"{peak_src} (MEASURED_PEAKS.json hbm_gbs)"}

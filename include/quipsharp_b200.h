@@ -228,7 +228,7 @@ int qs_fit_scale_sweep(const float *x, int64_t samples, int prev_stages, const i
  * GPUs of a node.  Rank r of `world` holds weight rows [r m/world, (r+1)
  * m/world) (its own qs_pack_codes stream of those rows).  Every rank allocates
  * (zeroed) a float32 receive buffer of two regions of recv_floats each, an
- * int32 flag array [2][world] and two uint32 control words; it exports the
+ * int32 flag array [2][world] and four uint32 control words; it exports the
  * receive buffer and the flags with qs_ipc_export, exchanges the handles with
  * its peers (any host channel) and maps theirs with qs_ipc_import; qs_tp_peers
  * then lists every rank's buffers as mapped in this process.  Each call pushes
@@ -246,8 +246,10 @@ typedef struct qs_tp_peers {
   int rank;                             /* this process's rank */
   float *recv[QS_TP_MAX_RANKS];         /* every rank's receive buffer (float32 [2][recv_floats]) */
   int *flags[QS_TP_MAX_RANKS];          /* every rank's flags (int32 [2][world]) */
-  unsigned *ctl;                        /* this rank's control words (uint32 [2], 8-byte aligned) */
-  int64_t recv_floats;                  /* floats per region (>= batch * m of every call) */
+  unsigned *ctl;                        /* this rank's control words (uint32 [4], zeroed, 16-byte aligned) */
+  int64_t recv_floats;                  /* floats per region (>= batch * m of every call, twice
+                                           that for batches of at most 32 tokens, which travel
+                                           as 8-byte words {value, call number}) */
 } qs_tp_peers;
 
 /* CUDA IPC of a device pointer (any pointer into a cudaMalloc allocation):
@@ -283,6 +285,13 @@ int qs_linear_fwd_tp(const void *x, int x_dtype, int64_t batch, int64_t n, int64
  * call and applies the output step to the gathered y1 (m = m_local * world). */
 int qs_tp_push(const qs_tp_peers *peers, const float *y1, int64_t batch, int64_t m_local,
                qs_stream_t stream);
+/* qs_linear_matmul followed by qs_tp_push of its y1 shard, fused for batches
+ * of at most 32 tokens (the matmul's last CTA to finish pushes the shard and
+ * announces it, saving a kernel); larger batches run the two in sequence. */
+int qs_linear_matmul_tp(const void *x2_workspace, int64_t batch, int64_t n, int64_t m_local,
+                        const void *packed, int stages, const int *kinds, const float *stage_scales,
+                        const float *layer_scale, float *y1, const qs_tp_peers *peers,
+                        qs_stream_t stream);
 int qs_linear_output_peers(const qs_tp_peers *peers, int64_t batch, int64_t m, int transform,
                            const float *su, const void *phase_u, const float *bias, void *y,
                            int y_dtype, qs_stream_t stream);

@@ -68,6 +68,7 @@ _SIGS = {
     "qs_fit_workspace_bytes": (_L, [_L, _I]),
     "qs_fit_scale_sweep": (_I, [_P, _L, _I, _P, _P, _I, _I, _P, _P, _P, _I, _P, _L, _P, _P, _P]),
     "qs_tp_push": (_I, [_P, _P, _L, _L, _P]),
+    "qs_linear_matmul_tp": (_I, [_P, _L, _L, _L, _P, _I, _P, _P, _P, _P, _P, _P]),
     "qs_linear_output_peers": (_I, [_P, _L, _L, _I, _P, _P, _P, _P, _I, _P]),
     "qs_linear_fwd_tp": (_I, [_P, _I, _L, _L, _L, _P, _I, _P, _P, _P, _I, _P, _P, _P, _P, _P, _P, _P, _L, _P,
                               _P]),

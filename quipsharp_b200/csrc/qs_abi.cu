@@ -220,6 +220,20 @@ QS_API int qs_linear_matmul(const void *x2_workspace, int64_t batch, int64_t n, 
                        layer_scale, y1, (cudaStream_t)stream);
 }
 
+QS_API int qs_linear_matmul_tp(const void *x2_workspace, int64_t batch, int64_t n, int64_t m_local,
+                               const void *packed, int stages, const int *kinds, const float *stage_scales,
+                               const float *layer_scale, float *y1, const qs_tp_peers *peers, qs_stream_t stream) {
+  int st = check_kinds(stages, kinds);
+  if (st) return st;
+  if (batch < 0 || n <= 0 || n % 8 || m_local <= 0) return fail(QS_ERR_INVALID_ARG, "bad shape");
+  if (batch == 0) return launch_tp_push(peers, y1, 0, m_local, (cudaStream_t)stream);  // the call still counts
+  if (!x2_workspace || !packed || !layer_scale || !y1) return fail(QS_ERR_INVALID_ARG, "null pointer");
+  if (stages == 2 && !stage_scales) return fail(QS_ERR_INVALID_ARG, "RVQ needs stage scales");
+  if (!aligned(packed, 256)) return fail(QS_ERR_ALIGNMENT, "packed buffer must be 256-byte aligned");
+  return launch_matmul_tp(x2_workspace, batch, n, m_local, packed, stages, kinds, stage_scales, layer_scale, y1,
+                          peers, (cudaStream_t)stream);
+}
+
 QS_API int qs_linear_output(float *y1, int64_t ld_y1, int64_t shards, int64_t batch,
                             int64_t m, int transform, const float *su, const void *phase_u,
                             const float *bias, void *y, int y_dtype, qs_stream_t stream) {
@@ -327,7 +341,8 @@ QS_API int qs_linear_fwd_tp(const void *x, int x_dtype, int64_t batch, int64_t n
     return fail(QS_ERR_WORKSPACE, "workspace too small");
   if (!aligned(workspace, 256) || !aligned(packed, 256))
     return fail(QS_ERR_ALIGNMENT, "workspace/packed must be 256-byte aligned");
-  if (batch * m > peers->recv_floats) return fail(QS_ERR_WORKSPACE, "receive buffers too small");
+  if (batch * m * (batch < kTcMinBatch ? 2 : 1) > peers->recv_floats)
+    return fail(QS_ERR_WORKSPACE, "receive buffers too small");
   return launch_linear_fwd_tp(x, x_dtype, batch, n, m, packed, stages, kinds, stage_scales, layer_scale, transform,
                               su, sv, phase_u, phase_v, bias, y, workspace, peers, (cudaStream_t)stream);
 }

@@ -32,6 +32,7 @@
 // float32 y1 with atomics (y1 is zeroed by the input-transform kernel).
 #include "qs_common.cuh"
 #include "qs_launch.h"
+#include "qs_tp.cuh"
 
 namespace qs {
 
@@ -47,6 +48,9 @@ struct GemvArgs {
   float *y1;               // (batch, m)
   int64_t m, RT, KC, n_pad, items;  // RT: 16-row tiles, KC: 32-code chunks
   int tok0, ntok;
+  TpPush push;  // world > 0: the CTAs push y1 to every rank after a grid barrier (tensor parallelism)
+  uint64_t wait_ns;  // bound of that barrier
+  int *error;        // set when it ran out
 };
 
 // f16x2 words of the natural coordinate pairs (0,1), (2,3), (4,5), (6,7) from
@@ -232,24 +236,10 @@ __device__ __forceinline__ void load_activations(const GemvArgs &a, uint32_t kc,
 // 9 and more in passes of 16 tokens over the weights, one CTA per SM for the
 // registers; the tcgen05 GEMM takes over at kTcMinBatch).
 template <int K0, int K1, int NST, int NTG>
-__global__ void __launch_bounds__(kGemvThreads, NTG == 1 ? 2 : 1) gemv_kernel(GemvArgs a) {
-  extern __shared__ __align__(256) uint8_t gsm[];
-  pdl_launch_dependents();
-  // 256-byte aligned table rows: the row index is multiplied by 256 and the
-  // lane replica offset (< 256) added in one integer multiply-add
-  uint8_t *tbl = gsm + ((256u - (smem_u32(gsm) & 255u)) & 255u);
+__device__ __forceinline__ void gemv_items(const GemvArgs &a, const uint8_t *tbl, uint32_t start, uint32_t end,
+                                           uint4 (&q)[4], uint4 (&nq)[4]) {
   const int lane = threadIdx.x & 31;
-  const int64_t warp = blockIdx.x * (kGemvThreads / 32) + (threadIdx.x >> 5);
-  const int64_t nwarps = static_cast<int64_t>(gridDim.x) * (kGemvThreads / 32);
-  const uint32_t start = static_cast<uint32_t>(warp * a.items / nwarps);
-  const uint32_t end = static_cast<uint32_t>((warp + 1) * a.items / nwarps);
   const uint32_t m = static_cast<uint32_t>(a.m), RT = static_cast<uint32_t>(a.RT);
-  // prologue, independent of the previous kernel: first weights in flight, table fill
-  uint4 q[4], nq[4];
-  if (start < end) load_item<K0, K1, NST>(a, start, lane, q);
-  load_table(tbl);
-  __syncthreads();
-  if (start >= end) return;
   pdl_wait();  // x2h, rowscale and the zeroed y1 come from the input-transform kernel
 
   const uint32_t off_e8p = (lane & 7) * 16;        // E8P replicas: bytes [0, 128) of a row
@@ -318,6 +308,27 @@ __global__ void __launch_bounds__(kGemvThreads, NTG == 1 ? 2 : 1) gemv_kernel(Ge
   }
 }
 
+template <int K0, int K1, int NST, int NTG>
+__global__ void __launch_bounds__(kGemvThreads, NTG == 1 ? 2 : 1) gemv_kernel(GemvArgs a) {
+  extern __shared__ __align__(256) uint8_t gsm[];
+  pdl_launch_dependents();
+  // 256-byte aligned table rows: the row index is multiplied by 256 and the
+  // lane replica offset (< 256) added in one integer multiply-add
+  uint8_t *tbl = gsm + ((256u - (smem_u32(gsm) & 255u)) & 255u);
+  const int lane = threadIdx.x & 31;
+  const int64_t warp = blockIdx.x * (kGemvThreads / 32) + (threadIdx.x >> 5);
+  const int64_t nwarps = static_cast<int64_t>(gridDim.x) * (kGemvThreads / 32);
+  const uint32_t start = static_cast<uint32_t>(warp * a.items / nwarps);
+  const uint32_t end = static_cast<uint32_t>((warp + 1) * a.items / nwarps);
+  // prologue, independent of the previous kernel: first weights in flight, table fill
+  uint4 q[4], nq[4];
+  if (start < end) load_item<K0, K1, NST>(a, start, lane, q);
+  load_table(tbl);
+  __syncthreads();
+  if (start < end) gemv_items<K0, K1, NST, NTG>(a, tbl, start, end, q, nq);
+  if (a.push.world) tp_push_grid(a.push, a.wait_ns, a.error);  // every thread of every CTA arrives
+}
+
 static int num_sms() {
   static int cached[64] = {0};
   int dev = 0;
@@ -330,7 +341,7 @@ static int num_sms() {
 }
 
 template <int K0, int K1, int NST>
-static int run_gemv(GemvArgs &a, int64_t batch, cudaStream_t s) {
+static int run_gemv(GemvArgs &a, int64_t batch, cudaStream_t s, const TpPush *push) {
   // batches above 8: passes of 16 tokens (two token groups); else one pass of 8
   const bool two = batch > 8;
   auto kern = two ? gemv_kernel<K0, K1, NST, 2> : gemv_kernel<K0, K1, NST, 1>;
@@ -343,6 +354,12 @@ static int run_gemv(GemvArgs &a, int64_t batch, cudaStream_t s) {
   for (int64_t tok0 = 0; tok0 < batch; tok0 += per_pass) {
     a.tok0 = static_cast<int>(tok0);
     a.ntok = static_cast<int>(batch - tok0 < per_pass ? batch - tok0 : per_pass);
+    if (push && tok0 + per_pass >= batch) {  // the last pass pushes every token's rows
+      a.push = *push;
+      a.wait_ns = pipeline_wait_ns();
+      a.error = device_error_flag();
+      if (!a.error) return fail(QS_ERR_CUDA, "device error flag unavailable");
+    }
     int st = launch_pdl("gemv", kern, dim3(grid), dim3(kGemvThreads), kTblBytes + 256, s, a);
     if (st) return st;
   }
@@ -351,9 +368,11 @@ static int run_gemv(GemvArgs &a, int64_t batch, cudaStream_t s) {
 
 int launch_matmul(const void *x2ws, int64_t batch, int64_t n, int64_t m, const void *packed,
                   int stages, const int *kinds, const float *stage_scales,
-                  const float *layer_scale, float *y1, cudaStream_t s) {
-  if (batch >= kTcMinBatch)
+                  const float *layer_scale, float *y1, cudaStream_t s, const TpPush *push) {
+  if (batch >= kTcMinBatch) {
+    if (push) return fail(QS_ERR_INVALID_ARG, "the prefill matmul does not push");
     return launch_matmul_tc(x2ws, batch, n, m, packed, stages, kinds, stage_scales, layer_scale, y1, s);
+  }
   // the decode kernel indexes with 32 bits
   if (batch * m >= (int64_t(1) << 31) || stage_bytes(QS_CB_E8P, m, n) >= (int64_t(1) << 31) ||
       batch * padded_T(n) * 8 >= (int64_t(1) << 31))
@@ -378,13 +397,13 @@ int launch_matmul(const void *x2ws, int64_t batch, int64_t n, int64_t m, const v
   }
   const int k0 = kinds[0], k1 = stages == 2 ? kinds[1] : 0;
   if (stages == 1) {
-    return k0 == QS_CB_E8P ? run_gemv<QS_CB_E8P, 0, 1>(a, batch, s)
-                           : run_gemv<QS_CB_E8_1BIT, 0, 1>(a, batch, s);
+    return k0 == QS_CB_E8P ? run_gemv<QS_CB_E8P, 0, 1>(a, batch, s, push)
+                           : run_gemv<QS_CB_E8_1BIT, 0, 1>(a, batch, s, push);
   }
-  if (k0 == QS_CB_E8P && k1 == QS_CB_E8_1BIT) return run_gemv<QS_CB_E8P, QS_CB_E8_1BIT, 2>(a, batch, s);
-  if (k0 == QS_CB_E8P && k1 == QS_CB_E8P) return run_gemv<QS_CB_E8P, QS_CB_E8P, 2>(a, batch, s);
-  if (k0 == QS_CB_E8_1BIT && k1 == QS_CB_E8P) return run_gemv<QS_CB_E8_1BIT, QS_CB_E8P, 2>(a, batch, s);
-  return run_gemv<QS_CB_E8_1BIT, QS_CB_E8_1BIT, 2>(a, batch, s);
+  if (k0 == QS_CB_E8P && k1 == QS_CB_E8_1BIT) return run_gemv<QS_CB_E8P, QS_CB_E8_1BIT, 2>(a, batch, s, push);
+  if (k0 == QS_CB_E8P && k1 == QS_CB_E8P) return run_gemv<QS_CB_E8P, QS_CB_E8P, 2>(a, batch, s, push);
+  if (k0 == QS_CB_E8_1BIT && k1 == QS_CB_E8P) return run_gemv<QS_CB_E8_1BIT, QS_CB_E8P, 2>(a, batch, s, push);
+  return run_gemv<QS_CB_E8_1BIT, QS_CB_E8_1BIT, 2>(a, batch, s, push);
 }
 
 }  // namespace qs

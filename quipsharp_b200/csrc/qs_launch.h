@@ -30,6 +30,7 @@ int launch_linear_input(const void *x, int x_dtype, int64_t batch, int64_t n, in
                         const float *sv, const void *phase_v, void *x2ws, float *y1,
                         int64_t m_local, cudaStream_t s);
 struct XPeerGather;
+struct TpPush;
 int launch_linear_output(float *y1, int64_t ld_y1, int64_t shards, int64_t batch, int64_t m,
                          int transform, const float *su, const void *phase_u, const float *bias,
                          void *y, int y_dtype, cudaStream_t s, const XPeerGather *pg = nullptr);
@@ -74,6 +75,9 @@ int ipc_import(const void *handle, int64_t offset, void **ptr);
 int ipc_close(void *ptr, int64_t offset);
 int64_t tp_workspace_bytes(int64_t batch, int64_t n, int64_t m_local);
 int launch_tp_push(const qs_tp_peers *pe, const float *y1, int64_t batch, int64_t m_local, cudaStream_t s);
+int launch_matmul_tp(const void *x2ws, int64_t batch, int64_t n, int64_t m_local, const void *packed, int stages,
+                     const int *kinds, const float *stage_scales, const float *layer_scale, float *y1,
+                     const qs_tp_peers *pe, cudaStream_t s);
 int launch_output_peers(const qs_tp_peers *pe, int64_t batch, int64_t m, int transform, const float *su,
                         const void *phase_u, const float *bias, void *y, int y_dtype, cudaStream_t s);
 int launch_linear_fwd_tp(const void *x, int x_dtype, int64_t batch, int64_t n, int64_t m, const void *packed,
@@ -86,10 +90,11 @@ int launch_pack(const int16_t *codes, int stages, const int *kinds, int64_t m, i
                 void *packed, cudaStream_t s);
 
 // qs_gemv.cu: fused decode + matmul; batches below kTcMinBatch run the
-// decode-regime kernel of this file, larger ones launch_matmul_tc
+// decode-regime kernel of this file, larger ones launch_matmul_tc.  push
+// (decode batches only): the grid's last CTA pushes y1 to every rank.
 int launch_matmul(const void *x2ws, int64_t batch, int64_t n, int64_t m, const void *packed,
                   int stages, const int *kinds, const float *stage_scales,
-                  const float *layer_scale, float *y1, cudaStream_t s);
+                  const float *layer_scale, float *y1, cudaStream_t s, const TpPush *push = nullptr);
 
 // qs_gemm_tc.cu
 int launch_matmul_tc(const void *x2ws, int64_t batch, int64_t n, int64_t m, const void *packed, int stages,

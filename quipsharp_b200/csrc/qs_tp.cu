@@ -25,6 +25,7 @@
 
 #include "qs_common.cuh"
 #include "qs_launch.h"
+#include "qs_tp.cuh"
 #include "qs_xform.cuh"
 
 namespace qs {
@@ -33,52 +34,28 @@ namespace {
 
 constexpr int kPushThreads = 256;
 
-struct TpPush {
-  const float *y1;         // private shard (count floats)
-  float *dst[kMaxPeers];   // every rank's receive buffer (region 0) + this shard's gathered offset
-  int *flag[kMaxPeers];    // every rank's flags (region 0) + this rank
-  unsigned *ctl;           // this rank's [sequence number, finished CTAs]
-  int64_t count;
-  int64_t stride;          // floats between parity regions of a receive buffer
-  int nflag_stride;        // ints between parity regions of a flag array (world)
-  int world;
-};
-
+// Separate push (prefill batches, or a shard computed by the caller): every CTA
+// copies its part, then arrives; the last CTA announces the call.
 __global__ void __launch_bounds__(kPushThreads) tp_push_kernel(TpPush a) {
   __shared__ unsigned s_seq;
   pdl_wait();  // the matmul's y1 writes are complete
   if (threadIdx.x == 0) s_seq = *reinterpret_cast<volatile unsigned *>(a.ctl) + 1u;
   __syncthreads();
   const unsigned seq = s_seq;
-  const int64_t off = (seq & 1u) * a.stride;
   const int64_t tid = blockIdx.x * static_cast<int64_t>(blockDim.x) + threadIdx.x;
-  const int64_t nth = static_cast<int64_t>(gridDim.x) * blockDim.x;
-  bool vec = (a.count & 3) == 0 && (reinterpret_cast<uintptr_t>(a.y1) & 15) == 0;
-  for (int r = 0; r < a.world; ++r) vec = vec && (reinterpret_cast<uintptr_t>(a.dst[r] + off) & 15) == 0;
-  if (vec) {
-    const float4 *src = reinterpret_cast<const float4 *>(a.y1);
-    for (int64_t i = tid; i < a.count / 4; i += nth) {
-      const float4 v = src[i];
-      for (int r = 0; r < a.world; ++r) reinterpret_cast<float4 *>(a.dst[r] + off)[i] = v;
-    }
-  } else {
-    for (int64_t i = tid; i < a.count; i += nth) {
-      const float v = a.y1[i];
-      for (int r = 0; r < a.world; ++r) a.dst[r][off + i] = v;
-    }
-  }
+  tp_push_copy(a, (seq & 1u) * a.stride, tid, static_cast<int64_t>(gridDim.x) * blockDim.x, seq);
   __syncthreads();
   if (threadIdx.x == 0) {
-    __threadfence_system();  // this CTA's pushed data before its arrival count
-    const unsigned done = atomicAdd(a.ctl + 1, 1u);
-    if (done == gridDim.x - 1) {  // the last CTA: every CTA's data is out
-      a.ctl[1] = 0;
-      a.ctl[0] = seq;  // every CTA read the old value before its arrival count
-      __threadfence_system();
-      for (int r = 0; r < a.world; ++r)
-        asm volatile("st.release.sys.global.b32 [%0], %1;" ::"l"(a.flag[r] + (seq & 1u) * a.nflag_stride),
-                     "r"(seq)
-                     : "memory");
+    if (a.words) {
+      __threadfence();  // the sequence number is read by every CTA before the last one records it
+      if (atomicAdd(a.ctl + 1, 1u) == gridDim.x - 1) {
+        a.ctl[1] = 0;
+        a.ctl[0] = seq;
+      }
+    } else {
+      __threadfence_system();  // this CTA's pushed data before its arrival count
+      // every CTA read the old sequence number before its arrival count
+      if (atomicAdd(a.ctl + 1, 1u) == gridDim.x - 1) tp_announce(a, seq);
     }
   }
   pdl_launch_dependents();
@@ -111,7 +88,7 @@ int check_peers(const qs_tp_peers *pe) {
   if (!pe) return fail(QS_ERR_INVALID_ARG, "null peers");
   if (pe->world < 1 || pe->world > kMaxPeers || pe->rank < 0 || pe->rank >= pe->world)
     return fail(QS_ERR_INVALID_ARG, "bad world %d / rank %d (at most %d ranks)", pe->world, pe->rank, kMaxPeers);
-  if (!pe->ctl || (reinterpret_cast<uintptr_t>(pe->ctl) & 7)) return fail(QS_ERR_INVALID_ARG, "bad ctl words");
+  if (!pe->ctl || (reinterpret_cast<uintptr_t>(pe->ctl) & 15)) return fail(QS_ERR_INVALID_ARG, "bad ctl words");
   for (int r = 0; r < pe->world; ++r)
     if (!pe->recv[r] || !pe->flags[r]) return fail(QS_ERR_INVALID_ARG, "missing buffer of rank %d", r);
   return QS_OK;
@@ -148,11 +125,17 @@ int64_t tp_workspace_bytes(int64_t batch, int64_t n, int64_t m_local) {
   return round_up(linear_input_bytes(batch, n), 256) + round_up(batch * m_local * 4, 256);
 }
 
-int launch_tp_push(const qs_tp_peers *pe, const float *y1, int64_t batch, int64_t m_local, cudaStream_t s) {
+// Decode batches exchange self-validating words (qs_tp.cuh), prefill batches
+// flagged floats; push and output step pick the same format from the batch.
+static bool word_format(int64_t batch) { return batch < kTcMinBatch; }
+
+static int make_push(const qs_tp_peers *pe, const float *y1, int64_t batch, int64_t m_local, TpPush &a) {
   int st = check_peers(pe);
   if (st) return st;
-  if (batch * m_local * pe->world > pe->recv_floats) return fail(QS_ERR_WORKSPACE, "receive buffers too small");
-  TpPush a{};
+  const int64_t per = word_format(batch) ? 2 : 1;  // floats of receive region per value
+  if (batch * m_local * pe->world * per > pe->recv_floats) return fail(QS_ERR_WORKSPACE, "receive buffers too small");
+  a = TpPush{};
+  a.words = word_format(batch) ? 1 : 0;
   a.y1 = y1;
   a.count = batch * m_local;
   a.stride = pe->recv_floats;
@@ -160,14 +143,33 @@ int launch_tp_push(const qs_tp_peers *pe, const float *y1, int64_t batch, int64_
   a.world = pe->world;
   a.ctl = pe->ctl;
   for (int r = 0; r < pe->world; ++r) {
-    a.dst[r] = pe->recv[r] + pe->rank * a.count;
+    a.dst[r] = pe->recv[r] + per * pe->rank * a.count;
     a.flag[r] = pe->flags[r] + pe->rank;
   }
+  return QS_OK;
+}
+
+int launch_tp_push(const qs_tp_peers *pe, const float *y1, int64_t batch, int64_t m_local, cudaStream_t s) {
+  TpPush a;
+  int st = make_push(pe, y1, batch, m_local, a);
+  if (st) return st;
   // ~16 KB of shard per CTA, at most one wave of 4 CTAs per SM
   const int64_t want = (a.count + 4095) / 4096;
   const int64_t most = 4 * static_cast<int64_t>(xlaunch_sms());
   const int grid = static_cast<int>(want < 1 ? 1 : want > most ? most : want);
   return launch_pdl("tp_push", tp_push_kernel, dim3(grid), dim3(kPushThreads), 0, s, a);
+}
+
+int launch_matmul_tp(const void *x2ws, int64_t batch, int64_t n, int64_t m_local, const void *packed, int stages,
+                     const int *kinds, const float *stage_scales, const float *layer_scale, float *y1,
+                     const qs_tp_peers *pe, cudaStream_t s) {
+  if (batch >= kTcMinBatch) {  // the tcgen05 GEMM, then the push kernel
+    int st = launch_matmul(x2ws, batch, n, m_local, packed, stages, kinds, stage_scales, layer_scale, y1, s);
+    return st ? st : launch_tp_push(pe, y1, batch, m_local, s);
+  }
+  TpPush push;  // the decode matmul's last CTA pushes the shard
+  int st = make_push(pe, y1, batch, m_local, push);
+  return st ? st : launch_matmul(x2ws, batch, n, m_local, packed, stages, kinds, stage_scales, layer_scale, y1, s, &push);
 }
 
 int launch_output_peers(const qs_tp_peers *pe, int64_t batch, int64_t m, int transform, const float *su,
@@ -177,8 +179,10 @@ int launch_output_peers(const qs_tp_peers *pe, int64_t batch, int64_t m, int tra
   if (m % pe->world) return fail(QS_ERR_INVALID_ARG, "m=%lld not divisible by %d ranks", (long long)m, pe->world);
   if (transform == QS_RFFT && (m / pe->world) % 2)
     return fail(QS_ERR_INVALID_ARG, "RFFT shards must hold an even number of columns");
-  if (batch * m > pe->recv_floats) return fail(QS_ERR_WORKSPACE, "receive buffers too small");
+  if (batch * m * (word_format(batch) ? 2 : 1) > pe->recv_floats)
+    return fail(QS_ERR_WORKSPACE, "receive buffers too small");
   XPeerGather pg{};
+  pg.words = word_format(batch) ? 1 : 0;
   pg.base = pe->recv[pe->rank];
   pg.stride = pe->recv_floats;
   pg.flags = pe->flags[pe->rank];
@@ -199,9 +203,7 @@ int launch_linear_fwd_tp(const void *x, int x_dtype, int64_t batch, int64_t n, i
   const bool tc = batch >= kTcMinBatch;  // the prefill GEMM writes every y1 element
   int st = launch_linear_input(x, x_dtype, batch, n, transform, sv, phase_v, workspace, tc ? nullptr : y1, m_local, s);
   if (st) return st;
-  st = launch_matmul(workspace, batch, n, m_local, packed, stages, kinds, stage_scales, layer_scale, y1, s);
-  if (st) return st;
-  st = launch_tp_push(pe, y1, batch, m_local, s);
+  st = launch_matmul_tp(workspace, batch, n, m_local, packed, stages, kinds, stage_scales, layer_scale, y1, pe, s);
   if (st) return st;
   return launch_output_peers(pe, batch, m, transform, su, phase_u, bias, y, x_dtype, s);
 }

@@ -958,19 +958,74 @@ __device__ __forceinline__ int64_t xy1_offset(int64_t row, int64_t col, int64_t 
 // Output step of a column-sharded layer whose y1 shards every rank pushed into
 // this rank's receive buffer (tensor parallelism over peer memory): the call's
 // parity region base + (seq & 1) * stride holds the rank-major gathered layout
-// of xy1_offset, complete once every flags[(seq & 1) * nflags + r] has reached
-// the call's sequence number seq (set by rank r after its pushed data,
-// system-scope release).  flags == null: y1 is the kernel's y1 argument.
+// of xy1_offset, seq being the call's sequence number.  Flagged format: plain
+// floats, complete once every flags[(seq & 1) * nflags + r] has reached seq
+// (set by rank r after its pushed data, system-scope release).  Word format
+// (words = 1): value i is the 8-byte word i {float bits, seq of the call that
+// wrote it}, valid once its seq matches.  flags == null: y1 is the kernel's y1
+// argument.
 constexpr int kMaxPeers = 8;
 struct XPeerGather {
   const float *base;     // this rank's receive buffer (parity region 0): gathered rank-major shards
   int64_t stride;        // floats between the two parity regions
   const int *flags;       // this rank's arrival flags, int32 [2][nflags]
-  const unsigned *seq;    // this rank's call sequence number (written by its push kernel)
+  const unsigned *seq;    // this rank's call sequence number (written by its push)
   int nflags;
+  int words;              // 1: self-validating 8-byte words, no flags
   uint64_t wait_ns;
-  int *error;  // set when the flags did not all arrive within wait_ns
+  int *error;  // set when a wait ran out
 };
+
+// Where an output step reads y1 from: the kernel's own y1 (plain floats) or a
+// receive region.  A reader that gives up (wait limit) marks itself dead and
+// reads zeros from then on; the error flag tells the host.
+struct XPeerSrc {
+  const float *base;
+  unsigned seq;
+  int words;
+  uint64_t wait_ns;
+  int *error;
+
+  __device__ __forceinline__ bool expired(uint64_t &t0, bool &dead) const {
+    uint64_t t;
+    asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
+    if (!t0) t0 = t;
+    if (t - t0 <= wait_ns) return false;
+    atomicExch(error, 1);
+    dead = true;
+    return true;
+  }
+  __device__ __forceinline__ float get(int64_t i, bool &dead) const {
+    if (!base || dead) return 0.f;
+    if (!words) return base[i];
+    const uint32_t *w = reinterpret_cast<const uint32_t *>(base) + 2 * i;
+    uint64_t t0 = 0;
+    for (;;) {
+      uint32_t v, sq;
+      asm volatile("ld.volatile.global.v2.u32 {%0, %1}, [%2];" : "=r"(v), "=r"(sq) : "l"(w) : "memory");
+      if (sq == seq) return __uint_as_float(v);
+      if (expired(t0, dead)) return 0.f;
+    }
+  }
+  // values i, i + 1 (i even)
+  __device__ __forceinline__ float2 get2(int64_t i, bool &dead) const {
+    if (!base || dead) return make_float2(0.f, 0.f);
+    if (!words) return *reinterpret_cast<const float2 *>(base + i);
+    const uint32_t *w = reinterpret_cast<const uint32_t *>(base) + 2 * i;
+    uint64_t t0 = 0;
+    for (;;) {
+      uint32_t v0, s0, v1, s1;
+      asm volatile("ld.volatile.global.v4.u32 {%0, %1, %2, %3}, [%4];"
+                   : "=r"(v0), "=r"(s0), "=r"(v1), "=r"(s1)
+                   : "l"(w)
+                   : "memory");
+      if (s0 == seq && s1 == seq) return make_float2(__uint_as_float(v0), __uint_as_float(v1));
+      if (expired(t0, dead)) return make_float2(0.f, 0.f);
+    }
+  }
+};
+
+__device__ __forceinline__ XPeerSrc xplain_src(const float *y1) { return XPeerSrc{y1, 0u, 0, 0, nullptr}; }
 
 struct XRowArgs {
   int64_t row_base;
@@ -981,39 +1036,42 @@ struct XRowArgs {
   XPeerGather pg;
 };
 
-// Waits (every CTA, bounded) until every rank's shard of this call has arrived
-// in this rank's receive buffer and returns the parity region holding them;
-// nullptr on timeout (error flag set, the caller then reads zeros).  The call's
-// sequence number was written by this rank's push kernel, complete before the
-// caller's pdl_wait returned; each rank stores the sequence number into flag
-// [parity][its rank] after its pushed data.
-__device__ __forceinline__ const float *xwait_peers(const XPeerGather &pg) {
-  __shared__ int s_par;
+// The receive region of this call (every thread of the CTA calls it).  The
+// call's sequence number was written by this rank's push, complete before the
+// caller's pdl_wait returned.  Flagged format: waits (thread 0, bounded) until
+// every rank's flag of this call is set, else gives up (error flag set, base
+// null: zeros are read).  Word format: no wait here; the reads wait per word.
+__device__ __forceinline__ XPeerSrc xwait_peers(const XPeerGather &pg) {
+  __shared__ int s_ok;
+  __shared__ unsigned s_seq;
   if (threadIdx.x == 0) {
     const unsigned seq = *reinterpret_cast<const volatile unsigned *>(pg.seq);
-    const int par = static_cast<int>(seq & 1u);
-    const int *fl = pg.flags + par * pg.nflags;
     bool ok = true;
-    uint64_t t0 = 0;
-    for (int r = 0; r < pg.nflags && ok; ++r) {
-      for (;;) {
-        int v;
-        asm volatile("ld.acquire.sys.global.b32 %0, [%1];" : "=r"(v) : "l"(fl + r) : "memory");
-        if (static_cast<int>(static_cast<unsigned>(v) - seq) >= 0) break;
-        uint64_t t;
-        asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
-        if (!t0) t0 = t;
-        if (t - t0 > pg.wait_ns) {
-          ok = false;
-          atomicExch(pg.error, 1);
-          break;
+    if (!pg.words) {
+      const int *fl = pg.flags + static_cast<int>(seq & 1u) * pg.nflags;
+      uint64_t t0 = 0;
+      for (int r = 0; r < pg.nflags && ok; ++r) {
+        for (;;) {
+          int v;
+          asm volatile("ld.acquire.sys.global.b32 %0, [%1];" : "=r"(v) : "l"(fl + r) : "memory");
+          if (static_cast<int>(static_cast<unsigned>(v) - seq) >= 0) break;
+          uint64_t t;
+          asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
+          if (!t0) t0 = t;
+          if (t - t0 > pg.wait_ns) {
+            ok = false;
+            atomicExch(pg.error, 1);
+            break;
+          }
         }
       }
     }
-    s_par = ok ? par : -1;
+    s_ok = ok;
+    s_seq = seq;
   }
   __syncthreads();
-  return s_par < 0 ? nullptr : pg.base + s_par * pg.stride;
+  const unsigned seq = s_seq;
+  return XPeerSrc{s_ok ? pg.base + (seq & 1u) * pg.stride : nullptr, seq, pg.words, pg.wait_ns, pg.error};
 }
 
 // Hint flag for the input kernels' dry pass: few-row output steps set it at
@@ -1173,11 +1231,9 @@ __global__ void __launch_bounds__(kXMaxThreads, 1) xoutput_rfft_kernel(
   }
   build_xtw(tw, N);
   pdl_wait();  // y1 comes from the matmul (or the all-gather, or the ranks' pushes)
-  const float *src = ra.pg.flags ? xwait_peers(ra.pg) : y1;
-  auto gsrc = [&](int e) {
-    return src ? *reinterpret_cast<const float2 *>(src + xy1_offset(row, 2 * e, ld_y1, shards, mp, batch))
-               : float2{0.f, 0.f};
-  };
+  const XPeerSrc src = ra.pg.flags ? xwait_peers(ra.pg) : xplain_src(y1);
+  bool dead = false;
+  auto gsrc = [&](int e) { return src.get2(xy1_offset(row, 2 * e, ld_y1, shards, mp, batch), dead); };
   auto sink = [&](int e, float2 z) {
     z.x *= scale;
     z.y *= scale;
@@ -1301,8 +1357,9 @@ __global__ void __launch_bounds__(kXMaxThreads, 1) xoutput_rht_kernel(
     xprefetch_l2(bias, 4 * static_cast<int64_t>(m), rank, plan.C);
   }
   pdl_wait();  // y1 comes from the matmul (or the all-gather, or the ranks' pushes)
-  const float *src = ra.pg.flags ? xwait_peers(ra.pg) : y1;
-  auto gsrc = [&](int i) { return src ? src[xy1_offset(row, i, ld_y1, shards, mp, batch)] : 0.f; };
+  const XPeerSrc src = ra.pg.flags ? xwait_peers(ra.pg) : xplain_src(y1);
+  bool dead = false;
+  auto gsrc = [&](int i) { return src.get(xy1_offset(row, i, ld_y1, shards, mp, batch), dead); };
   auto sink = [&](int i, float v) {
     v = v * scale * su[i];
     if (bias) v += bias[i];

@@ -209,7 +209,8 @@ __global__ void __launch_bounds__(32 << LW) xsmall_output_rht_kernel(SmallOut a)
       bb[j * W + k] = a.bias ? __ldg(a.bias + i) : 0.f;
     }
   pdl_wait();  // y1 comes from the matmul (or the ranks' pushes)
-  const float *src = a.pg.flags ? xwait_peers(a.pg) : a.y1;
+  const XPeerSrc src = a.pg.flags ? xwait_peers(a.pg) : xplain_src(a.y1);
+  bool dead = false;
   float v[V];
 #pragma unroll
   for (int r = 0; r < V; ++r) {
@@ -217,7 +218,7 @@ __global__ void __launch_bounds__(32 << LW) xsmall_output_rht_kernel(SmallOut a)
     int64_t off;
     if (a.shard_log2 < 0) off = row * a.ld_y1 + i;
     else off = ((static_cast<int64_t>(i >> a.shard_log2) * a.batch + row) << a.shard_log2) + (i & ((1 << a.shard_log2) - 1));
-    v[r] = src ? src[off] : 0.f;
+    v[r] = src.get(off, dead);
   }
   fwht_row_small<LV, LW>(v, sm_small);
 #pragma unroll
@@ -510,7 +511,8 @@ __global__ void __launch_bounds__(32 << LW) xsmall_output_rfft_kernel(SmallOutF 
     if constexpr (kBiasEarly) bb[i] = bias2 ? ldg_pinned(bias2 + t + T * i) : make_float2(0.f, 0.f);
   }
   pdl_wait();  // y1 comes from the matmul (or the ranks' pushes)
-  const float *src = a.pg.flags ? xwait_peers(a.pg) : a.y1;
+  const XPeerSrc src = a.pg.flags ? xwait_peers(a.pg) : xplain_src(a.y1);
+  bool dead = false;
   float2 v[V];
 #pragma unroll
   for (int r = 0; r < V; ++r) {
@@ -518,7 +520,7 @@ __global__ void __launch_bounds__(32 << LW) xsmall_output_rfft_kernel(SmallOutF 
     int64_t off;
     if (a.shard_log2 < 0) off = row * a.ld_y1 + c;
     else off = ((static_cast<int64_t>(c >> a.shard_log2) * a.batch + row) << a.shard_log2) + (c & ((1 << a.shard_log2) - 1));
-    v[r] = src ? *reinterpret_cast<const float2 *>(src + off) : make_float2(0.f, 0.f);
+    v[r] = src.get2(off, dead);
   }
   f.run(v, smf_small, stage);
   __syncthreads();

@@ -3,10 +3,11 @@
 Rank r of P holds weight rows [r*m/P, (r+1)*m/P) (its slice of `codes`).  A
 forward runs, on every rank, the input transform of the full activations, the
 fused decode + matmul of the local rows into a private float32 y1 shard, a push
-kernel that stores the shard into every rank's receive buffer over NVLink and
-then raises this rank's flag there, and the output transform, which waits for
-all ranks' flags and reads the gathered y1 locally (no collective library call
-on the data path).  Every rank ends with the full output, ready for the next
+of the shard into every rank's receive buffer over NVLink (decode batches: by
+the matmul's last CTA, as 8-byte words that carry the call's sequence number, so
+no fence or flag is needed; prefill batches: a push kernel, then a flag in every
+rank's memory), and the output transform, which reads the gathered y1 locally
+once it has arrived (no collective library call on the data path).  Every rank ends with the full output, ready for the next
 layer.
 
 The receive buffers and flags live in a `TPContext` per (process group,
@@ -46,8 +47,14 @@ def gathered_offset(b: int, c: int, batch: int, m: int, world: int) -> int:
 
 def exchange_floats(capacity: int, world: int) -> int:
     """float32 elements of one rank's exchange allocation: receive regions
-    [2][capacity], flags [2][world] (int32) and two uint32 control words."""
-    return 2 * capacity + 2 * world + 2
+    [2][capacity], flags [2][world] (int32, padded to 4 entries) and four uint32
+    control words (16-byte aligned: capacity is a multiple of 4)."""
+    return ctl_offset(capacity, world) + 4
+
+
+def ctl_offset(capacity: int, world: int) -> int:
+    """float32 index of the control words in an exchange allocation."""
+    return 2 * capacity + (2 * world + 3) // 4 * 4
 
 
 def make_peers(world: int, rank: int, bases: list[int], capacity: int) -> "N.TPPeers":
@@ -59,7 +66,7 @@ def make_peers(world: int, rank: int, bases: list[int], capacity: int) -> "N.TPP
     for r, base in enumerate(bases):
         peers.recv[r] = base
         peers.flags[r] = base + 2 * capacity * 4
-    peers.ctl = bases[rank] + (2 * capacity + 2 * world) * 4
+    peers.ctl = bases[rank] + ctl_offset(capacity, world) * 4
     return peers
 
 
@@ -95,7 +102,7 @@ class TPContext:
         if torch.cuda.is_current_stream_capturing():
             raise RuntimeError("tensor-parallel exchange buffers must grow outside CUDA graph capture "
                                "(run one eager forward of the largest batch first)")
-        cap = max(floats, 2 * self.capacity, 1 << 16)
+        cap = (max(floats, 2 * self.capacity, 1 << 16) + 3) // 4 * 4
         self.release()
         # one allocation (one IPC handle): receive regions [2][cap] float32, flags
         # [2][world] int32, then this rank's two uint32 control words
@@ -166,7 +173,8 @@ class TPQuantizedLinear(nn.Module):
         y = torch.empty(B, self.m, dtype=io_dtype, device=x.device)
         if B == 0:
             return y.view(*lead, self.m).to(x.dtype)
-        self.ctx.ensure(B * self.m)
+        # decode batches exchange 8-byte self-validating words, prefill batches floats
+        self.ctx.ensure(B * self.m * (2 if B <= 32 else 1))
         nb = N.lib().qs_linear_tp_workspace_bytes(B, self.n, self.mp)
         ws = torch.empty(nb, dtype=torch.uint8, device=x.device)
         k = self.local

@@ -2,7 +2,7 @@
 
 P ranks are emulated in one process on one stream: each rank's exchange
 allocation is an ordinary device buffer, and every "rank" runs input step,
-matmul of its row shard and qs_tp_push (stores into all ranks' receive buffers
+matmul of its row shard and qs_tp_push, or the fused qs_linear_matmul_tp, (stores into all ranks' receive buffers
 plus flags) before any rank runs qs_linear_output_peers.  Kernels therefore run
 strictly one after another, so no kernel ever waits for one that has not been
 launched; every output step finds its flags already set.  This checks the
@@ -25,7 +25,8 @@ class Emulated:
     def __init__(self, full, world):
         from quipsharp_b200 import _native as N
         from quipsharp_b200.quantize import LinearKernel
-        from quipsharp_b200.tensor_parallel import exchange_floats, make_peers, shard_rows
+        from quipsharp_b200.tensor_parallel import exchange_floats, make_peers, shard_rows, ctl_offset
+        self.ctl_at = ctl_offset
         self.N, self.world = N, world
         m, n = full.out_features, full.in_features
         self.m, self.n, self.mp = m, n, m // world
@@ -47,8 +48,10 @@ class Emulated:
         bases = [b.data_ptr() for b in self.bufs]
         self.peers = [make_peers(world, r, bases, self.cap) for r in range(world)]
 
-    def __call__(self, x, ys):
-        """One call of every rank; ys[r] receives rank r's full output."""
+    def __call__(self, x, ys, fused=False):
+        """One call of every rank; ys[r] receives rank r's full output.  fused: the
+        matmul's last CTA pushes (qs_linear_matmul_tp), else qs_linear_matmul then
+        qs_tp_push."""
         import ctypes
         N = self.N
         B = x.shape[0]
@@ -56,15 +59,21 @@ class Emulated:
         for r, k in enumerate(self.shards):
             y1 = torch.empty(B, self.mp, dtype=torch.float32, device=x.device)
             ws = k.input(x, None if B >= 33 else y1)
-            k.matmul(ws, B, y1)
-            N.check(N.lib().qs_tp_push(ctypes.addressof(self.peers[r]), N.ptr(y1), B, self.mp, N.stream_of(x)))
+            pr = ctypes.addressof(self.peers[r])
+            if fused:
+                N.check(N.lib().qs_linear_matmul_tp(N.ptr(ws), B, k.n, k.m, N.ptr(k.packed), len(k.kinds),
+                                                    k._kinds_c, k._ss_c, N.ptr(k.scale), N.ptr(y1), pr,
+                                                    N.stream_of(x)))
+            else:
+                k.matmul(ws, B, y1)
+                N.check(N.lib().qs_tp_push(pr, N.ptr(y1), B, self.mp, N.stream_of(x)))
         for r in range(self.world):
             N.check(N.lib().qs_linear_output_peers(
                 ctypes.addressof(self.peers[r]), B, self.m, self.shards[r].transform, N.ptr(self.su),
                 N.ptr(self.phase_u), N.ptr(self.bias), N.ptr(ys[r]), N.IO_DTYPES[x.dtype], N.stream_of(x)))
 
     def sequence(self):
-        return [int(b[2 * self.cap + 2 * self.world].view(torch.int32).item()) for b in self.bufs]
+        return [int(b[self.ctl_at(self.cap, self.world)].view(torch.int32).item()) for b in self.bufs]
 
 
 def _module(m, n, kinds, transform):
@@ -85,18 +94,18 @@ def test_emulated_ranks_match_unsharded(world, m, n, kinds, transform, B):
     from quipsharp_b200 import _native as N
     full = _module(m, n, kinds, transform)
     em = Emulated(full, world)
-    for call in range(3):  # successive calls alternate receive regions
+    for call in range(4):  # successive calls alternate receive regions and push routes
         x = syn.make_activations(B, n, dtype=torch.float16, seed=30 + call).cuda()
         y_ref = full(x)
         ys = [torch.empty(B, m, dtype=torch.float16, device="cuda") for _ in range(world)]
-        em(x, ys)
+        em(x, ys, fused=call % 2 == 1)
         torch.cuda.synchronize()
         assert N.lib().qs_device_status(N.stream_of(ys[0])) == 0
         for r in range(world):
             err = rel_l2(ys[r].float().cpu().numpy(), y_ref.float().cpu().numpy())
             assert err < 2e-3, (call, r, err)
             assert torch.equal(ys[r], ys[0]), (call, r)
-    assert em.sequence() == [3] * world
+    assert em.sequence() == [4] * world
 
 
 def test_emulated_graph_replay_mixed_with_direct_calls():
@@ -109,14 +118,14 @@ def test_emulated_graph_replay_mixed_with_direct_calls():
     em = Emulated(full, world)
     xg = syn.make_activations(B, n, dtype=torch.float16, seed=40).cuda()
     yg = [torch.empty(B, m, dtype=torch.float16, device="cuda") for _ in range(world)]
-    em(xg, yg)  # warm-up outside capture (call 1)
+    em(xg, yg, fused=True)  # warm-up outside capture (call 1)
     torch.cuda.synchronize()
     g = torch.cuda.CUDAGraph()
     s = torch.cuda.Stream()
     s.wait_stream(torch.cuda.current_stream())
     with torch.cuda.stream(s):
         with torch.cuda.graph(g, stream=s):
-            em(xg, yg)
+            em(xg, yg, fused=True)
     torch.cuda.current_stream().wait_stream(s)
     torch.cuda.synchronize()
     calls = 1
