@@ -13,10 +13,10 @@ take o's output; down takes up's output in place of act(gate) * up).
 
 One GPU runs the layers unsharded.  N GPUs (torchrun, one process per GPU) run
 them column-sharded over output rows (TPQuantizedLinear: each rank decodes and
-multiplies its rows, pushes its float32 row shard into every rank's receive
-buffer over NVLink with a flag in peer memory, and every rank applies the full
-output transform to the gathered rows): strong scaling, the same tokens per
-step at every N.
+multiplies its rows, its matmul CTAs push the float32 row shard into every
+rank's receive buffer over NVLink as self-validating words, and every rank
+applies the full output transform to the gathered rows): strong scaling, the
+same tokens per step at every N.
 Each rank cycles over enough distinct weight copies that its weights exceed
 twice the 126 MB L2 (every weight read is an HBM read).
 
@@ -27,7 +27,8 @@ with the pinned host input copied in and the output copied back every step.
 roofline: the fused decode + matmul kernel of the set, timed alone.
 At one GPU the line also carries `decode_c2` (3-bit RVQ
 4096 -> 11008 at batch 1) and `prefill_c4` (Qwen2.5-7B MLP
-at 2048 tokens) sub-records.  `--impl reference` times the CPU port of the
+at 2048 tokens) sub-records, and with --breakdown the per-step timings of the
+layer set (transforms / matmuls / each layer's input and output step).  `--impl reference` times the CPU port of the
 reference algorithm (oracle/, numpy, all host cores) on the same workload.
 Prints one JSON line (rank 0).
 """
@@ -63,6 +64,8 @@ def parse():
                    help="layer-set passes per step (0: about 2k layer forwards per step at decode batches)")
     p.add_argument("--cpu-sample-s", type=float, default=20.0)
     p.add_argument("--no-extras", action="store_true", help="skip the decode_c2 / prefill_c4 sub-records")
+    p.add_argument("--breakdown", action="store_true",
+                   help="one GPU: add per-step timings of the layer set (input / matmul / output steps)")
     return p.parse_args()
 
 
@@ -191,12 +194,12 @@ def _two_pass_width(N):
 def kernels_per_forward(m, n, batch, sms, shards=1):
     """This library's kernel launches for one forward of an (n -> m) layer (m the full
     output width): input transform (two kernels for a two-pass RFFT width), matmul
-    (batches 9-32: one launch per 16 tokens), with shards > 1 the push of the row
-    shard to every rank, output transform (two kernels for a two-pass width; the
+    (batches 9-32: one launch per 16 tokens), with shards > 1 at prefill batches
+    the push of the row shard to every rank, output transform (two kernels for a two-pass width; the
     gathered output step of a sharded layer is one kernel)."""
     pow2 = lambda v: v & (v - 1) == 0
     matmul = 1 if batch >= 33 or batch <= 8 else math.ceil(batch / 16)
-    push = 1 if shards > 1 else 0
+    push = 1 if shards > 1 and batch >= 33 else 0  # decode batches: the matmul pushes
     if pow2(m) and pow2(n):
         return 1 + matmul + push + 1
     inp = 2 if _two_pass_width(n // 2) and (batch >= 33 or 2 * batch <= sms) else 1
@@ -476,6 +479,67 @@ def measure_set(ls, steps, warmup, stream, dev, world, passes, clocks=None):
                 h2d=x_host.numel() * x_host.element_size(), d2h=y_host.numel() * y_host.element_size())
 
 
+def breakdown(ls, dev):
+    """Where a decode step's time goes (one GPU): CUDA-graph replays of the whole
+    layer set, of its transform steps alone (input + output step of every layer),
+    of its matmuls alone (weights streamed from HBM: every copy of the set), and of
+    each layer's input and output step repeated.  Microseconds per layer set / step."""
+    import torch
+    from quipsharp_b200 import _native as N
+    B = ls.B
+    stream = torch.cuda.Stream(dev)
+
+    def timed(fn, R=20, reps=5):
+        with torch.cuda.stream(stream):
+            fn()
+            torch.cuda.synchronize(dev)
+            g = torch.cuda.CUDAGraph()
+            with torch.cuda.graph(g, stream=stream):
+                for _ in range(R):
+                    fn()
+            for _ in range(3):
+                g.replay()
+            torch.cuda.synchronize(dev)
+            e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            e0.record(stream)
+            for _ in range(reps):
+                g.replay()
+            e1.record(stream)
+            torch.cuda.synchronize(dev)
+        del g
+        return e0.elapsed_time(e1) * 1e3 / (reps * R)
+
+    xs = {n: torch.randn(B, n, device=dev).to(ls.dtype) for _, _, n in ls.layers}
+    y1s, wss, ys = {}, {}, {}
+    for li, (_, m, n) in enumerate(ls.layers):
+        y1s[li] = torch.zeros(B, m, device=dev)
+        wss[li] = ls.kernels(li, 0).input(xs[n], y1s[li])
+        ys[li] = torch.empty(B, m, dtype=ls.dtype, device=dev)
+    io = N.IO_DTYPES[ls.dtype]
+
+    def in_step(li, c):
+        k, n = ls.kernels(li, c), ls.layers[li][2]
+        N.check(N.lib().qs_linear_input(N.ptr(xs[n]), io, B, n, k.transform, N.ptr(k.sv), N.ptr(k.phase_v),
+                                        N.ptr(wss[li]), wss[li].numel(), N.ptr(y1s[li]), k.m, N.stream_of(xs[n])))
+
+    def out_step(li, c):
+        k = ls.kernels(li, c)
+        N.check(N.lib().qs_linear_output(N.ptr(y1s[li]), k.m, 1, B, k.m, k.transform, N.ptr(k.su), N.ptr(k.phase_u),
+                                         N.ptr(k.bias), N.ptr(ys[li]), io, N.stream_of(ys[li])))
+
+    L, nl = ls.L, len(ls.layers)
+    x0 = torch.randn(B, ls.layers[0][2], device=dev).to(ls.dtype)
+    out = {"us_layer_set": timed(lambda: [ls.forward(x0, c) for c in range(L)]) / L,
+           "us_transforms_only": timed(lambda: [(in_step(li, c), out_step(li, c))
+                                                for c in range(L) for li in range(nl)]) / L,
+           "us_matmuls_only": timed(lambda: [ls.kernels(li, c).matmul(wss[li], B, y1s[li])
+                                             for c in range(L) for li in range(nl)]) / L}
+    for li, (name, m, n) in enumerate(ls.layers):
+        out[f"us_input_{name}"] = timed(lambda: in_step(li, 0), R=50)
+        out[f"us_output_{name}"] = timed(lambda: out_step(li, 0), R=50)
+    return {k: round(v, 2) for k, v in out.items()}
+
+
 def default_passes(ls):
     if ls.prefill:
         return 1
@@ -577,8 +641,10 @@ def run_ours(args):
     sms = torch.cuda.get_device_properties(dev).multi_processor_count
     launches = args.steps * passes * ls.L * sum(kernels_per_forward(m, n, B, sms, world) for _, m, n in ls.layers)
     copies = ls.L
-    del ls
     extras = {}
+    if world == 1 and args.breakdown and not ls.prefill:
+        extras["breakdown"] = breakdown(ls, dev)
+    del ls
     if world == 1 and not args.no_extras:
         extras["decode_c2"] = sub_record_decode(dev, stream)
         extras["prefill_c4"] = sub_record_prefill(dev, stream)

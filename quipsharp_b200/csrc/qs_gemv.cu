@@ -48,8 +48,14 @@ struct GemvArgs {
   float *y1;               // (batch, m)
   int64_t m, RT, KC, n_pad, items;  // RT: 16-row tiles, KC: 32-code chunks
   int tok0, ntok;
-  TpPush push;  // world > 0: the CTAs push y1 to every rank after a grid barrier (tensor parallelism)
-  uint64_t wait_ns;  // bound of that barrier
+};
+
+// Tensor parallelism: the push of the finished y1 shard to every rank by all
+// CTAs after a grid barrier (a separate kernel instance: the one-GPU kernel
+// carries neither the arguments nor the tail, which measurably slowed it).
+struct GemvPush {
+  TpPush push;
+  uint64_t wait_ns;  // bound of the barrier
   int *error;        // set when it ran out
 };
 
@@ -309,8 +315,7 @@ __device__ __forceinline__ void gemv_items(const GemvArgs &a, const uint8_t *tbl
 }
 
 template <int K0, int K1, int NST, int NTG>
-__global__ void __launch_bounds__(kGemvThreads, NTG == 1 ? 2 : 1) gemv_kernel(GemvArgs a) {
-  extern __shared__ __align__(256) uint8_t gsm[];
+__device__ __forceinline__ void gemv_body(const GemvArgs &a, uint8_t *gsm) {
   pdl_launch_dependents();
   // 256-byte aligned table rows: the row index is multiplied by 256 and the
   // lane replica offset (< 256) added in one integer multiply-add
@@ -326,7 +331,20 @@ __global__ void __launch_bounds__(kGemvThreads, NTG == 1 ? 2 : 1) gemv_kernel(Ge
   load_table(tbl);
   __syncthreads();
   if (start < end) gemv_items<K0, K1, NST, NTG>(a, tbl, start, end, q, nq);
-  if (a.push.world) tp_push_grid(a.push, a.wait_ns, a.error);  // every thread of every CTA arrives
+}
+
+template <int K0, int K1, int NST, int NTG>
+__global__ void __launch_bounds__(kGemvThreads, NTG == 1 ? 2 : 1) gemv_kernel(GemvArgs a) {
+  extern __shared__ __align__(256) uint8_t gsm[];
+  gemv_body<K0, K1, NST, NTG>(a, gsm);
+}
+
+template <int K0, int K1, int NST, int NTG>
+__global__ void __launch_bounds__(kGemvThreads, NTG == 1 ? 2 : 1) gemv_push_kernel(GemvArgs a, GemvPush p) {
+  extern __shared__ __align__(256) uint8_t gsm[];
+  gemv_body<K0, K1, NST, NTG>(a, gsm);
+  // every thread of every CTA arrives; the broadcast word sits past the table
+  tp_push_grid(p.push, p.wait_ns, p.error, reinterpret_cast<unsigned *>(gsm + kTblBytes + 256));
 }
 
 static int num_sms() {
@@ -345,7 +363,9 @@ static int run_gemv(GemvArgs &a, int64_t batch, cudaStream_t s, const TpPush *pu
   // batches above 8: passes of 16 tokens (two token groups); else one pass of 8
   const bool two = batch > 8;
   auto kern = two ? gemv_kernel<K0, K1, NST, 2> : gemv_kernel<K0, K1, NST, 1>;
+  auto kpush = two ? gemv_push_kernel<K0, K1, NST, 2> : gemv_push_kernel<K0, K1, NST, 1>;
   QS_CUDA_TRY(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, kTblBytes + 256));
+  if (push) QS_CUDA_TRY(cudaFuncSetAttribute(kpush, cudaFuncAttributeMaxDynamicSharedMemorySize, kTblBytes + 512));
   const int per_pass = two ? 16 : 8;
   const int64_t warps_needed = a.items;
   int grid = (two ? 1 : 2) * num_sms();
@@ -354,13 +374,15 @@ static int run_gemv(GemvArgs &a, int64_t batch, cudaStream_t s, const TpPush *pu
   for (int64_t tok0 = 0; tok0 < batch; tok0 += per_pass) {
     a.tok0 = static_cast<int>(tok0);
     a.ntok = static_cast<int>(batch - tok0 < per_pass ? batch - tok0 : per_pass);
+    int st;
     if (push && tok0 + per_pass >= batch) {  // the last pass pushes every token's rows
-      a.push = *push;
-      a.wait_ns = pipeline_wait_ns();
-      a.error = device_error_flag();
-      if (!a.error) return fail(QS_ERR_CUDA, "device error flag unavailable");
+      GemvPush p{*push, pipeline_wait_ns(), device_error_flag()};
+      if (!p.error) return fail(QS_ERR_CUDA, "device error flag unavailable");
+      // table (256-byte aligned inside the first 256 + kTblBytes bytes), then the push's word
+      st = launch_pdl("gemv_push", kpush, dim3(grid), dim3(kGemvThreads), kTblBytes + 512, s, a, p);
+    } else {
+      st = launch_pdl("gemv", kern, dim3(grid), dim3(kGemvThreads), kTblBytes + 256, s, a);
     }
-    int st = launch_pdl("gemv", kern, dim3(grid), dim3(kGemvThreads), kTblBytes + 256, s, a);
     if (st) return st;
   }
   return QS_OK;

@@ -79,8 +79,10 @@ __device__ __forceinline__ void tp_announce(const TpPush &a, unsigned seq) {
 // pushes its 1/grid slice of it, so the copy runs on all SMs at once; the last
 // CTA to finish (count ctl[2]) records the call's sequence number and resets
 // the counts.  Every CTA read the old sequence number before arriving.
-__device__ __forceinline__ void tp_push_grid(const TpPush &a, uint64_t wait_ns, int *error) {
-  __shared__ unsigned s_seq;
+// s_seq: a shared-memory word of the caller's (its own allocation, so the
+// caller's shared-memory layout stays as it is without a push).
+__device__ __forceinline__ void tp_push_grid(const TpPush &a, uint64_t wait_ns, int *error, unsigned *s_seq_slot) {
+  unsigned &s_seq = *s_seq_slot;
   __syncthreads();
   if (threadIdx.x == 0) {
     const unsigned seq = *reinterpret_cast<volatile unsigned *>(a.ctl) + 1u;

@@ -977,8 +977,11 @@ struct XPeerGather {
 };
 
 // Where an output step reads y1 from: the kernel's own y1 (plain floats) or a
-// receive region.  A reader that gives up (wait limit) marks itself dead and
-// reads zeros from then on; the error flag tells the host.
+// receive region.  In word format value i is word i: base[2 i] holds its bits
+// and base[2 i + 1] the call number.  The decode-batch row kernels verify a
+// thread's words with batched loads before plain reads (verify, get); the
+// general row engine waits per word where it reads (get_wait).  A reader that gives up (wait limit)
+// stops waiting and the error flag tells the host the output is invalid.
 struct XPeerSrc {
   const float *base;
   unsigned seq;
@@ -995,33 +998,65 @@ struct XPeerSrc {
     dead = true;
     return true;
   }
-  __device__ __forceinline__ float get(int64_t i, bool &dead) const {
-    if (!base || dead) return 0.f;
-    if (!words) return base[i];
-    const uint32_t *w = reinterpret_cast<const uint32_t *>(base) + 2 * i;
+  // word i, loaded without waiting: {bits, call number}
+  __device__ __forceinline__ uint2 load_word(int64_t i) const {
+    uint2 w;
+    asm volatile("ld.volatile.global.v2.u32 {%0, %1}, [%2];" : "=r"(w.x), "=r"(w.y) : "l"(base + 2 * i) : "memory");
+    return w;
+  }
+  // waits (bounded) until word i holds this call; returns its value
+  __device__ __forceinline__ float wait_word(int64_t i, uint2 w, bool &dead) const {
     uint64_t t0 = 0;
-    for (;;) {
-      uint32_t v, sq;
-      asm volatile("ld.volatile.global.v2.u32 {%0, %1}, [%2];" : "=r"(v), "=r"(sq) : "l"(w) : "memory");
-      if (sq == seq) return __uint_as_float(v);
-      if (expired(t0, dead)) return 0.f;
+    while (w.y != seq && !dead && !expired(t0, dead)) w = load_word(i);
+    return dead ? 0.f : __uint_as_float(w.x);
+  }
+  // Word format: waits until the words off(r) (and off(r) + 1 with pair), r < R,
+  // hold this call.  The call-number halves of up to 16 values are loaded
+  // together; only words not yet arrived are waited on.
+  template <int R, typename Off>
+  __device__ __forceinline__ void verify(Off off, bool pair) const {
+    constexpr int kChunk = R < 16 ? R : 16;
+    bool dead = false;
+#pragma unroll 1
+    for (int r0 = 0; r0 < R; r0 += kChunk) {
+      uint32_t miss = 0;
+#pragma unroll
+      for (int j = 0; j < kChunk; ++j) {
+        const float *w = base + 2 * off(r0 + j);
+        uint32_t s0, s1 = seq;
+        asm volatile("ld.volatile.global.u32 %0, [%1];" : "=r"(s0) : "l"(w + 1) : "memory");
+        if (pair) asm volatile("ld.volatile.global.u32 %0, [%1];" : "=r"(s1) : "l"(w + 3) : "memory");
+        if (s0 != seq || s1 != seq) miss |= 1u << j;
+      }
+      if (!miss) continue;
+      const uint2 stale = make_uint2(0u, seq + 1u);  // forces a fresh load
+#pragma unroll
+      for (int j = 0; j < kChunk; ++j)
+        if ((miss >> j) & 1u) {
+          wait_word(off(r0 + j), stale, dead);
+          if (pair) wait_word(off(r0 + j) + 1, stale, dead);
+        }
     }
   }
-  // values i, i + 1 (i even)
-  __device__ __forceinline__ float2 get2(int64_t i, bool &dead) const {
-    if (!base || dead) return make_float2(0.f, 0.f);
+  // value i of the word format, waiting (bounded) for its word
+  __device__ __forceinline__ float get_wait(int64_t i, bool &dead) const {
+    if (!base || dead) return 0.f;
+    return wait_word(i, load_word(i), dead);
+  }
+  __device__ __forceinline__ float2 get2_wait(int64_t i, bool &dead) const {  // i even
+    const float x = get_wait(i, dead);
+    return make_float2(x, get_wait(i + 1, dead));
+  }
+  // value i (plain floats, or a verified word, read from L2); no base: zeros
+  __device__ __forceinline__ float get(int64_t i) const {
+    if (!base) return 0.f;
+    return words ? __ldcg(base + 2 * i) : base[i];
+  }
+  __device__ __forceinline__ float2 get2(int64_t i) const {  // values i, i + 1 (i even)
+    if (!base) return make_float2(0.f, 0.f);
     if (!words) return *reinterpret_cast<const float2 *>(base + i);
-    const uint32_t *w = reinterpret_cast<const uint32_t *>(base) + 2 * i;
-    uint64_t t0 = 0;
-    for (;;) {
-      uint32_t v0, s0, v1, s1;
-      asm volatile("ld.volatile.global.v4.u32 {%0, %1, %2, %3}, [%4];"
-                   : "=r"(v0), "=r"(s0), "=r"(v1), "=r"(s1)
-                   : "l"(w)
-                   : "memory");
-      if (s0 == seq && s1 == seq) return make_float2(__uint_as_float(v0), __uint_as_float(v1));
-      if (expired(t0, dead)) return make_float2(0.f, 0.f);
-    }
+    const float4 q = __ldcg(reinterpret_cast<const float4 *>(base + 2 * i));
+    return make_float2(q.x, q.z);
   }
 };
 
@@ -1233,7 +1268,10 @@ __global__ void __launch_bounds__(kXMaxThreads, 1) xoutput_rfft_kernel(
   pdl_wait();  // y1 comes from the matmul (or the all-gather, or the ranks' pushes)
   const XPeerSrc src = ra.pg.flags ? xwait_peers(ra.pg) : xplain_src(y1);
   bool dead = false;
-  auto gsrc = [&](int e) { return src.get2(xy1_offset(row, 2 * e, ld_y1, shards, mp, batch), dead); };
+  auto gsrc = [&](int e) {
+    const int64_t off = xy1_offset(row, 2 * e, ld_y1, shards, mp, batch);
+    return src.words ? src.get2_wait(off, dead) : src.get2(off);
+  };
   auto sink = [&](int e, float2 z) {
     z.x *= scale;
     z.y *= scale;
@@ -1359,7 +1397,10 @@ __global__ void __launch_bounds__(kXMaxThreads, 1) xoutput_rht_kernel(
   pdl_wait();  // y1 comes from the matmul (or the all-gather, or the ranks' pushes)
   const XPeerSrc src = ra.pg.flags ? xwait_peers(ra.pg) : xplain_src(y1);
   bool dead = false;
-  auto gsrc = [&](int i) { return src.get(xy1_offset(row, i, ld_y1, shards, mp, batch), dead); };
+  auto gsrc = [&](int i) {
+    const int64_t off = xy1_offset(row, i, ld_y1, shards, mp, batch);
+    return src.words ? src.get_wait(off, dead) : src.get(off);
+  };
   auto sink = [&](int i, float v) {
     v = v * scale * su[i];
     if (bias) v += bias[i];

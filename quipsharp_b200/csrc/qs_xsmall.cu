@@ -192,33 +192,41 @@ struct SmallOut {
 };
 
 template <int LV, int LW>
-__global__ void __launch_bounds__(32 << LW) xsmall_output_rht_kernel(SmallOut a) {
+__global__ void __maxnreg__(128) xsmall_output_rht_kernel(SmallOut a) {  // 512 threads at most
   constexpr int V = 1 << LV, W = 1 << LW, m = 32 * V * W;
   extern __shared__ float sm_small[];
   const int64_t row = blockIdx.x;
   const bool flag = row == 0 && threadIdx.x == 0;
   if (flag) xbusy_set(a.busy, 1);  // before the release: the next input step reads it at its start
   pdl_launch_dependents();
-  float sg[V], bb[V];
+  constexpr bool kBiasEarly = V <= 16;  // registers: 32 points per thread leave no room for the bias
+  float sg[V], bb[kBiasEarly ? V : 1];
 #pragma unroll
   for (int j = 0; j < V / W; ++j)
 #pragma unroll
     for (int k = 0; k < W; ++k) {
       const int i = point_b<LV, LW>(j, k);
       sg[j * W + k] = __ldg(a.su + i) * a.scale;  // layer constants
-      bb[j * W + k] = a.bias ? __ldg(a.bias + i) : 0.f;
+      if constexpr (kBiasEarly) bb[j * W + k] = a.bias ? __ldg(a.bias + i) : 0.f;
     }
   pdl_wait();  // y1 comes from the matmul (or the ranks' pushes)
   const XPeerSrc src = a.pg.flags ? xwait_peers(a.pg) : xplain_src(a.y1);
-  bool dead = false;
-  float v[V];
-#pragma unroll
-  for (int r = 0; r < V; ++r) {
+  auto off = [&](int r) -> int64_t {
     const int i = point_a<LV>(r);
-    int64_t off;
-    if (a.shard_log2 < 0) off = row * a.ld_y1 + i;
-    else off = ((static_cast<int64_t>(i >> a.shard_log2) * a.batch + row) << a.shard_log2) + (i & ((1 << a.shard_log2) - 1));
-    v[r] = src.get(off, dead);
+    if (a.shard_log2 < 0) return row * a.ld_y1 + i;
+    return ((static_cast<int64_t>(i >> a.shard_log2) * a.batch + row) << a.shard_log2) + (i & ((1 << a.shard_log2) - 1));
+  };
+  float v[V];
+  if (!src.base) {
+#pragma unroll
+    for (int r = 0; r < V; ++r) v[r] = 0.f;
+  } else if (src.words) {  // verified words, read from L2
+    src.verify<V>(off, false);
+#pragma unroll
+    for (int r = 0; r < V; ++r) v[r] = __ldcg(src.base + 2 * off(r));
+  } else {
+#pragma unroll
+    for (int r = 0; r < V; ++r) v[r] = src.base[off(r)];
   }
   fwht_row_small<LV, LW>(v, sm_small);
 #pragma unroll
@@ -226,7 +234,10 @@ __global__ void __launch_bounds__(32 << LW) xsmall_output_rht_kernel(SmallOut a)
 #pragma unroll
     for (int k = 0; k < W; ++k) {
       const int i = point_b<LV, LW>(j, k);
-      store_from_float(a.y, row * m + i, a.dtype, fmaf(v[j * W + k], sg[j * W + k], bb[j * W + k]));
+      float b;
+      if constexpr (kBiasEarly) b = bb[j * W + k];
+      else b = a.bias ? __ldg(a.bias + i) : 0.f;
+      store_from_float(a.y, row * m + i, a.dtype, fmaf(v[j * W + k], sg[j * W + k], b));
     }
   if (flag) xbusy_set(a.busy, 0);
 }
@@ -345,14 +356,17 @@ template <int LV, int LW, bool INV>
 struct FftRow {
   static constexpr int V = 1 << LV, W = 1 << LW, T = 32 * W, N = T * V, LN = 5 + LV + LW;
   static constexpr int kStage = N + N / (V * W);  // staging slots (padded)
-  float2 t1[V];  // w_N^{t k_r}, by register position p (k_r = bitrev(p))
+  // w_N^{t k_r}, by register position p (k_r = bitrev(p)); with 32 points per
+  // thread they are loaded where used (registers)
+  static constexpr bool kT1Early = V <= 16;
+  float2 t1[kT1Early ? V : 1];
   float2 t3[W];  // w_N^{V lane k_w}, by position q (k_w = bitrev(q))
   float2 tl[5];  // lane stages: w_{2m}^{lane mod m}, m = 16, 8, 4, 2, 1
 
   __device__ __forceinline__ void prefetch_twiddles() {
     const int lane = threadIdx.x & 31, t = threadIdx.x;
 #pragma unroll
-    for (int p = 0; p < V; ++p) t1[p] = twiddle_pinned<INV>((t * bitrev(p, LV)) & (N - 1), LN);
+    for (int p = 0; p < (kT1Early ? V : 0); ++p) t1[p] = twiddle_pinned<INV>((t * bitrev(p, LV)) & (N - 1), LN);
 #pragma unroll
     for (int q = 0; q < W; ++q) t3[q] = twiddle_pinned<INV>((V * lane * bitrev(q, LW)) & (N - 1), LN);
 #pragma unroll
@@ -370,7 +384,12 @@ struct FftRow {
     const int lane = threadIdx.x & 31, w = threadIdx.x >> 5;
     dft_regs<V, INV>(v);
 #pragma unroll
-    for (int p = 1; p < V; ++p) v[p] = cmul(v[p], t1[p]);
+    for (int p = 1; p < V; ++p) {
+      float2 tw;
+      if constexpr (kT1Early) tw = t1[p];
+      else tw = twiddle<INV>((static_cast<int>(threadIdx.x) * bitrev(p, LV)) & (N - 1), LN);
+      v[p] = cmul(v[p], tw);
+    }
 #pragma unroll
     for (int p = 0; p < V; ++p) sm[lane + 32 * (w + W * bitrev(p, LV))] = v[p];
     __syncthreads();
@@ -512,15 +531,25 @@ __global__ void __launch_bounds__(32 << LW) xsmall_output_rfft_kernel(SmallOutF 
   }
   pdl_wait();  // y1 comes from the matmul (or the ranks' pushes)
   const XPeerSrc src = a.pg.flags ? xwait_peers(a.pg) : xplain_src(a.y1);
-  bool dead = false;
-  float2 v[V];
-#pragma unroll
-  for (int r = 0; r < V; ++r) {
+  auto off = [&](int r) -> int64_t {
     const int c = 2 * (t + T * r);  // real index of the complex point's first half
-    int64_t off;
-    if (a.shard_log2 < 0) off = row * a.ld_y1 + c;
-    else off = ((static_cast<int64_t>(c >> a.shard_log2) * a.batch + row) << a.shard_log2) + (c & ((1 << a.shard_log2) - 1));
-    v[r] = src.get2(off, dead);
+    if (a.shard_log2 < 0) return row * a.ld_y1 + c;
+    return ((static_cast<int64_t>(c >> a.shard_log2) * a.batch + row) << a.shard_log2) + (c & ((1 << a.shard_log2) - 1));
+  };
+  float2 v[V];
+  if (!src.base) {
+#pragma unroll
+    for (int r = 0; r < V; ++r) v[r] = make_float2(0.f, 0.f);
+  } else if (src.words) {  // verified words, read from L2
+    src.verify<V>(off, true);
+#pragma unroll
+    for (int r = 0; r < V; ++r) {
+      const float4 q = __ldcg(reinterpret_cast<const float4 *>(src.base + 2 * off(r)));
+      v[r] = make_float2(q.x, q.z);
+    }
+  } else {
+#pragma unroll
+    for (int r = 0; r < V; ++r) v[r] = *reinterpret_cast<const float2 *>(src.base + off(r));
   }
   f.run(v, smf_small, stage);
   __syncthreads();
