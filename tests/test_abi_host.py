@@ -114,3 +114,36 @@ def test_quantized_linear_state_dict_keys_match_reference():
     r = QuantizedLinear(48, 40, 8, "rfft")
     assert set(r.state_dict()) == {"codes", "scale", "phase_u", "phase_v"}
     assert r.phase_u.dtype == torch.complex64 and r.phase_u.shape == (20,)
+
+
+def test_tp_peers_struct_matches_the_header(tmp_path):
+    """The ctypes mirror of qs_tp_peers has the C layout of include/quipsharp_b200.h
+    (compiled here with the host compiler), and the exchange allocation's layout
+    helpers give 16-byte aligned control words after the padded flags."""
+    import shutil
+    import subprocess
+    from quipsharp_b200.tensor_parallel import exchange_floats, ctl_offset, make_peers
+    cc = shutil.which("gcc") or shutil.which("cc")
+    if cc is None:
+        pytest.skip("no host C compiler")
+    src = tmp_path / "peers.c"
+    src.write_text(
+        '#include <stdio.h>\n#include <stddef.h>\n#include "quipsharp_b200.h"\n'
+        "int main(void) {\n"
+        '  printf("%zu %zu %zu %zu %zu %zu %d\\n", sizeof(qs_tp_peers), offsetof(qs_tp_peers, rank),\n'
+        "         offsetof(qs_tp_peers, recv), offsetof(qs_tp_peers, flags), offsetof(qs_tp_peers, ctl),\n"
+        "         offsetof(qs_tp_peers, recv_floats), QS_TP_MAX_RANKS);\n"
+        "  return 0;\n}\n")
+    exe = tmp_path / "peers"
+    subprocess.run([cc, "-I", os.path.join(ROOT, "include"), str(src), "-o", str(exe)], check=True)
+    got = [int(v) for v in subprocess.run([str(exe)], check=True, capture_output=True, text=True).stdout.split()]
+    P = N.TPPeers
+    assert got == [ctypes.sizeof(P), P.rank.offset, P.recv.offset, P.flags.offset, P.ctl.offset,
+                   P.recv_floats.offset, N.QS_TP_MAX_RANKS]
+    for world in range(1, 9):
+        cap = 1 << 16
+        assert (ctl_offset(cap, world) * 4) % 16 == 0 and ctl_offset(cap, world) >= 2 * cap + 2 * world
+        assert exchange_floats(cap, world) == ctl_offset(cap, world) + 4
+        bases = [0x10000 * (r + 1) * 4096 for r in range(world)]
+        pe = make_peers(world, world - 1, bases, cap)
+        assert pe.flags[0] == bases[0] + 2 * cap * 4 and pe.ctl == bases[-1] + ctl_offset(cap, world) * 4
