@@ -286,8 +286,9 @@ int qs_linear_fwd_tp(const void *x, int x_dtype, int64_t batch, int64_t n, int64
 int qs_tp_push(const qs_tp_peers *peers, const float *y1, int64_t batch, int64_t m_local,
                qs_stream_t stream);
 /* qs_linear_matmul followed by qs_tp_push of its y1 shard, fused for batches
- * of at most 32 tokens (the matmul's last CTA to finish pushes the shard and
- * announces it, saving a kernel); larger batches run the two in sequence. */
+ * of at most 32 tokens (after a grid barrier every CTA of the matmul pushes its
+ * slice of the shard as self-validating words, saving a kernel); larger
+ * batches run the two in sequence. */
 int qs_linear_matmul_tp(const void *x2_workspace, int64_t batch, int64_t n, int64_t m_local,
                         const void *packed, int stages, const int *kinds, const float *stage_scales,
                         const float *layer_scale, float *y1, const qs_tp_peers *peers,

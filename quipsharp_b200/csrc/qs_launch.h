@@ -91,7 +91,7 @@ int launch_pack(const int16_t *codes, int stages, const int *kinds, int64_t m, i
 
 // qs_gemv.cu: fused decode + matmul; batches below kTcMinBatch run the
 // decode-regime kernel of this file, larger ones launch_matmul_tc.  push
-// (decode batches only): the grid's last CTA pushes y1 to every rank.
+// (decode batches only): after a grid barrier the CTAs push y1 to every rank.
 int launch_matmul(const void *x2ws, int64_t batch, int64_t n, int64_t m, const void *packed,
                   int stages, const int *kinds, const float *stage_scales,
                   const float *layer_scale, float *y1, cudaStream_t s, const TpPush *push = nullptr);

@@ -4,20 +4,23 @@
 //   1. input step: x -> x2 (local workspace); zero the private y1 shard
 //      (decode batches: the matmul accumulates into it);
 //   2. fused decode + matmul of the local rows into the private y1 (batch, m/P);
-//   3. push: copy y1 into every rank's receive buffer (remote stores over the
+//   3. push of y1 into every rank's receive buffer (remote stores over the
 //      interconnect; this rank's own copy is a local store) at the rank-major
-//      gathered position of this rank's shard, in the parity region of the
-//      call's sequence number s; then, after a system-scope fence, store s into
-//      flag [s & 1][this rank] of every rank (release);
-//   4. output step: wait (bounded) until this rank's flags [s & 1][0..P) all
-//      hold s, then read the gathered y1 locally and apply the full-width output
-//      transform, signs / conjugate phases, bias and cast.
-// The sequence number lives in device memory (incremented by the last CTA of
-// each push kernel), so CUDA graphs holding any number of calls replay in any
-// order with eager calls.  Two regions suffice: a rank pushes call s + 2 only
-// after its own output step of call s + 1, which saw every rank's call-s+1
-// push, which each rank issues after its output step of call s (stream order)
-// -- so nobody still reads region s & 1.
+//      gathered position of this rank's shard, in the region of the call's
+//      sequence number s (s & 1):
+//      * decode batches: by the matmul itself (gemv_push_kernel): after a grid
+//        barrier every CTA stores its slice as 8-byte words {value, s} (qs_tp.cuh);
+//      * prefill batches: tp_push_kernel stores plain floats, then after a
+//        system-scope fence stores s into flag [s & 1][this rank] of every rank;
+//   4. output step: reads the gathered y1 once it has arrived (words: each word
+//      holds s; flags: every flag [s & 1][0..P) holds s; bounded waits) and
+//      applies the full-width output transform, signs / phases, bias and cast.
+// The sequence number lives in device memory (recorded by the last CTA of each
+// push), so CUDA graphs holding any number of calls replay in any order with
+// eager calls.  Two regions suffice: a rank pushes call s + 2 only after its own
+// output step of call s + 1, which saw every rank's call-s+1 data, which each
+// rank pushes after its output step of call s (stream order) -- so nobody
+// still reads region s & 1.
 #include <cuda.h>
 
 #include <cstring>
@@ -167,7 +170,7 @@ int launch_matmul_tp(const void *x2ws, int64_t batch, int64_t n, int64_t m_local
     int st = launch_matmul(x2ws, batch, n, m_local, packed, stages, kinds, stage_scales, layer_scale, y1, s);
     return st ? st : launch_tp_push(pe, y1, batch, m_local, s);
   }
-  TpPush push;  // the decode matmul's last CTA pushes the shard
+  TpPush push;  // the decode matmul's CTAs push the shard after a grid barrier
   int st = make_push(pe, y1, batch, m_local, push);
   return st ? st : launch_matmul(x2ws, batch, n, m_local, packed, stages, kinds, stage_scales, layer_scale, y1, s, &push);
 }

@@ -1,6 +1,6 @@
 // Push of a column-sharded layer's y1 shard to every rank (tensor parallelism
 // over peer memory; see qs_tp.cu): the descriptor and the device routines that
-// the push kernel and the decode matmul's last CTA share.
+// the push kernel and the decode matmul's push tail share.
 //
 // Two receive formats:
 //  * flagged (prefill batches): plain floats, then after a system-scope fence

@@ -4,7 +4,8 @@ Rank r of P holds weight rows [r*m/P, (r+1)*m/P) (its slice of `codes`).  A
 forward runs, on every rank, the input transform of the full activations, the
 fused decode + matmul of the local rows into a private float32 y1 shard, a push
 of the shard into every rank's receive buffer over NVLink (decode batches: by
-the matmul's last CTA, as 8-byte words that carry the call's sequence number, so
+every CTA of the matmul after a grid barrier, as 8-byte words that carry the
+call's sequence number, so
 no fence or flag is needed; prefill batches: a push kernel, then a flag in every
 rank's memory), and the output transform, which reads the gathered y1 locally
 once it has arrived (no collective library call on the data path).  Every rank ends with the full output, ready for the next

@@ -1,11 +1,12 @@
 """The peer-memory exchange of column-sharded tensor parallelism on ONE GPU.
 
 P ranks are emulated in one process on one stream: each rank's exchange
-allocation is an ordinary device buffer, and every "rank" runs input step,
-matmul of its row shard and qs_tp_push, or the fused qs_linear_matmul_tp, (stores into all ranks' receive buffers
-plus flags) before any rank runs qs_linear_output_peers.  Kernels therefore run
-strictly one after another, so no kernel ever waits for one that has not been
-launched; every output step finds its flags already set.  This checks the
+allocation is an ordinary device buffer, and every "rank" runs the input step,
+the matmul of its row shard and the push (qs_tp_push after qs_linear_matmul, or
+the fused qs_linear_matmul_tp), which stores into all ranks' receive buffers,
+before any rank runs qs_linear_output_peers.  Kernels therefore run strictly one
+after another, so no kernel ever waits for one that has not been launched;
+every output step finds its data already there.  This checks the
 gathered layout, the device-side call counter that picks the receive region,
 and CUDA graph replay in any mix with direct calls, for P = 2, 4, 8; the
 multi-process path over NVLink is covered by test_gpu_tp.py."""
@@ -50,8 +51,8 @@ class Emulated:
 
     def __call__(self, x, ys, fused=False):
         """One call of every rank; ys[r] receives rank r's full output.  fused: the
-        matmul's last CTA pushes (qs_linear_matmul_tp), else qs_linear_matmul then
-        qs_tp_push."""
+        matmul's CTAs push after a grid barrier (qs_linear_matmul_tp), else
+        qs_linear_matmul then qs_tp_push."""
         import ctypes
         N = self.N
         B = x.shape[0]
