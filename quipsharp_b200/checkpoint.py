@@ -196,15 +196,13 @@ def is_quantized_checkpoint(path) -> bool:
 
 
 def _meta_skeleton(model_id: str) -> nn.Module:
-    """The architecture of `model_id` on the meta device (no weights), as
-    lazy_weights.py:149-179 builds it; needs the model's config locally (a
+    """The architecture of `model_id` with its parameters on the meta device and
+    its computed buffers real (lazy_weights.build_meta_model, as
+    checkpoint.py:206-209 uses it); needs the model's config locally (a
     directory or the Hugging Face cache: there is no download here)."""
     try:
-        from transformers import AutoConfig, AutoModelForCausalLM
-        full = AutoConfig.from_pretrained(model_id)
-        dtype = getattr(full, "dtype", None) or getattr(full, "torch_dtype", None) or torch.bfloat16
-        with torch.device("meta"):
-            return AutoModelForCausalLM.from_config(full.get_text_config(), dtype=dtype)
+        from .lazy_weights import build_meta_model
+        return build_meta_model(model_id)[0]
     except Exception as e:  # no transformers, no local config, unknown architecture
         raise RuntimeError(f"cannot build the architecture of {model_id!r} ({e}); pass model= "
                            "(a skeleton whose quantized submodules will be replaced)") from e
