@@ -11,7 +11,10 @@ taking the latest earlier output of its input width (q takes the layer input;
 k, v and o take q's output in place of the attention input / output; gate and up
 take o's output; down takes up's output in place of act(gate) * up).
 
-One GPU runs the layers unsharded.  N GPUs (torchrun, one process per GPU) run
+One GPU runs the layers unsharded; layers that read one input (k, v, o here,
+as q, k, v in a decoder; gate and up) run as one group (groups.LinearGroup:
+qs_linear_fwd_group overlaps their kernels on forked streams; --groups off
+runs each layer's forward in turn).  N GPUs (torchrun, one process per GPU) run
 them column-sharded over output rows (TPQuantizedLinear: each rank decodes and
 multiplies its rows, its matmul CTAs push the float32 row shard into every
 rank's receive buffer over NVLink as self-validating words, and every rank
@@ -64,6 +67,9 @@ def parse():
                    help="layer-set passes per step (0: about 2k layer forwards per step at decode batches)")
     p.add_argument("--cpu-sample-s", type=float, default=20.0)
     p.add_argument("--no-extras", action="store_true", help="skip the decode_c2 / prefill_c4 sub-records")
+    p.add_argument("--groups", default="on", choices=["on", "off"],
+                   help="one GPU: run the layers that read one input as one group (groups.LinearGroup); "
+                        "off: each layer's forward in turn")
     p.add_argument("--breakdown", action="store_true",
                    help="one GPU: add per-step timings of the layer set (input / matmul / output steps)")
     return p.parse_args()
@@ -324,9 +330,10 @@ def make_full_module(name, m, n, kinds, li, copy_id, dev, chained):
 class LayerSet:
     """Copies of a config's layer set on this rank (sharded when world > 1)."""
 
-    def __init__(self, config, batch, dev, world, rank, copies=None):
+    def __init__(self, config, batch, dev, world, rank, copies=None, groups=False):
         import torch
         from quipsharp_b200 import _native as N
+        from quipsharp_b200.groups import LinearGroup
         from quipsharp_b200.tensor_parallel import TPQuantizedLinear
         self.layers, self.kinds, self.dtype = config_spec(config)
         self.config, self.B, self.dev, self.world = config, batch, dev, world
@@ -351,12 +358,33 @@ class LayerSet:
                     full.kernel()  # pack once, outside every timed region
                     row.append(full)
             self.mods.append(row)
+        # layers that read one input run as one group (one GPU only: the tensor-
+        # parallel matmuls wait on a grid barrier and must not share the GPU)
+        self.group_of = {}  # first member -> member indices
+        if groups and world == 1:
+            by_src = {}
+            for li, s in enumerate(self.src):
+                by_src.setdefault(s, []).append(li)
+            self.group_of = {members[0]: members for members in by_src.values() if len(members) > 1}
+        self.groups = [{first: LinearGroup([row[j] for j in members]) for first, members in self.group_of.items()}
+                       for row in self.mods]
         torch.cuda.synchronize(dev)
 
+    def group_names(self):
+        return [[self.layers[j][0] for j in members] for members in self.group_of.values()]
+
     def forward(self, x, copy):
-        outs = []
+        outs = [None] * len(self.layers)
         for li, mod in enumerate(self.mods[copy]):
-            outs.append(mod(x if self.src[li] < 0 else outs[self.src[li]]))
+            if outs[li] is not None:  # computed with its group
+                continue
+            inp = x if self.src[li] < 0 else outs[self.src[li]]
+            members = self.group_of.get(li)
+            if members:
+                for j, y in zip(members, self.groups[copy][li](inp)):
+                    outs[j] = y
+            else:
+                outs[li] = mod(inp)
         return outs[-1]
 
     def kernels(self, li, copy):
@@ -596,7 +624,8 @@ def run_ours(args):
     stream = torch.cuda.Stream(dev)
     hbm, burst, sust, peak_src = measured_peaks()
 
-    ls = LayerSet(args.config, args.batch, dev, world, rank)
+    ls = LayerSet(args.config, args.batch, dev, world, rank, groups=args.groups == "on")
+    group_names = ls.group_names()
     passes = args.passes or default_passes(ls)
     clk = ClockSampler(local)
     r = measure_set(ls, args.steps, args.warmup, stream, dev, world, passes, clocks=clk)
@@ -660,6 +689,7 @@ def run_ours(args):
             "config": {"workload": args.config, "batch": B, "layers": [list(l) for l in layers], "kinds": list(kinds),
                        "parallelism": f"tp{world} (column-sharded output rows)" if world > 1 else "single GPU",
                        "layer_sets_per_step": sets,
+                       "linear_groups": group_names or None,
                        "distinct_copies_per_rank": copies,
                        "l2": "inputs larger than L2: distinct weight copies cycled so each rank streams more than "
                              "2 x 126 MB per pass" if B < 33 else
@@ -671,9 +701,10 @@ def run_ours(args):
             "cpu_baseline": cpu,
             "e2e": {"value": tokens / (r["ms_e2e"] / 1e3), "unit": "tokens/s", "h2d_bytes_per_step": r["h2d"],
                     "d2h_bytes_per_step": r["d2h"],
-                    "path": "QuantizedLinear.forward (TPQuantizedLinear.forward at N > 1) called eagerly from "
-                            "Python over the layer set x passes per step; pinned host input copied in and the last "
-                            "layer's output copied out each step"},
+                    "path": "QuantizedLinear.forward (TPQuantizedLinear.forward at N > 1; LinearGroup.forward "
+                            "for the layers of a linear group) called eagerly from Python over the layer set x "
+                            "passes per step; pinned host input copied in and the last layer's output copied out "
+                            "each step"},
             "e2e_graph": {"value": tokens / (r["ms_e2e_graph"] / 1e3), "unit": "tokens/s",
                           "path": "the same step captured once as a CUDA graph and replayed"},
             "gpu_launches": launches,

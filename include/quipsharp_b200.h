@@ -170,6 +170,44 @@ int qs_linear_fwd_noalloc(const void *x, int x_dtype, int64_t batch, int64_t n, 
                           const float *su, const float *sv, const void *phase_u,
                           const void *phase_v, const float *bias, void *y, qs_stream_t stream);
 
+/* One layer of qs_linear_fwd_group: the arguments of qs_linear_fwd that
+ * follow (x, x_dtype, batch, n), which the layers of a group share. */
+typedef struct qs_linear_layer {
+  int64_t m;
+  const void *packed;
+  int stages;
+  const int *kinds;
+  const float *stage_scales;
+  const float *layer_scale;
+  int transform;
+  const float *su;
+  const float *sv;
+  const void *phase_u;
+  const void *phase_v;
+  const float *bias;
+  void *y;
+  void *workspace;
+  int64_t workspace_bytes;
+} qs_linear_layer;
+
+#define QS_GROUP_MAX_LAYERS 8
+/* The layers of a decoder that read one input ([q,k,v], [gate,up]; the
+ * reference groups them in architectures.py:52-94 get_linear_groups) in one
+ * call: y_i = qs_linear_fwd(x, layers[i]) for each of `count` layers
+ * (1..QS_GROUP_MAX_LAYERS).  At batches of at most 32 tokens layer 0 runs on
+ * `stream` and the others on side streams of this library that fork from
+ * `stream` and join back into it, so the group's latency-bound transform steps
+ * and its matmuls overlap on the GPU; larger batches, whose kernels each fill
+ * the GPU, run the layers one after another on `stream`.  Work queued on
+ * `stream` after the call sees every y_i.  The call may
+ * be captured in a CUDA graph (the side streams join the capture); make the
+ * first call on a device outside capture (it creates the side streams).
+ * Every layer is validated before anything is launched.  Workspaces and
+ * outputs must not overlap one another (the layers run concurrently).
+ * Calls from several host threads are serialised. */
+int qs_linear_fwd_group(const void *x, int x_dtype, int64_t batch, int64_t n, int count,
+                        const qs_linear_layer *layers, qs_stream_t stream);
+
 /* The three steps of qs_linear_fwd, for callers that put a collective between
  * the matmul and the output transform (column-sharded tensor parallelism:
  * each rank runs qs_linear_input + qs_linear_matmul on its rows of the

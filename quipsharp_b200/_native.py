@@ -55,6 +55,7 @@ _SIGS = {
     "qs_linear_workspace_bytes": (_L, [_L, _L, _L]),
     "qs_linear_fwd": (_I, [_P, _I, _L, _L, _L, _P, _I, _P, _P, _P, _I, _P, _P, _P, _P, _P, _P,
                            _P, _L, _P]),
+    "qs_linear_fwd_group": (_I, [_P, _I, _L, _L, _I, _P, _P]),
     "qs_linear_fwd_noalloc": (_I, [_P, _I, _L, _L, _L, _P, _I, _P, _P, _P, _I, _P, _P, _P, _P, _P, _P,
                                    _P]),
     "qs_linear_input_bytes": (_L, [_L, _L]),
@@ -85,6 +86,23 @@ class TPPeers(ctypes.Structure):
                 ("flags", ctypes.c_void_p * QS_TP_MAX_RANKS),
                 ("ctl", ctypes.c_void_p),
                 ("recv_floats", ctypes.c_int64)]
+
+
+QS_GROUP_MAX_LAYERS = 8
+
+
+class LinearLayer(ctypes.Structure):
+    """qs_linear_layer (include/quipsharp_b200.h): one layer of
+    qs_linear_fwd_group."""
+    _fields_ = [("m", ctypes.c_int64), ("packed", ctypes.c_void_p), ("stages", ctypes.c_int),
+                ("kinds", ctypes.c_void_p), ("stage_scales", ctypes.c_void_p),
+                ("layer_scale", ctypes.c_void_p), ("transform", ctypes.c_int),
+                ("su", ctypes.c_void_p), ("sv", ctypes.c_void_p),
+                ("phase_u", ctypes.c_void_p), ("phase_v", ctypes.c_void_p),
+                ("bias", ctypes.c_void_p), ("y", ctypes.c_void_p),
+                ("workspace", ctypes.c_void_p), ("workspace_bytes", ctypes.c_int64)]
+
+
 EXPORTS = tuple(_SIGS)
 
 _lib = None

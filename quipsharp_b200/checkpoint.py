@@ -65,6 +65,8 @@ class QuantizedLinear(nn.Module):
             self.register_buffer("phase_v", torch.zeros(in_features // 2, dtype=torch.complex64))
         self._kernel = None
         self._kernel_key = None
+        self._group = None  # a groups.LinearGroup this layer is a member of (fuse_linear_groups)
+        self._group_index = 0
 
     @classmethod
     def from_quantized_layer(cls, layer: QuantizedLayer, bias: Tensor = None) -> "QuantizedLinear":
@@ -117,6 +119,8 @@ class QuantizedLinear(nn.Module):
         return self._kernel
 
     def forward(self, x: Tensor) -> Tensor:
+        if self._group is not None:
+            return self._group.member_forward(self._group_index, x)
         return self.kernel()(x)
 
 

@@ -3,6 +3,7 @@
 #include <cstdarg>
 #include <cstdio>
 #include <cstring>
+#include <mutex>
 
 #include "qs_common.cuh"
 #include "qs_launch.h"
@@ -347,31 +348,142 @@ QS_API int qs_linear_fwd_tp(const void *x, int x_dtype, int64_t batch, int64_t n
                               su, sv, phase_u, phase_v, bias, y, workspace, peers, (cudaStream_t)stream);
 }
 
+// Checks of one layer of qs_linear_fwd / qs_linear_fwd_group (nothing launched).
+static int check_linear(const void *x, int x_dtype, int64_t batch, int64_t n, const qs_linear_layer &L) {
+  int st = check_kinds(L.stages, L.kinds);
+  if (st) return st;
+  if (!valid_io_dtype(x_dtype)) return fail(QS_ERR_INVALID_ARG, "bad dtype %d", x_dtype);
+  if (batch < 0 || n <= 0 || L.m <= 0 || n % 8) return fail(QS_ERR_INVALID_ARG, "bad shape");
+  st = check_transform_args(L.transform, L.m, n, L.su, L.sv, L.phase_u, L.phase_v);
+  if (st) return st;
+  if (batch == 0) return QS_OK;
+  if (!x || !L.y || !L.packed || !L.layer_scale || !L.workspace) return fail(QS_ERR_INVALID_ARG, "null pointer");
+  if (L.stages == 2 && !L.stage_scales) return fail(QS_ERR_INVALID_ARG, "RVQ needs stage scales");
+  if (L.workspace_bytes < qs_linear_workspace_bytes(batch, L.m, n)) return fail(QS_ERR_WORKSPACE, "workspace too small");
+  if (!aligned(L.workspace, 256) || !aligned(L.packed, 256))
+    return fail(QS_ERR_ALIGNMENT, "workspace/packed must be 256-byte aligned");
+  return QS_OK;
+}
+
+// Step `step` (0 input, 1 matmul, 2 output) of one checked layer on stream s.
+static int launch_linear_step(int step, const void *x, int x_dtype, int64_t batch, int64_t n,
+                              const qs_linear_layer &L, cudaStream_t s) {
+  const int64_t x2b = ws_align(linear_input_bytes(batch, n));
+  float *y1 = reinterpret_cast<float *>(static_cast<char *>(L.workspace) + x2b);
+  // the prefill matmul writes every y1 element; only the decode-regime kernel accumulates
+  const bool tc = batch >= kTcMinBatch;
+  if (step == 0)
+    return launch_linear_input(x, x_dtype, batch, n, L.transform, L.sv, L.phase_v, L.workspace, tc ? nullptr : y1,
+                               L.m, s);
+  if (step == 1)
+    return launch_matmul(L.workspace, batch, n, L.m, L.packed, L.stages, L.kinds, L.stage_scales, L.layer_scale,
+                         y1, s);
+  return launch_linear_output(y1, L.m, 1, batch, L.m, L.transform, L.su, L.phase_u, L.bias, L.y, x_dtype, s);
+}
+
 QS_API int qs_linear_fwd(const void *x, int x_dtype, int64_t batch, int64_t n, int64_t m,
                          const void *packed, int stages, const int *kinds,
                          const float *stage_scales, const float *layer_scale, int transform,
                          const float *su, const float *sv, const void *phase_u,
                          const void *phase_v, const float *bias, void *y, void *workspace,
                          int64_t workspace_bytes, qs_stream_t stream) {
-  int st = check_kinds(stages, kinds);
-  if (st) return st;
-  if (!valid_io_dtype(x_dtype)) return fail(QS_ERR_INVALID_ARG, "bad dtype %d", x_dtype);
-  if (batch < 0 || n <= 0 || m <= 0 || n % 8) return fail(QS_ERR_INVALID_ARG, "bad shape");
-  st = check_transform_args(transform, m, n, su, sv, phase_u, phase_v);
-  if (st) return st;
+  const qs_linear_layer L{m, packed, stages, kinds, stage_scales, layer_scale, transform, su, sv, phase_u, phase_v,
+                          bias, y, workspace, workspace_bytes};
+  int st = check_linear(x, x_dtype, batch, n, L);
+  if (st || batch == 0) return st;
+  for (int step = 0; step < 3; ++step)
+    if ((st = launch_linear_step(step, x, x_dtype, batch, n, L, (cudaStream_t)stream))) return st;
+  return QS_OK;
+}
+
+// Side streams and events of qs_linear_fwd_group, per device, made on first use
+// and kept until exit (guarded by g_group_mutex, which also serialises the
+// calls: the events are reused by every call).
+namespace {
+struct GroupStreams {
+  bool ready = false;
+  cudaStream_t side[QS_GROUP_MAX_LAYERS - 1];
+  cudaEvent_t fork;
+  cudaEvent_t join[QS_GROUP_MAX_LAYERS - 1];
+};
+constexpr int kGroupDevices = 64;
+std::mutex g_group_mutex;
+GroupStreams g_group[kGroupDevices];
+
+int group_streams(GroupStreams **out) {
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= kGroupDevices)
+    return fail(QS_ERR_CUDA, "no usable current device for the group's side streams");
+  GroupStreams &g = g_group[dev];
+  if (!g.ready) {
+    if (cudaEventCreateWithFlags(&g.fork, cudaEventDisableTiming) != cudaSuccess)
+      return fail(QS_ERR_CUDA, "cannot create the group's fork event");
+    for (int i = 0; i < QS_GROUP_MAX_LAYERS - 1; ++i)
+      if (cudaStreamCreateWithFlags(&g.side[i], cudaStreamNonBlocking) != cudaSuccess ||
+          cudaEventCreateWithFlags(&g.join[i], cudaEventDisableTiming) != cudaSuccess)
+        return fail(QS_ERR_CUDA, "cannot create the group's side streams");
+    g.ready = true;
+  }
+  *out = &g;
+  return QS_OK;
+}
+
+bool overlaps(const void *a, int64_t na, const void *b, int64_t nb) {
+  const uintptr_t pa = reinterpret_cast<uintptr_t>(a), pb = reinterpret_cast<uintptr_t>(b);
+  return pa < pb + static_cast<uintptr_t>(nb) && pb < pa + static_cast<uintptr_t>(na);
+}
+}  // namespace
+
+QS_API int qs_linear_fwd_group(const void *x, int x_dtype, int64_t batch, int64_t n, int count,
+                               const qs_linear_layer *layers, qs_stream_t stream) {
+  if (count < 1 || count > QS_GROUP_MAX_LAYERS || !layers)
+    return fail(QS_ERR_INVALID_ARG, "a group has 1 to %d layers (got %d) and a layers array", QS_GROUP_MAX_LAYERS,
+                count);
+  for (int i = 0; i < count; ++i) {
+    const int st = check_linear(x, x_dtype, batch, n, layers[i]);
+    if (st) return st;
+  }
   if (batch == 0) return QS_OK;
-  if (!x || !y || !packed || !layer_scale || !workspace) return fail(QS_ERR_INVALID_ARG, "null pointer");
-  if (stages == 2 && !stage_scales) return fail(QS_ERR_INVALID_ARG, "RVQ needs stage scales");
-  if (workspace_bytes < qs_linear_workspace_bytes(batch, m, n)) return fail(QS_ERR_WORKSPACE, "workspace too small");
-  if (!aligned(workspace, 256) || !aligned(packed, 256)) return fail(QS_ERR_ALIGNMENT, "workspace/packed must be 256-byte aligned");
-  const int64_t x2b = ws_align(linear_input_bytes(batch, n));
-  float *y1 = reinterpret_cast<float *>(static_cast<char *>(workspace) + x2b);
+  const int64_t esz = x_dtype == QS_F32 ? 4 : 2;
+  for (int i = 0; i < count; ++i)
+    for (int j = i + 1; j < count; ++j) {
+      const qs_linear_layer &a = layers[i], &b = layers[j];
+      const int64_t wa = qs_linear_workspace_bytes(batch, a.m, n), wb = qs_linear_workspace_bytes(batch, b.m, n);
+      const int64_t ya = batch * a.m * esz, yb = batch * b.m * esz;
+      if (overlaps(a.workspace, wa, b.workspace, wb) || overlaps(a.y, ya, b.y, yb) ||
+          overlaps(a.workspace, wa, b.y, yb) || overlaps(a.y, ya, b.workspace, wb))
+        return fail(QS_ERR_INVALID_ARG, "layers %d and %d of the group share workspace or output memory", i, j);
+    }
   cudaStream_t s = (cudaStream_t)stream;
-  // the prefill matmul writes every y1 element; only the decode-regime kernel accumulates
-  const bool tc = batch >= kTcMinBatch;
-  st = launch_linear_input(x, x_dtype, batch, n, transform, sv, phase_v, workspace, tc ? nullptr : y1, m, s);
+  // Prefill batches: every kernel of a layer fills the GPU (and the tensor-core
+  // GEMM holds all of an SM's tensor memory), so the layers follow one another.
+  if (count == 1 || batch >= kTcMinBatch) {
+    for (int i = 0; i < count; ++i)
+      for (int step = 0; step < 3; ++step) {
+        const int st = launch_linear_step(step, x, x_dtype, batch, n, layers[i], s);
+        if (st) return st;
+      }
+    return QS_OK;
+  }
+  std::lock_guard<std::mutex> lock(g_group_mutex);
+  GroupStreams *g = nullptr;
+  int st = group_streams(&g);
   if (st) return st;
-  st = launch_matmul(workspace, batch, n, m, packed, stages, kinds, stage_scales, layer_scale, y1, s);
-  if (st) return st;
-  return launch_linear_output(y1, m, 1, batch, m, transform, su, phase_u, bias, y, x_dtype, s);
+  if (cudaEventRecord(g->fork, s) != cudaSuccess) return fail(QS_ERR_CUDA, "group fork: event record failed");
+  int forked = 1;  // layers with a stream: 0 on s, i on side[i - 1]
+  for (; forked < count; ++forked)
+    if (cudaStreamWaitEvent(g->side[forked - 1], g->fork, 0) != cudaSuccess) {
+      st = fail(QS_ERR_CUDA, "group fork: stream wait failed");
+      break;
+    }
+  // step by step across the layers, so every layer's first kernel is queued early
+  for (int step = 0; step < 3 && !st; ++step)
+    for (int i = 0; i < forked && !st; ++i)
+      st = launch_linear_step(step, x, x_dtype, batch, n, layers[i], i ? g->side[i - 1] : s);
+  // join every forked stream whatever happened: a capture must end with all of them joined
+  for (int i = 1; i < forked; ++i)
+    if ((cudaEventRecord(g->join[i - 1], g->side[i - 1]) != cudaSuccess ||
+         cudaStreamWaitEvent(s, g->join[i - 1], 0) != cudaSuccess) && !st)
+      st = fail(QS_ERR_CUDA, "group join failed");
+  return st;
 }

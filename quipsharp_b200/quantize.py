@@ -133,6 +133,9 @@ class LinearKernel:
     def __call__(self, x: Tensor, out: Tensor | None = None, workspace: Tensor | None = None) -> Tensor:
         """x (..., n) of float32/float16/bfloat16 -> y (..., m) of the same dtype."""
         N.require_cuda(x)
+        if x.device.index != torch.cuda.current_device():  # launch on the device that holds the layer
+            with torch.cuda.device(x.device):
+                return self(x, out, workspace)
         lead = x.shape[:-1]
         io_dtype = x.dtype if x.dtype in N.IO_DTYPES else torch.float32
         x2 = x.reshape(-1, self.n).to(io_dtype).contiguous()

@@ -147,3 +147,58 @@ def test_tp_peers_struct_matches_the_header(tmp_path):
         bases = [0x10000 * (r + 1) * 4096 for r in range(world)]
         pe = make_peers(world, world - 1, bases, cap)
         assert pe.flags[0] == bases[0] + 2 * cap * 4 and pe.ctl == bases[-1] + ctl_offset(cap, world) * 4
+
+
+def _group_layer(m, ws, y, k, fake=0x100000):
+    """A qs_linear_layer with well-formed (never dereferenced) device pointers."""
+    L = N.LinearLayer()
+    L.m, L.packed, L.stages, L.kinds = m, fake, 1, ctypes.cast(k, ctypes.c_void_p)
+    L.layer_scale, L.transform, L.su, L.sv = fake, N.QS_RHT, fake, fake
+    L.y, L.workspace, L.workspace_bytes = y, ws, N.lib().qs_linear_workspace_bytes(1, m, 4096)
+    return L
+
+
+def test_linear_group_struct_and_checks(tmp_path):
+    """qs_linear_layer's ctypes mirror has the header's C layout; qs_linear_fwd_group
+    validates every layer (and that no two share memory) before launching."""
+    import shutil
+    import subprocess
+    cc = shutil.which("gcc") or shutil.which("cc")
+    if cc is None:
+        pytest.skip("no host C compiler")
+    fields = [f for f, _ in N.LinearLayer._fields_]
+    src = tmp_path / "layer.c"
+    src.write_text(
+        '#include <stdio.h>\n#include <stddef.h>\n#include "quipsharp_b200.h"\n'
+        "int main(void) {\n"
+        '  printf("%zu %d\\n", sizeof(qs_linear_layer), QS_GROUP_MAX_LAYERS);\n'
+        + "".join(f'  printf("%zu\\n", offsetof(qs_linear_layer, {f}));\n' for f in fields)
+        + "  return 0;\n}\n")
+    exe = tmp_path / "layer"
+    subprocess.run([cc, "-I", os.path.join(ROOT, "include"), str(src), "-o", str(exe)], check=True)
+    got = [int(v) for v in subprocess.run([str(exe)], check=True, capture_output=True, text=True).stdout.split()]
+    assert got == [ctypes.sizeof(N.LinearLayer), N.QS_GROUP_MAX_LAYERS] + \
+        [getattr(N.LinearLayer, f).offset for f in fields]
+
+    lib = N.lib()
+    k = N.int_array([N.QS_CB_E8P])
+    MB = 1 << 20
+    a = _group_layer(4096, 0x10000000, 0x20000000, k)
+    b = _group_layer(1024, 0x10000000 + 64 * MB, 0x20000000 + 64 * MB, k)
+    arr = (N.LinearLayer * 2)(a, b)
+    assert lib.qs_linear_fwd_group(0x30000000, N.QS_F16, 1, 4096, 0, arr, None) == N.QS_ERR_INVALID_ARG
+    assert lib.qs_linear_fwd_group(0x30000000, N.QS_F16, 1, 4096, 9, arr, None) == N.QS_ERR_INVALID_ARG
+    assert lib.qs_linear_fwd_group(0x30000000, N.QS_F16, 0, 4096, 2, arr, None) == N.QS_OK  # empty batch
+    bad = (N.LinearLayer * 2)(a, _group_layer(1000, 0x10000000 + 64 * MB, 0x20000000 + 64 * MB, k))
+    assert lib.qs_linear_fwd_group(0x30000000, N.QS_F16, 1, 4096, 2, bad, None) == N.QS_ERR_NOT_POW2
+    small = _group_layer(1024, 0x10000000 + 64 * MB, 0x20000000 + 64 * MB, k)
+    small.workspace_bytes = 16
+    arr2 = (N.LinearLayer * 2)(a, small)
+    assert lib.qs_linear_fwd_group(0x30000000, N.QS_F16, 1, 4096, 2, arr2, None) == N.QS_ERR_WORKSPACE
+    for shared in (dict(workspace=a.workspace + 256), dict(y=a.y), dict(y=a.workspace)):
+        c = _group_layer(1024, 0x10000000 + 64 * MB, 0x20000000 + 64 * MB, k)
+        for f, v in shared.items():
+            setattr(c, f, v)
+        arr3 = (N.LinearLayer * 2)(a, c)
+        assert lib.qs_linear_fwd_group(0x30000000, N.QS_F16, 1, 4096, 2, arr3, None) == N.QS_ERR_INVALID_ARG
+        assert b"share" in lib.qs_last_error()

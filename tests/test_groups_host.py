@@ -1,0 +1,96 @@
+"""Host logic of groups.py (no GPU): which layers of a decoder form groups, and
+when a member call reuses the group's outputs or computes the group again."""
+import pytest
+import torch
+from torch import nn
+
+from quipsharp_b200.checkpoint import QuantizedLinear
+from quipsharp_b200.groups import LinearGroup, fuse_linear_groups, linear_groups, unfuse_linear_groups
+
+
+class CountingGroup(LinearGroup):
+    """forward() replaced by a host computation that counts its calls."""
+
+    def __init__(self, modules):
+        super().__init__(modules)
+        self.calls = 0
+
+    def forward(self, x):
+        self.calls += 1
+        return [x.sum(-1, keepdim=True) * (i + 1) + self.calls for i in range(len(self.modules))]
+
+
+def _qlin(n, m, kind="rht"):
+    return QuantizedLinear(n, m, 8, kind)
+
+
+def _decoder_layer(n=64, kv=32, inter=96):
+    layer = nn.Module()
+    layer.self_attn = nn.Module()
+    layer.self_attn.q_proj, layer.self_attn.k_proj = _qlin(n, n), _qlin(n, kv)
+    layer.self_attn.v_proj, layer.self_attn.o_proj = _qlin(n, kv), _qlin(n, n)
+    layer.mlp = nn.Module()
+    layer.mlp.gate_proj, layer.mlp.up_proj = _qlin(n, inter, "rfft"), _qlin(n, inter, "rfft")
+    layer.mlp.down_proj = _qlin(inter, n, "rfft")
+    return layer
+
+
+def test_linear_groups_follow_the_reference_grouping():
+    layer = _decoder_layer()
+    groups = linear_groups(layer)
+    assert [[name for name, _ in g] for g in groups] == [
+        ["self_attn.q_proj", "self_attn.k_proj", "self_attn.v_proj"], ["mlp.gate_proj", "mlp.up_proj"]]
+    layer.self_attn.k_proj = nn.Linear(64, 32)  # not quantized: left out of the group
+    layer.self_attn.v_proj = None                # absent (KV-shared layers)
+    assert linear_groups(layer) == [linear_groups(layer)[0]]
+    assert [n for n, _ in linear_groups(layer)[0]] == ["mlp.gate_proj", "mlp.up_proj"]
+
+
+def test_fuse_links_every_decoder_layer_and_unfuse_undoes_it():
+    model = nn.Module()
+    model.layers = nn.ModuleList([_decoder_layer(), _decoder_layer()])
+    assert fuse_linear_groups(model) == 4
+    q, k = model.layers[1].self_attn.q_proj, model.layers[1].self_attn.k_proj
+    assert q._group is k._group and (q._group_index, k._group_index) == (0, 1)
+    assert model.layers[0].mlp.down_proj._group is None and model.layers[0].self_attn.o_proj._group is None
+    assert q._group is not model.layers[0].self_attn.q_proj._group
+    assert "_group" not in "".join(model.state_dict())  # no state: checkpoints unchanged
+    unfuse_linear_groups(model)
+    assert all(m._group is None for m in model.modules() if isinstance(m, QuantizedLinear))
+
+
+def test_group_rejects_mismatched_inputs():
+    with pytest.raises(ValueError):
+        LinearGroup([_qlin(64, 64), _qlin(128, 64)])
+    with pytest.raises(ValueError):
+        LinearGroup([])
+    with pytest.raises(ValueError):
+        LinearGroup([_qlin(64, 64) for _ in range(9)])
+
+
+def test_member_calls_share_one_group_call_per_input():
+    mods = [_qlin(64, 64), _qlin(64, 32), _qlin(64, 32)]
+    g = CountingGroup(mods)
+    x = torch.randn(2, 64)
+    outs = [g.member_forward(i, x) for i in (0, 1, 2)]
+    assert g.calls == 1
+    assert torch.equal(outs[1], x.sum(-1, keepdim=True) * 2 + 1)
+    assert g._pending is None and g._src is None  # all taken: nothing held
+    g.member_forward(1, x)  # the same input again: a new step
+    assert g.calls == 2
+    g.member_forward(1, x)  # member 1 asked twice before the others: computes again
+    assert g.calls == 3
+    g.member_forward(0, x)
+    assert g.calls == 3     # member 0's output from that call is still pending
+    x.add_(1.0)             # in-place change: pending outputs no longer apply
+    g.member_forward(2, x)
+    assert g.calls == 4
+    y = torch.randn(2, 64)  # another tensor with the same contents is another input
+    y.copy_(x)
+    g.member_forward(0, y)
+    assert g.calls == 5
+    with torch.inference_mode():  # no version counter: identity alone
+        z = torch.randn(2, 64)
+        g.member_forward(0, z)
+        g.member_forward(1, z)
+    assert g.calls == 6
