@@ -401,7 +401,8 @@ QS_API int qs_linear_fwd(const void *x, int x_dtype, int64_t batch, int64_t n, i
 // calls: the events are reused by every call).
 namespace {
 struct GroupStreams {
-  bool ready = false;
+  bool have_fork = false;
+  int made = 0;  // side streams (with their join events) created so far
   cudaStream_t side[QS_GROUP_MAX_LAYERS - 1];
   cudaEvent_t fork;
   cudaEvent_t join[QS_GROUP_MAX_LAYERS - 1];
@@ -415,14 +416,19 @@ int group_streams(GroupStreams **out) {
   if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= kGroupDevices)
     return fail(QS_ERR_CUDA, "no usable current device for the group's side streams");
   GroupStreams &g = g_group[dev];
-  if (!g.ready) {
+  if (!g.have_fork) {
     if (cudaEventCreateWithFlags(&g.fork, cudaEventDisableTiming) != cudaSuccess)
       return fail(QS_ERR_CUDA, "cannot create the group's fork event");
-    for (int i = 0; i < QS_GROUP_MAX_LAYERS - 1; ++i)
-      if (cudaStreamCreateWithFlags(&g.side[i], cudaStreamNonBlocking) != cudaSuccess ||
-          cudaEventCreateWithFlags(&g.join[i], cudaEventDisableTiming) != cudaSuccess)
-        return fail(QS_ERR_CUDA, "cannot create the group's side streams");
-    g.ready = true;
+    g.have_fork = true;
+  }
+  // a failed creation is retried by the next call from where it stopped
+  for (; g.made < QS_GROUP_MAX_LAYERS - 1; ++g.made) {
+    if (cudaStreamCreateWithFlags(&g.side[g.made], cudaStreamNonBlocking) != cudaSuccess)
+      return fail(QS_ERR_CUDA, "cannot create the group's side streams");
+    if (cudaEventCreateWithFlags(&g.join[g.made], cudaEventDisableTiming) != cudaSuccess) {
+      cudaStreamDestroy(g.side[g.made]);
+      return fail(QS_ERR_CUDA, "cannot create the group's join events");
+    }
   }
   *out = &g;
   return QS_OK;
