@@ -65,6 +65,7 @@ class QuantizedLinear(nn.Module):
             self.register_buffer("phase_v", torch.zeros(in_features // 2, dtype=torch.complex64))
         self._kernel = None
         self._kernel_key = None
+        self._kernel_codebook = None  # held: a new codebook at a freed one's address is still new
         self._group = None  # a groups.LinearGroup this layer is a member of (fuse_linear_groups)
         self._group_index = 0
 
@@ -108,7 +109,7 @@ class QuantizedLinear(nn.Module):
         if self.codebook is None:
             raise RuntimeError("QuantizedLinear.codebook must be assigned before forward")
         key = self._buffers_key()
-        if self._kernel is None or key != self._kernel_key:
+        if self._kernel is None or key != self._kernel_key or self.codebook is not self._kernel_codebook:
             targs = (dict(su=self.su, sv=self.sv) if self.transform_kind == "rht"
                      else dict(phase_u=self.phase_u, phase_v=self.phase_v))
             with torch.no_grad():
@@ -116,6 +117,7 @@ class QuantizedLinear(nn.Module):
                                             self.in_features, self.scale, self.transform_kind,
                                             bias=self.bias, **targs)
             self._kernel_key = key
+            self.__dict__["_kernel_codebook"] = self.codebook  # a plain reference, never a submodule
         return self._kernel
 
     def forward(self, x: Tensor) -> Tensor:

@@ -52,12 +52,15 @@ class LinearGroup:
             raise ValueError("the layers of a group read one input: in_features must agree")
         self.modules = modules
         self.in_features = modules[0].in_features
-        self._layers, self._layers_key = None, None
+        self._layers, self._layers_kernels = None, None
         self._pending, self._src, self._src_key = None, None, None
 
     def _descriptors(self, kernels):
-        key = tuple(id(k) for k in kernels)
-        if self._layers_key != key:
+        """The members' qs_linear_layer array, rebuilt when a member rebuilt its
+        kernel (the cached kernels are held, so a new one is never mistaken for
+        a freed one at the same address)."""
+        old = self._layers_kernels
+        if old is None or any(a is not b for a, b in zip(old, kernels)):
             arr = (N.LinearLayer * len(kernels))()
             for d, k in zip(arr, kernels):
                 d.m, d.packed, d.stages = k.m, N.ptr(k.packed), len(k.kinds)
@@ -66,7 +69,7 @@ class LinearGroup:
                 d.layer_scale, d.transform = N.ptr(k.scale), k.transform
                 d.su, d.sv, d.phase_u, d.phase_v = N.ptr(k.su), N.ptr(k.sv), N.ptr(k.phase_u), N.ptr(k.phase_v)
                 d.bias = N.ptr(k.bias)
-            self._layers, self._layers_key = arr, key
+            self._layers, self._layers_kernels = arr, list(kernels)
         return self._layers
 
     def forward(self, x: Tensor) -> list[Tensor]:

@@ -137,3 +137,29 @@ def test_place_decoder_layers_moves_inputs_between_devices():
     place_decoder_layers(model, model.state_dict(), ["cpu", "cpu"], [10**6, 10**6])
     assert torch.allclose(model(ids), ref)
     assert len(seen) == 4 and all(d.type == "cpu" for d in seen)
+
+
+def test_kernel_cache_follows_codebook_and_buffers(monkeypatch):
+    """QuantizedLinear.kernel() rebuilds its fused-forward state when the codebook
+    object or a buffer changes, and reuses it otherwise (LinearKernel replaced by
+    a host fake: building the real one packs codes on the GPU)."""
+    built = []
+
+    class FakeKernel:
+        def __init__(self, codes, codebook, *a, **k):
+            built.append(codebook)
+
+    monkeypatch.setattr(C, "LinearKernel", FakeKernel)
+    q = C.QuantizedLinear(64, 32, 8, "rht")
+    q.codebook = E8PCodebook()
+    k = q.kernel()
+    assert q.kernel() is k and len(built) == 1
+    q.codebook = E8PCodebook()            # another codebook object
+    assert q.kernel() is not k and len(built) == 2
+    q.codes.add_(1)                       # in-place change of a buffer
+    q.kernel()
+    assert len(built) == 3
+    q.kernel()
+    assert len(built) == 3
+    assert "_kernel_codebook" not in dict(q.named_modules()) and set(q.state_dict()) == {
+        "codes", "scale", "su", "sv"}

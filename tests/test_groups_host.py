@@ -94,3 +94,27 @@ def test_member_calls_share_one_group_call_per_input():
         g.member_forward(0, z)
         g.member_forward(1, z)
     assert g.calls == 6
+
+
+def test_descriptors_follow_rebuilt_kernels():
+    """A member whose kernel was rebuilt (new packed weights) gets a new
+    descriptor array; unchanged kernels reuse the cached one."""
+    import ctypes
+    from types import SimpleNamespace
+    from quipsharp_b200 import _native as N
+
+    def fake_kernel(base):
+        t = lambda off: SimpleNamespace(data_ptr=lambda: base + off)
+        return SimpleNamespace(m=64, packed=t(0), kinds=[N.QS_CB_E8P], _kinds_c=N.int_array([N.QS_CB_E8P]),
+                               _ss_c=None, scale=t(256), transform=N.QS_RHT, su=t(512), sv=t(768),
+                               phase_u=None, phase_v=None, bias=None)
+
+    g = LinearGroup([_qlin(64, 64), _qlin(64, 64)])
+    k1, k2 = fake_kernel(0x100000), fake_kernel(0x200000)
+    a = g._descriptors([k1, k2])
+    assert g._descriptors([k1, k2]) is a
+    assert a[1].packed == 0x200000 and a[0].sv == 0x100000 + 768
+    assert a[0].kinds == ctypes.addressof(k1._kinds_c) and a[0].stage_scales is None
+    k2b = fake_kernel(0x300000)
+    b = g._descriptors([k1, k2b])
+    assert b is not a and b[1].packed == 0x300000
