@@ -5,11 +5,12 @@ forward runs, on every rank, the input transform of the full activations, the
 fused decode + matmul of the local rows into a private float32 y1 shard, a push
 of the shard into every rank's receive buffer over NVLink (decode batches: by
 every CTA of the matmul after a grid barrier, as 8-byte words that carry the
-call's sequence number, so
-no fence or flag is needed; prefill batches: a push kernel, then a flag in every
-rank's memory), and the output transform, which reads the gathered y1 locally
-once it has arrived (no collective library call on the data path).  Every rank ends with the full output, ready for the next
-layer.
+call's sequence number, so no fence or flag is needed; prefill batches: a push
+kernel, then a flag in every rank's memory), and the output transform, which
+reads the gathered y1 locally once it has arrived (no collective library call on
+the data path).  Every rank ends with the full output, ready for the next layer.
+Layers are not grouped across streams here (groups.py): the decode matmul's grid
+barrier needs every CTA of its grid resident.
 
 The receive buffers and flags live in a `TPContext` per (process group,
 device): allocated once, shared with the peers through CUDA IPC handles
