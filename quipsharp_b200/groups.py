@@ -87,7 +87,8 @@ class LinearGroup:
         sizes = [_round_up(max(k.workspace_bytes(B), 1), 256) for k in kernels]
         ws = torch.empty(sum(sizes), dtype=torch.uint8, device=x.device)
         ys = [torch.empty(B, k.m, device=x.device, dtype=io_dtype) for k in kernels]
-        arr = self._descriptors(kernels)
+        tpl = self._descriptors(kernels)
+        arr = type(tpl)(*tpl)  # a copy per call: concurrent calls never share output pointers
         off = ws.data_ptr()
         for d, y, size in zip(arr, ys, sizes):
             d.y, d.workspace, d.workspace_bytes = y.data_ptr(), off, size
