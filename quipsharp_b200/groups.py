@@ -85,11 +85,11 @@ class LinearGroup:
         x2 = x.reshape(-1, n).to(io_dtype).contiguous()
         B = x2.shape[0]
         sizes = [_round_up(max(k.workspace_bytes(B), 1), 256) for k in kernels]
-        ws = torch.empty(sum(sizes), dtype=torch.uint8, device=x.device)
+        ws = torch.empty(sum(sizes) + 255, dtype=torch.uint8, device=x.device)
         ys = [torch.empty(B, k.m, device=x.device, dtype=io_dtype) for k in kernels]
         tpl = self._descriptors(kernels)
         arr = type(tpl)(*tpl)  # a copy per call: concurrent calls never share output pointers
-        off = ws.data_ptr()
+        off = _round_up(ws.data_ptr(), 256)  # every piece 256-byte aligned, as the library requires
         for d, y, size in zip(arr, ys, sizes):
             d.y, d.workspace, d.workspace_bytes = y.data_ptr(), off, size
             off += size

@@ -118,3 +118,56 @@ def test_descriptors_follow_rebuilt_kernels():
     k2b = fake_kernel(0x300000)
     b = g._descriptors([k1, k2b])
     assert b is not a and b[1].packed == 0x300000
+
+
+def test_group_forward_host_side(monkeypatch):
+    """LinearGroup.forward's host logic with the library call replaced by a
+    recorder: one workspace carved into 256-byte aligned, disjoint per-layer
+    pieces of the sizes the library asks for, one output per member, and a fresh
+    descriptor array per call (the cached template is never written)."""
+    import ctypes
+    from types import SimpleNamespace
+    from quipsharp_b200 import _native as N
+    from quipsharp_b200 import checkpoint as C
+
+    class FakeKernel:
+        def __init__(self, codes, codebook, m, n, *a, **k):
+            self.m, self.n = m, n
+            self.packed = self.scale = self.su = self.sv = torch.zeros(4)
+            self.phase_u = self.phase_v = self.bias = None
+            self.kinds, self._kinds_c, self._ss_c, self.transform = [0], N.int_array([0]), None, N.QS_RHT
+
+        def workspace_bytes(self, B):
+            return 1000 * self.m + B
+
+    calls = []
+
+    class FakeLib:
+        def qs_linear_fwd_group(self, x, dtype, B, n, count, arr, stream):
+            calls.append((x, dtype, B, n, count, [(d.m, d.y, d.workspace, d.workspace_bytes) for d in arr[:count]],
+                          ctypes.addressof(arr)))
+            return N.QS_OK
+
+    monkeypatch.setattr(C, "LinearKernel", FakeKernel)
+    monkeypatch.setattr(N, "lib", lambda: FakeLib())
+    monkeypatch.setattr(N, "require_cuda", lambda *t: None)
+    monkeypatch.setattr(N, "stream_of", lambda t: 0)
+    monkeypatch.setattr(torch.cuda, "current_device", lambda: None)  # a CPU tensor's device index
+    mods = [_qlin(64, 64), _qlin(64, 32), _qlin(64, 32)]
+    for m in mods:
+        m.codebook = object()
+    g = LinearGroup(mods)
+    x = torch.randn(2, 3, 64, dtype=torch.bfloat16)
+    ys = g(x)
+    assert [tuple(y.shape) for y in ys] == [(2, 3, 64), (2, 3, 32), (2, 3, 32)]
+    assert all(y.dtype == torch.bfloat16 for y in ys)
+    _, dtype, B, n, count, layers, addr1 = calls[0]
+    assert (dtype, B, n, count) == (N.QS_BF16, 6, 64, 3)
+    for (m, y, ws, wb), want_m in zip(layers, (64, 32, 32)):
+        assert m == want_m and ws % 256 == 0 and wb >= 1000 * m + 6
+    spans = sorted((ws, ws + wb) for _, _, ws, wb in layers)
+    assert all(a[1] <= b[0] for a, b in zip(spans, spans[1:]))
+    assert len({y for _, y, _, _ in layers}) == 3
+    g(x)
+    assert calls[1][6] != ctypes.addressof(g._layers)  # a copy, not the template
+    assert all(d.y is None and d.workspace is None for d in g._layers)
